@@ -1,0 +1,451 @@
+"""Benchmark of the B200 StrideWeave carrier hot path.
+
+Default workload: layout-aware Float32 reductions - sum,
+max and argmax over mode 1 of X[8192 x 4096] ~ U(-1, 1), on (a) a row-major
+layout, (b) a transposed stride layout and (c) a hierarchical tiled layout
+((128,64),(32,128)) stored through a 3-bit swizzle.  One step = the 9
+reductions.  The line also carries the MX contractions of configs 1 and 3
+(MXFP8 / MXFP4, M=N=K=8192) measured on the same device.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Inputs are larger than L2 (each layout's X is 128 MiB, and consecutive
+launches read different buffers), timing is by CUDA events on the launching
+stream, and the multi-GPU value is the max over ranks (weak scaling: each
+rank reduces its own X, there is no collective on the data path).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+R, C = 8192, 4096
+X_BYTES = R * C * 4
+RED_BYTES = X_BYTES + R * 4  # algorithmic bytes of one reduction launch
+LAYOUTS = ("rowmajor", "transposed", "tiled_swizzled")
+OPS = ("reduce_sum", "reduce_max", "argmax")
+SWZ = [(3, 2, 3)]
+
+
+def plan_of(layout: str):
+    if layout == "rowmajor":
+        return [(R, C)], [(C, 1)], []
+    if layout == "transposed":
+        return [(R, 1)], [(C, R)], []
+    return [(128, 32), (64, 128 * 32 * 128)], [(32, 1), (128, 128 * 32)], SWZ
+
+
+def storage_of(layout: str, x: np.ndarray) -> np.ndarray:
+    """Physical storage holding logical X under `layout`."""
+    if layout == "rowmajor":
+        return np.ascontiguousarray(x).ravel()
+    if layout == "transposed":
+        return np.ascontiguousarray(x.T).ravel()
+    # tile (tr, tc) of 128 x 32 at (tr * 128 + tc) * 4096, row-major inside
+    t = x.reshape(64, 128, 128, 32).transpose(0, 2, 1, 3)  # [tr, tc, r, c]
+    flat = np.ascontiguousarray(t).ravel()
+    # carrier flat index f lives at swizzle(f): bits 2..4 ^= bits 5..7
+    f = np.arange(flat.size, dtype=np.int64)
+    phys = f ^ (((f >> 5) & 7) << 2)
+    out = np.empty_like(flat)
+    out[phys] = flat
+    return out
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------
+# reference arm: the reference CPU carrier on the host cores
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.append(str(ROOT / "baseline" / "_ref"))
+    try:
+        import strideweave as sw
+        from strideweave import CPU, Layout, Shape, Stride, Tensor
+    except Exception as exc:  # pragma: no cover - reported, not raised
+        print(json.dumps({"impl": "reference", "unavailable": f"reference not importable: {exc}"}))
+        return
+    from concurrent.futures import ThreadPoolExecutor
+
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, size=(R, C)).astype(np.float32)
+    # The reference cannot place a tensor through a Swizzle: layout (c) runs on
+    # the tiled layout over un-swizzled storage (the logical data it reduces is
+    # the same).
+    stores = {
+        "rowmajor": np.ascontiguousarray(x).ravel(),
+        "transposed": np.ascontiguousarray(x.T).ravel(),
+        "tiled_swizzled": np.ascontiguousarray(x.reshape(64, 128, 128, 32).transpose(0, 2, 1, 3)).ravel(),
+    }
+    layouts = {
+        "rowmajor": Layout(Shape([R, C]), Stride([C, 1])),
+        "transposed": Layout(Shape([R, C]), Stride([1, R])),
+        "tiled_swizzled": Layout(Shape([[128, 64], [32, 128]]), Stride([[32, 128 * 32 * 128], [1, 128 * 32]])),
+    }
+    threads = os.cpu_count() or 1
+    fns = {"reduce_sum": sw.reduce_sum, "reduce_max": sw.reduce_max, "argmax": sw.argmax}
+    carriers = {k: CPU(v.size, pointer=v.ctypes.data) for k, v in stores.items()}
+
+    def slice_job(layout, op, lo, hi):
+        # rows lo..hi of the kept mode as a zero-copy view (the reference
+        # kernels are single-threaded; slices run on separate host threads)
+        base = Tensor(carriers[layout], 0, layouts[layout])
+        view = base[lo:hi, :] if layout != "tiled_swizzled" else None
+        if view is None:
+            # tiled layout: slice whole 128-row tiles through the outer leaf
+            tlo, thi = lo // 128, hi // 128
+            view = Tensor(carriers[layout], tlo * 128 * 32 * 128,
+                          Layout(Shape([[128, thi - tlo], [32, 128]]), Stride([[32, 128 * 32 * 128], [1, 128 * 32]])))
+        with sw.no_grad():
+            return fns[op](view, "a b -> a")
+
+    bounds = [(i * R // threads // 128 * 128, (i + 1) * R // threads // 128 * 128) for i in range(threads)]
+    bounds[-1] = (bounds[-1][0], R)
+
+    def step(pool):
+        futures = [pool.submit(slice_job, lay, op, lo, hi) for op in OPS for lay in LAYOUTS for lo, hi in bounds
+                   if hi > lo]
+        for f in futures:
+            f.result()
+
+    with ThreadPoolExecutor(threads) as pool:
+        for _ in range(args.warmup):
+            step(pool)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step(pool)
+        dt = (time.perf_counter() - t0) / args.steps
+    value = 9 * RED_BYTES / dt / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": "reduction HBM GB/s", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2_reductions_8192x4096", "ops": list(OPS), "layouts": list(LAYOUTS)},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "sample": "full X[8192x4096] per step, kept rows split over host threads"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---------------------------------------------------------------------------------
+# our arm
+
+
+def cpu_baseline_sample() -> dict:
+    """The reference CPU carrier on a bounded sample (rank 0, N=1 only)."""
+    sys.path.append(str(ROOT / "baseline" / "_ref"))
+    try:
+        import strideweave as sw
+        from strideweave import CPU, Layout, Shape, Stride, Tensor
+        kind = "reference"
+    except Exception:
+        sw = None
+        kind = "port"
+    rng = np.random.default_rng(1)
+    rows = 2048  # a quarter of X: ~1/4 of the config's work per op
+    x = rng.uniform(-1, 1, size=(rows, C)).astype(np.float32)
+    t0 = time.perf_counter()
+    if kind == "reference":
+        store_a = np.ascontiguousarray(x).ravel()
+        store_b = np.ascontiguousarray(x.T).ravel()
+        ta = Tensor(CPU(store_a.size, pointer=store_a.ctypes.data), 0, Layout(Shape([rows, C]), Stride([C, 1])))
+        tb = Tensor(CPU(store_b.size, pointer=store_b.ctypes.data), 0, Layout(Shape([rows, C]), Stride([1, rows])))
+        with sw.no_grad():
+            for fn in (sw.reduce_sum, sw.reduce_max, sw.argmax):
+                fn(ta, "a b -> a")
+                fn(tb, "a b -> a")
+        n_ops = 6
+    else:
+        from oracle import oracle as O
+        flat = np.ascontiguousarray(x).ravel()
+        for k in ("sum", "max", "argmax"):
+            O.reduce(k, flat, 0, [(rows, C)], [(C, 1)])
+        n_ops = 3
+    dt = time.perf_counter() - t0
+    gbs = n_ops * (rows * C * 4 + rows * 4) / dt / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{n_ops} reductions over X[{rows}x{C}] (row-major and transposed), single-threaded kernels"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    from strideweave_b200 import _native as N
+    from strideweave_b200 import kernels
+
+    N.set_device(local)
+    stream = torch.cuda.current_stream()
+    s = stream.cuda_stream
+
+    rng = np.random.default_rng(1234 + rank)
+    x = rng.uniform(-1, 1, size=(R, C)).astype(np.float32)
+    host = {lay: storage_of(lay, x) for lay in LAYOUTS}
+    dev = {lay: N.DeviceBuffer(X_BYTES) for lay in LAYOUTS}
+    for lay in LAYOUTS:
+        dev[lay].upload(host[lay])
+    outs = {(op, lay): N.DeviceBuffer(R * 4) for op in OPS for lay in LAYOUTS}
+    N.synchronize()
+
+    # consecutive launches read different 128 MiB buffers (> L2)
+    order = [(op, lay) for op in OPS for lay in LAYOUTS]
+
+    def launch(op, lay):
+        kept, red, swz = plan_of(lay)
+        kernels.reduce_f32(op, dev[lay].ptr, R * C, 0, kept, red, outs[(op, lay)].ptr, swizzle=swz, stream=s)
+
+    for _ in range(args.warmup):
+        for op, lay in order:
+            launch(op, lay)
+    torch.cuda.synchronize()
+
+    # -------- timed region: device-resident inputs --------
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in order]
+           for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for it in range(args.steps):
+            for i, (op, lay) in enumerate(order):
+                evs[it][i][0].record(stream)
+                launch(op, lay)
+                evs[it][i][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = start.elapsed_time(end)
+    per_kernel = {}
+    for i, key in enumerate(order):
+        per_kernel[key] = statistics.mean(evs[it][i][0].elapsed_time(evs[it][i][1]) for it in range(args.steps))
+    t = torch.tensor([total_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_per_step = max_ms / args.steps
+    value = world * 9 * RED_BYTES / (ms_per_step / 1e3) / 1e9
+
+    # correctness spot check of what was timed (device vs the sequential rule)
+    check = np.empty(R, dtype=np.float32)
+    outs[("reduce_max", "rowmajor")].download(check)
+    assert np.array_equal(check, x.max(axis=1)), "timed reduce_max disagrees with numpy"
+
+    # -------- end-to-end: pinned host input -> device -> reduce -> host --------
+    pinned = {lay: torch.from_numpy(host[lay]).pin_memory() for lay in LAYOUTS}
+    res_host = torch.empty(R * 9, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, args.steps // 4)
+
+    def e2e_step():
+        for lay in LAYOUTS:
+            N.check(N.lib.sw_memcpy_h2d(N.c_void_p(dev[lay].ptr), N.c_void_p(pinned[lay].data_ptr()), X_BYTES,
+                                        N.c_void_p(s)))
+        for j, (op, lay) in enumerate(order):
+            launch(op, lay)
+        for j, (op, lay) in enumerate(order):
+            N.check(N.lib.sw_memcpy_d2h(N.c_void_p(res_host.data_ptr() + 4 * R * j), N.c_void_p(outs[(op, lay)].ptr),
+                                        R * 4, N.c_void_p(s)))
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / e2e_steps
+    e2e_value = world * 9 * RED_BYTES / (e2e_ms / 1e3) / 1e9
+
+    # -------- contractions (configs 1 and 3) on this device --------
+    contraction = None
+    if not args.no_gemm:
+        contraction = bench_gemm(torch, N, kernels, s, stream)
+
+    if rank == 0:
+        peaks = load_peaks()
+        by_layout = {lay: sum(per_kernel[(op, lay)] for op in OPS) for lay in LAYOUTS}
+        dominant = max(by_layout, key=by_layout.get)
+        dom_ms = by_layout[dominant] / 3
+        achieved = RED_BYTES / (dom_ms / 1e3) / 1e9
+        line = {
+            "metric": "reduction HBM GB/s",
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic U(-1,1), seeded",
+            "config": {"workload": "config2_reductions_8192x4096", "ops": list(OPS), "layouts": list(LAYOUTS),
+                       "step": "9 reductions (3 ops x 3 layouts)", "l2": "inputs larger than L2, rotated",
+                       "parallelism": f"replicas x{world} (each rank its own X)"},
+            "roofline": {"bound": "hbm", "kernel": f"sw_reduce_f32[{dominant}]", "achieved": round(achieved, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_source": peaks["source"], "traffic": None,
+                         "per_layout_gbs": {lay: round(3 * RED_BYTES / (by_layout[lay] / 1e3) / 1e9, 1)
+                                            for lay in LAYOUTS}},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 3 * X_BYTES,
+                    "d2h_bytes_per_step": 9 * R * 4},
+            "gpu_launches": 9 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if contraction:
+            line["contraction"] = contraction
+        if world == 1:
+            line["cpu_baseline"] = cpu_baseline_sample()
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_gemm(torch, N, kernels, s, stream) -> dict:
+    """MXFP8 and MXFP4 contraction at M=N=K=8192 (device-resident operands)."""
+    out = {}
+    M = Nn = K = 8192
+    rng = np.random.default_rng(0)
+    a = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+    b = torch.from_numpy((rng.standard_normal((Nn, K)) * 0.02).astype(np.float32)).cuda()
+    for name, fmt in (("mxfp8", N.SW_MX_E4M3), ("mxfp4", N.SW_MX_E2M1)):
+        row_bytes = K if fmt == N.SW_MX_E4M3 else K // 2
+        pa, pb = N.DeviceBuffer(M * row_bytes), N.DeviceBuffer(Nn * row_bytes)
+        sa = N.DeviceBuffer(kernels.scale_bytes_tc128(M, K // 32))
+        sb = N.DeviceBuffer(kernels.scale_bytes_tc128(Nn, K // 32))
+        kernels.mx_quantize(fmt, a.data_ptr(), M, K, K, 1, pa.ptr, row_bytes, sa.ptr, stream=s)
+        kernels.mx_quantize(fmt, b.data_ptr(), Nn, K, K, 1, pb.ptr, row_bytes, sb.ptr, stream=s)
+        c = N.DeviceBuffer(M * Nn * 2)
+        for _ in range(3):
+            kernels.mx_gemm(fmt, pa.ptr, row_bytes, sa.ptr, pb.ptr, row_bytes, sb.ptr, c.ptr, M, Nn, K,
+                            out_bf16=True, stream=s)
+        torch.cuda.synchronize()
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            kernels.mx_gemm(fmt, pa.ptr, row_bytes, sa.ptr, pb.ptr, row_bytes, sb.ptr, c.ptr, M, Nn, K,
+                            out_bf16=True, stream=s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        tflops = 2.0 * M * Nn * K / (ms / 1e3) / 1e12
+        spec = 4500.0 if fmt == N.SW_MX_E4M3 else 9000.0
+        peaks = load_peaks()
+        clock_adj = peaks["bf16_tflops"] * (2 if fmt == N.SW_MX_E4M3 else 4)
+        out[name] = {"tflops": round(tflops, 1), "ms": round(ms, 4), "frac_of_spec_dense": round(tflops / spec, 4),
+                     "frac_of_clock_adjusted": round(tflops / clock_adj, 4),
+                     "config": "M=N=K=8192, A~N(0,1), B~N(0,0.02), bf16 C"}
+        del pa, pb, sa, sb, c
+    N.raise_device_status()
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,198 @@
+/*
+ * strideweave_b200.h - C ABI of the B200 CUDA carrier for StrideWeave.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, returns an
+ * `int` status (SW_OK on success) and never aborts.  On failure the calling
+ * thread's message is available from sw_last_error().  Device pointers are
+ * addresses returned by sw_alloc (or any cudaMalloc'd address); `stream` is a
+ * cudaStream_t passed as `void*` (NULL = the legacy default stream).  Kernel
+ * entry points only enqueue work: they return before the device has finished.
+ *
+ * The reference (patrickk1998/strideweave) binds its CPU kernels through
+ * pybind11; these functions are what its Python carrier layer reaches through
+ * ctypes instead.  Each declaration names the reference interface it replaces.
+ */
+#ifndef STRIDEWEAVE_B200_H
+#define STRIDEWEAVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Everything declared here is exported from the shared library even when it
+ * is built with hidden default visibility. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define SW_OK 0
+#define SW_ERR_INVALID 1     /* bad argument: shape, stride, dtype, alignment  */
+#define SW_ERR_UNSUPPORTED 2 /* a valid request no kernel implements           */
+#define SW_ERR_CUDA 3        /* a CUDA runtime/driver call failed              */
+#define SW_ERR_TIMEOUT 4     /* a bounded device-side wait gave up             */
+#define SW_ERR_NOMEM 5       /* device allocation failed                       */
+
+/* ---- limits ------------------------------------------------------------- */
+#define SW_MAX_LEAVES 8   /* leaves per top-level mode in a strided plan */
+#define SW_MAX_SWIZZLE 4  /* XOR stages of a carrier-level swizzle       */
+
+/* ---- runtime ------------------------------------------------------------ */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* sw_last_error(void);
+
+/* ABI version, bumped on any incompatible change of this header. */
+int sw_abi_version(void);
+
+int sw_device_count(int* count);
+int sw_set_device(int device);
+int sw_get_device(int* device);
+
+/* Device storage of a carrier's flat index space.
+ * Replaces the owned storage of CPU(size, ...) in
+ * src/strideweave/carriers/cpu/native/_cpu_carrier.hpp:38-67. */
+int sw_alloc(void** ptr, int64_t bytes);
+int sw_free(void* ptr);
+
+/* Copies.  Host pointers may be pageable or pinned; pinned ones overlap. */
+int sw_memcpy_h2d(void* dst, const void* src, int64_t bytes, void* stream);
+int sw_memcpy_d2h(void* dst, const void* src, int64_t bytes, void* stream);
+int sw_memcpy_d2d(void* dst, const void* src, int64_t bytes, void* stream);
+int sw_memset(void* dst, int value, int64_t bytes, void* stream);
+
+/* Page-locked host buffers for overlapped host<->device copies. */
+int sw_host_alloc(void** ptr, int64_t bytes);
+int sw_host_free(void* ptr);
+
+int sw_stream_create(void** stream);
+int sw_stream_destroy(void* stream);
+int sw_stream_synchronize(void* stream);
+
+/* Reads and clears the device-side error word that bounded waits and device
+ * bound checks write (SW_OK if none fired).  Synchronises the device. */
+int sw_device_status(int* status);
+
+/* ---- layout-aware reductions -------------------------------------------- */
+
+#define SW_REDUCE_SUM 0
+#define SW_REDUCE_MAX 1
+#define SW_REDUCE_ARGMAX 2
+
+/* A two-mode (kept, reduced) Float32 view lowered to flat leaf arrays.
+ * Leaves are listed first-leaf-fastest (StrideWeave's colexicographic order,
+ * the order of LayoutCache::leaf_shapes, core/native/_layout_index.hpp:116-120).
+ * Element (i, j) lives at carrier flat index
+ *     f = offset + sum_l kept_stride[l]*i_l + sum_l reduced_stride[l]*j_l
+ * and, when the carrier stores its flat space through a swizzle, at physical
+ * index swizzle(f), each stage applied in order as in
+ * src/strideweave/core/swizzle.py:107-117. */
+typedef struct sw_reduce_plan {
+    int32_t kind;          /* SW_REDUCE_* */
+    int32_t kept_rank;     /* 0..SW_MAX_LEAVES (0 = a single kept element) */
+    int32_t reduced_rank;  /* 1..SW_MAX_LEAVES */
+    int32_t swizzle_rank;  /* 0..SW_MAX_SWIZZLE */
+    int64_t offset;
+    int64_t kept_shape[SW_MAX_LEAVES];
+    int64_t kept_stride[SW_MAX_LEAVES];
+    int64_t reduced_shape[SW_MAX_LEAVES];
+    int64_t reduced_stride[SW_MAX_LEAVES];
+    int32_t swizzle_bits[SW_MAX_SWIZZLE];
+    int32_t swizzle_base[SW_MAX_SWIZZLE];
+    int32_t swizzle_shift[SW_MAX_SWIZZLE];
+} sw_reduce_plan;
+
+/* out[i] for every kept ordinal i (canonical 1-mode result, stride 1):
+ * SUM -> float, MAX -> float (bit-exact with cpu.reduce_max), ARGMAX -> int32
+ * (bit-exact with cpu.argmax).  `x_size` is the carrier size in elements and
+ * bounds every address.
+ * Replaces CpuReduceSumOperation::_forward
+ * (src/strideweave/carriers/cpu/native/ops/reduce_sum.cpp:30-118) and
+ * CpuFloatReductionOperation<Kind>::_forward for reduce_max / argmax
+ * (src/strideweave/carriers/cpu/native/_cpu_reduction.hpp:47-120). */
+int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
+                  void* out, void* stream);
+
+/* ---- MX (OCP Microscaling v1.0) quantise / dequantise ------------------- */
+
+#define SW_MX_E4M3 1 /* MXFP8_E4M3: 1 byte per element              */
+#define SW_MX_E2M1 2 /* MXFP4: 2 elements per byte, even k in the low nibble */
+
+/* Scale-plane placements (E8M0 bytes, one per 32-element block along K). */
+#define SW_SCALES_ROWMAJOR 0 /* scales[r * ld_scales + kb]                 */
+#define SW_SCALES_TC128 1    /* 128-row x 4-block atoms, see sw_mx_scale_index */
+
+/* Byte offset of scale (row r, block kb) in the SW_SCALES_TC128 placement of a
+ * plane with `kblocks` 32-blocks per row: atoms of 128 rows x 4 blocks (512 B)
+ * ordered K-block-fastest within a 128-row group, inside an atom
+ * (r % 32) * 16 + ((r / 32) % 4) * 4 + kb % 4.  This is the StrideWeave layout
+ * ((32,4,R/128),(4,KB/4)) : ((16,4,512*ceil(KB/4)),(1,512)), and the order
+ * tcgen05.cp .32x128b.warpx4 consumes. Padding blocks hold 127 (1.0). */
+int64_t sw_mx_scale_index(int64_t r, int64_t kb, int64_t kblocks);
+/* Bytes of a SW_SCALES_TC128 scale plane for rows x kblocks (padded). */
+int64_t sw_mx_scale_bytes_tc128(int64_t rows, int64_t kblocks);
+
+/* Quantise X[rows, cols] (element (r, c) at x[r*ld_x_row + c*ld_x_col],
+ * Float32) into MX blocks of 32 along `cols`.  Payload row r starts at byte
+ * r*ld_payload (E2M1: byte c/2 of the row holds element c, even c low nibble).
+ * Bit-exact with the OCP MX v1.0 restatement in oracle/sw_oracle.c.
+ * There is no reference counterpart: the reference declares MXFP8_E4M3 and
+ * MXFP4 as descriptors only (src/strideweave/carriers/_dtype/builtins.py:39-52). */
+int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t cols,
+                   int64_t ld_x_row, int64_t ld_x_col, uint8_t* payload,
+                   int64_t ld_payload, uint8_t* scales, int scale_layout,
+                   int64_t ld_scales, void* stream);
+
+/* Exact inverse image: out[r*ld_out + c] = element * 2^(scale-127)
+ * (NaN where the scale byte is 0xFF). */
+int sw_mx_dequantize(int fmt, const uint8_t* payload, int64_t ld_payload,
+                     const uint8_t* scales, int scale_layout, int64_t ld_scales,
+                     int64_t rows, int64_t cols, float* out, int64_t ld_out,
+                     void* stream);
+
+/* ---- block-scaled contraction ------------------------------------------ */
+
+#define SW_OUT_F32 0
+#define SW_OUT_BF16 1
+
+/* C[m, n] = sum_k A[m, k] * B[n, k] over MX operands, fp32 accumulation.
+ * A: payload rows of K elements (K-major) with row pitch lda bytes, scales in
+ * the SW_SCALES_TC128 placement for M x K/32; B likewise for N x K/32.
+ * C[m, n] is written at c[m*ldc_m + n*ldc_n] (elements of out_dtype); either
+ * pitch may be 1 (row- or column-major).  When `beta_one` is non-zero the
+ * result is added to C's current fp32 contents instead of replacing them.
+ * Requires fmt_a == fmt_b, M % 128 == 0, N % 128 == 0, K % 128 == 0 (E4M3) or
+ * K % 256 == 0 (E2M1), 16-byte aligned payload pointers and pitches.
+ * Replaces CpuMatmulOperation::_forward
+ * (src/strideweave/carriers/cpu/native/ops/matmul.cpp:45-113) for MX operands,
+ * which the reference refuses (operation_policy.py:1407-1440). */
+int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
+               const uint8_t* scales_a, const uint8_t* b, int64_t ldb,
+               const uint8_t* scales_b, void* c, int out_dtype, int64_t ldc_m,
+               int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
+               void* stream);
+
+/* ---- Float32 contraction (the reference's own plan) ---------------------- */
+
+/* C[m, n] = sum_k A[m, k] * B[n, k], Float32 products accumulated in Float32,
+ * for arbitrary element strides (a[m*sam + k*sak], b[n*sbn + k*sbk],
+ * c[m*scm + n*scn]).
+ * Replaces CpuMatmulOperation::_forward
+ * (src/strideweave/carriers/cpu/native/ops/matmul.cpp:45-113) for the
+ * BINARY32 / FLOATING / Float32 plan (operation_policy.py:784-815). */
+int sw_matmul_f32(const float* a, int64_t sam, int64_t sak, const float* b,
+                  int64_t sbn, int64_t sbk, float* c, int64_t scm, int64_t scn,
+                  int64_t M, int64_t N, int64_t K, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STRIDEWEAVE_B200_H */

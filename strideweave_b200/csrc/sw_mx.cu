@@ -1,0 +1,348 @@
+// sw_mx.cu - OCP MX v1.0 quantise / dequantise (MXFP8_E4M3 and MXFP4 E2M1
+// payload planes plus E8M0 per-32 scale planes).
+//
+// Conversion rules (identical to the CPU restatement used by the tests):
+//   block   = 32 consecutive elements along the quantised axis (a trailing
+//             partial block uses the elements that exist);
+//   e       = floor(log2(amax)) - emax_elem (8 for E4M3, 2 for E2M1), clamped
+//             to >= -127; scale byte = e + 127;
+//   amax==0 -> scale 0x00, each zero keeps its sign;
+//   NaN/Inf -> scale 0xFF (NaN), payload codes 0;
+//   element = RNE(V * 2^-e) saturated to the largest finite element.
+// V * 2^-e is exact in binary32 whenever the result can round to a non-zero
+// element, so cvt.rn.satfinite on the product gives the exact rounding.
+//
+// There is no reference kernel: the reference registers MXFP8_E4M3 / MXFP4 as
+// descriptors only (src/strideweave/carriers/_dtype/builtins.py:39-52).
+#include <algorithm>
+#include <cstring>
+
+#include "sw_common.cuh"
+
+namespace sw {
+namespace {
+
+// floor(log2) of a finite non-zero |x| bit pattern.
+__device__ __forceinline__ int floor_log2_bits(uint32_t a) {
+    const uint32_t ex = a >> 23;
+    if (ex != 0) return int(ex) - 127;
+    return (31 - __clz(a & 0x7FFFFF)) - 149;
+}
+
+template <int FMT>
+__device__ __forceinline__ int emax_elem() { return FMT == SW_MX_E4M3 ? 8 : 2; }
+
+// Shared exponent and scale byte of a block from max |bits| over it.
+template <int FMT>
+__device__ __forceinline__ void block_scale(uint32_t amax_bits, uint8_t& scale, float& inv, bool& special) {
+    special = amax_bits >= 0x7F800000u;
+    int e;
+    if (amax_bits == 0) e = -127;
+    else e = max(floor_log2_bits(amax_bits) - emax_elem<FMT>(), -127);
+    scale = special ? uint8_t(0xFF) : uint8_t(e + 127);
+    inv = __uint_as_float(uint32_t(127 - e) << 23);  // 2^-e, normal for e in [-127, 125]
+}
+
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+    uint32_t out;
+    asm("{\n.reg .b16 lo, hi;\n"
+        "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
+        "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
+        "mov.b32 %0, {lo, hi};\n}"
+        : "=r"(out) : "f"(a), "f"(b), "f"(c), "f"(d));
+    return out;
+}
+
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+    uint32_t out;
+    asm("{\n.reg .b8 b0, b1, b2, b3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+        "mov.b32 %0, {b0, b1, b2, b3};\n}"
+        : "=r"(out)
+        : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+    return out;
+}
+
+__host__ __device__ __forceinline__ int64_t scale_offset(int layout, int64_t r, int64_t kb, int64_t kblocks,
+                                                          int64_t ld) {
+    if (layout == SW_SCALES_TC128) {
+        const int64_t katoms = (kblocks + 3) / 4;
+        return (r / 128) * katoms * 512 + (kb / 4) * 512 + (r % 32) * 16 + ((r / 32) % 4) * 4 + (kb % 4);
+    }
+    return r * ld + kb;
+}
+
+// ---- quantise: blocks along a unit-stride axis --------------------------------
+// Four threads per 32-block, eight elements each (two 16-byte loads).  A warp
+// covers eight consecutive blocks of one row.
+template <int FMT>
+__global__ void __launch_bounds__(256) quantize_rows(const float* __restrict__ x, int64_t rows, int64_t cols,
+                                                     int64_t ldx, uint8_t* __restrict__ payload, int64_t ldp,
+                                                     uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t total = rows * kblocks * 4;  // one work item per thread
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < total; t += stride) {
+        const bool live = t < total;
+        const int64_t blk = t >> 2;
+        const int part = int(t & 3);
+        const int64_t r = live ? blk / kblocks : 0;
+        const int64_t kb = live ? blk % kblocks : 0;
+        const int64_t c0 = kb * 32 + part * 8;
+        float v[8];
+        const float* src = x + r * ldx + c0;
+        if (live && c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
+            const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+            const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = (live && c0 + i < cols) ? src[i] : 0.0f;
+        }
+        uint32_t amax = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = max(amax, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        if (!live) continue;
+        uint8_t sc;
+        float inv;
+        bool special;
+        block_scale<FMT>(amax, sc, inv, special);
+        if (part == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+        float q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = special ? 0.0f : __fmul_rn(v[i], inv);
+        if (FMT == SW_MX_E4M3) {
+            uint8_t* dst = payload + r * ldp + c0;
+            const uint32_t lo = e4m3x4(q[0], q[1], q[2], q[3]);
+            const uint32_t hi = e4m3x4(q[4], q[5], q[6], q[7]);
+            if (c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 7) == 0)) {
+                *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+            } else {
+                for (int i = 0; i < 8 && c0 + i < cols; ++i)
+                    dst[i] = uint8_t(((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF);
+            }
+        } else {
+            uint8_t* dst = payload + r * ldp + c0 / 2;
+            uint32_t packed = e2m1x8(q);
+            if (c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 3) == 0)) {
+                *reinterpret_cast<uint32_t*>(dst) = packed;
+            } else {
+                // ragged tail: keep the nibbles beyond `cols` as they were
+                for (int i = 0; i < 8 && c0 + i < cols; i += 2) {
+                    const uint8_t byte = uint8_t((packed >> (4 * i)) & 0xFF);
+                    if (c0 + i + 1 < cols) dst[i / 2] = byte;
+                    else dst[i / 2] = uint8_t((dst[i / 2] & 0xF0) | (byte & 0x0F));
+                }
+            }
+        }
+    }
+}
+
+// ---- quantise: generic strides (one thread per 32-block) -----------------------
+// Threads of a warp take consecutive rows, so a unit row stride (blocks along a
+// strided axis, e.g. a transposed operand) reads 128-byte lines.
+template <int FMT>
+__global__ void __launch_bounds__(256) quantize_strided(const float* __restrict__ x, int64_t rows, int64_t cols,
+                                                        int64_t ldr, int64_t ldc, uint8_t* __restrict__ payload,
+                                                        int64_t ldp, uint8_t* __restrict__ scales, int layout,
+                                                        int64_t lds) {
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t total = rows * kblocks;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int64_t r = t % rows;
+        const int64_t kb = t / rows;
+        const int64_t c0 = kb * 32;
+        const int len = int((cols - c0) < 32 ? (cols - c0) : 32);
+        float v[32];
+        uint32_t amax = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            v[i] = i < len ? __ldcs(x + r * ldr + (c0 + i) * ldc) : 0.0f;
+            amax = max(amax, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+        }
+        uint8_t sc;
+        float inv;
+        bool special;
+        block_scale<FMT>(amax, sc, inv, special);
+        scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = special ? 0.0f : __fmul_rn(v[i], inv);
+        if (FMT == SW_MX_E4M3) {
+            uint8_t* dst = payload + r * ldp + c0;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const uint32_t w = e4m3x4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+                for (int i = 0; i < 4; ++i)
+                    if (4 * g + i < len) dst[4 * g + i] = uint8_t((w >> (8 * i)) & 0xFF);
+            }
+        } else {
+            uint8_t* dst = payload + r * ldp + c0 / 2;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const uint32_t w = e2m1x8(v + 8 * g);
+                for (int i = 0; i < 8; i += 2) {
+                    const int c = 8 * g + i;
+                    if (c >= len) break;
+                    const uint8_t byte = uint8_t((w >> (4 * i)) & 0xFF);
+                    if (c + 1 < len) dst[c / 2] = byte;
+                    else dst[c / 2] = uint8_t((dst[c / 2] & 0xF0) | (byte & 0x0F));
+                }
+            }
+        }
+    }
+}
+
+// ---- dequantise ----------------------------------------------------------------
+__device__ __forceinline__ float decode_e4m3(uint32_t c) {
+    const uint32_t s = (c >> 7) & 1, f = (c >> 3) & 15, m = c & 7;
+    float v;
+    if (f == 15 && m == 7) return __uint_as_float(0x7FC00000u);
+    if (f == 0) v = float(m) * 0.001953125f;  // m * 2^-9
+    else v = __uint_as_float(((f + 120u) << 23) | (m << 20));
+    return s ? -v : v;
+}
+
+__device__ __forceinline__ float decode_e2m1(uint32_t c) {
+    const uint32_t s = (c >> 3) & 1, f = (c >> 1) & 3, m = c & 1;
+    float v;
+    if (f == 0) v = m ? 0.5f : 0.0f;
+    else v = __uint_as_float(((f + 126u) << 23) | (m << 22));
+    return s ? -v : v;
+}
+
+__device__ __forceinline__ float pow2_scale(uint32_t sc) {
+    // 2^(sc-127); sc == 0 is the binary32 subnormal 2^-127.
+    return sc == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(sc << 23);
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restrict__ payload, int64_t ldp,
+                                                         const uint8_t* __restrict__ scales, int layout,
+                                                         int64_t lds, int64_t rows, int64_t cols,
+                                                         float* __restrict__ out, int64_t ldo) {
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t groups = (cols + 7) / 8;  // 8 elements per thread
+    const int64_t total = rows * groups;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int64_t r = t / groups;
+        const int64_t c0 = (t % groups) * 8;
+        const uint8_t sc = scales[scale_offset(layout, r, c0 / 32, kblocks, lds)];
+        const float scale = pow2_scale(sc);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int64_t c = c0 + i;
+            if (c >= cols) { v[i] = 0.0f; continue; }
+            uint32_t code;
+            if (FMT == SW_MX_E4M3) code = payload[r * ldp + c];
+            else code = (payload[r * ldp + c / 2] >> ((c & 1) * 4)) & 0xF;
+            const float e = FMT == SW_MX_E4M3 ? decode_e4m3(code) : decode_e2m1(code);
+            v[i] = sc == 0xFF ? __uint_as_float(0x7FC00000u) : __fmul_rn(e, scale);
+        }
+        float* dst = out + r * ldo + c0;
+        if (c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+            reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+            for (int i = 0; i < 8 && c0 + i < cols; ++i) dst[i] = v[i];
+        }
+    }
+}
+
+int grid_for(int64_t items, int threads) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        sms = 148;
+    }
+    const int64_t blocks = (items + threads - 1) / threads;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sms) * 16));
+}
+
+}  // namespace
+}  // namespace sw
+
+extern "C" int64_t sw_mx_scale_index(int64_t r, int64_t kb, int64_t kblocks) {
+    return sw::scale_offset(SW_SCALES_TC128, r, kb, kblocks, 0);
+}
+
+extern "C" int64_t sw_mx_scale_bytes_tc128(int64_t rows, int64_t kblocks) {
+    if (rows <= 0 || kblocks <= 0) return 0;
+    return ((rows + 127) / 128) * ((kblocks + 3) / 4) * 512;
+}
+
+extern "C" int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t cols, int64_t ld_x_row,
+                              int64_t ld_x_col, uint8_t* payload, int64_t ld_payload, uint8_t* scales,
+                              int scale_layout, int64_t ld_scales, void* stream) {
+    using namespace sw;
+    if (fmt != SW_MX_E4M3 && fmt != SW_MX_E2M1) return fail(SW_ERR_INVALID, "sw_mx_quantize: unknown format %d", fmt);
+    if (scale_layout != SW_SCALES_ROWMAJOR && scale_layout != SW_SCALES_TC128)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize: unknown scale layout %d", scale_layout);
+    if (rows < 0 || cols < 0) return fail(SW_ERR_INVALID, "sw_mx_quantize: negative extent");
+    if (rows == 0 || cols == 0) return ok();
+    if (!x || !payload || !scales) return fail(SW_ERR_INVALID, "sw_mx_quantize: null pointer");
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t min_ldp = fmt == SW_MX_E4M3 ? cols : (cols + 1) / 2;
+    if (ld_payload < min_ldp) return fail(SW_ERR_INVALID, "sw_mx_quantize: payload pitch %lld < row bytes %lld",
+                                          (long long)ld_payload, (long long)min_ldp);
+    if (scale_layout == SW_SCALES_ROWMAJOR && ld_scales < kblocks)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize: scale pitch smaller than blocks per row");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (scale_layout == SW_SCALES_TC128 && (rows % 128 != 0 || kblocks % 4 != 0)) {
+        // padding slots of the atom placement read as 1.0 (byte 127)
+        SW_CUDA_TRY(cudaMemsetAsync(scales, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s),
+                    "scale padding fill");
+    }
+    if (ld_x_col == 1) {
+        const int64_t items = rows * kblocks * 4;
+        const int grid = grid_for(items, 256);
+        if (fmt == SW_MX_E4M3)
+            quantize_rows<SW_MX_E4M3><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, payload, ld_payload, scales,
+                                                           scale_layout, ld_scales);
+        else
+            quantize_rows<SW_MX_E2M1><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, payload, ld_payload, scales,
+                                                           scale_layout, ld_scales);
+    } else {
+        const int grid = grid_for(rows * kblocks, 256);
+        if (fmt == SW_MX_E4M3)
+            quantize_strided<SW_MX_E4M3><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, ld_x_col, payload,
+                                                              ld_payload, scales, scale_layout, ld_scales);
+        else
+            quantize_strided<SW_MX_E2M1><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, ld_x_col, payload,
+                                                              ld_payload, scales, scale_layout, ld_scales);
+    }
+    SW_LAUNCH_CHECK("sw_mx_quantize launch");
+    return ok();
+}
+
+extern "C" int sw_mx_dequantize(int fmt, const uint8_t* payload, int64_t ld_payload, const uint8_t* scales,
+                                int scale_layout, int64_t ld_scales, int64_t rows, int64_t cols, float* out,
+                                int64_t ld_out, void* stream) {
+    using namespace sw;
+    if (fmt != SW_MX_E4M3 && fmt != SW_MX_E2M1) return fail(SW_ERR_INVALID, "sw_mx_dequantize: unknown format %d", fmt);
+    if (scale_layout != SW_SCALES_ROWMAJOR && scale_layout != SW_SCALES_TC128)
+        return fail(SW_ERR_INVALID, "sw_mx_dequantize: unknown scale layout %d", scale_layout);
+    if (rows < 0 || cols < 0) return fail(SW_ERR_INVALID, "sw_mx_dequantize: negative extent");
+    if (rows == 0 || cols == 0) return ok();
+    if (!payload || !scales || !out) return fail(SW_ERR_INVALID, "sw_mx_dequantize: null pointer");
+    if (ld_out < cols) return fail(SW_ERR_INVALID, "sw_mx_dequantize: output pitch smaller than a row");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int grid = grid_for(rows * ((cols + 7) / 8), 256);
+    if (fmt == SW_MX_E4M3)
+        dequantize_kernel<SW_MX_E4M3><<<grid, 256, 0, s>>>(payload, ld_payload, scales, scale_layout, ld_scales,
+                                                           rows, cols, out, ld_out);
+    else
+        dequantize_kernel<SW_MX_E2M1><<<grid, 256, 0, s>>>(payload, ld_payload, scales, scale_layout, ld_scales,
+                                                           rows, cols, out, ld_out);
+    SW_LAUNCH_CHECK("sw_mx_dequantize launch");
+    return ok();
+}

@@ -1,0 +1,434 @@
+// sw_mx_gemm.cu - block-scaled MX contraction on the 5th-generation tensor
+// cores: C[m, n] = sum_k A[m, k] * B[n, k] with E4M3 (kind::mxf8f6f4) or
+// packed E2M1 (kind::mxf4) payloads and E8M0 per-32 scales, fp32 accumulated
+// in TMEM.
+//
+// One persistent CTA per SM walks 128 x BN output tiles.  Warp roles:
+//   warp 0 - TMA producer: 2-D tiled loads of the payload tiles (128-byte
+//            swizzled rows) and 1-D bulk loads of the scale atoms into a
+//            4-stage shared-memory ring;
+//   warp 1 - allocates TMEM; one thread copies each stage's scale atoms from
+//            shared memory into TMEM (tcgen05.cp .32x128b.warpx4) and issues
+//            the tcgen05.mma block_scale instructions, committing each stage
+//            back to the producer and each finished tile to the epilogue;
+//   warps 2..5 - epilogue: tcgen05.ld of the accumulator, fp32 or bf16 stores.
+// The scale atoms are read exactly as the carrier stores them (the
+// SW_SCALES_TC128 placement): a 512-byte atom holds 128 rows x 4 blocks in the
+// order the tcgen05.cp replication expects, so no shuffle is needed.
+//
+// Every mbarrier wait is bounded; a wait that gives up records SW_ERR_TIMEOUT
+// and its role unwinds, waiting (bounded) for its own copies and MMAs in
+// flight before the CTA frees TMEM and exits.
+//
+// Reference counterpart: CpuMatmulOperation::_forward
+// (src/strideweave/carriers/cpu/native/ops/matmul.cpp:45-113) contracts mode 1
+// of both operands, i.e. C = A * B^T with both operands K-major, as here.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "sw_common.cuh"
+#include "sw_ptx.cuh"
+
+namespace sw {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBKBytes = 128;  // payload bytes of K per stage (one 128B swizzle row)
+constexpr int kStages = 4;
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kTmemCols = 512;
+
+template <int FMT, int BN>
+struct Cfg {
+    static constexpr int kAtoms = FMT == SW_MX_E4M3 ? 1 : 2;      // scale atoms (4 blocks) per stage
+    static constexpr int kABytes = kBM * kBKBytes;                 // 16 KiB
+    static constexpr int kBBytes = BN * kBKBytes;
+    static constexpr int kSfaBytes = kAtoms * 512;
+    static constexpr int kSfbBytes = (BN / 128) * kAtoms * 512;
+    static constexpr int kMmaPerStage = 4;                         // K=32 (E4M3) or K=64 (E2M1) each
+    static constexpr int kSfaCols = 4 * kAtoms;
+    static constexpr int kSfbCols = 4 * kAtoms * (BN / 128);
+    static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
+    static constexpr int kAccCol = 0;
+    static constexpr int kSfCol0 = BN;                             // scale columns follow the accumulator
+    static_assert(BN + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kABytes;
+    static constexpr int kOffSfa = kOffB + kStages * kBBytes;
+    static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
+    static constexpr int kOffBar = kOffSfb + kStages * kSfbBytes;
+    static constexpr int kNumBars = 2 * kStages + 3;
+    static constexpr int kOffSlot = kOffBar + kNumBars * 8;
+    static constexpr int kSmemBytes = kOffSlot + 16 + 1024;        // + alignment slack
+    static constexpr uint32_t kStageTx = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+};
+
+// Instruction descriptor of a block-scaled MMA (E8M0 scales, K-major A and B).
+__device__ __forceinline__ uint32_t make_idesc(uint32_t fmt_code, int M, int N, uint32_t sfa_id, uint32_t sfb_id) {
+    return (sfb_id << 4) | (fmt_code << 7) | (fmt_code << 10) | (uint32_t(N >> 3) << 17) | (1u << 23) |
+           (uint32_t(M >> 4) << 24) | (sfa_id << 29);
+}
+
+struct GemmArgs {
+    const uint8_t* sfa;
+    const uint8_t* sfb;
+    void* c;
+    int64_t ldc_m, ldc_n;
+    int M, N, K;          // K in elements
+    int k_stages;         // K / elements-per-stage
+    int katoms;           // scale atoms per row group (ceil(K/128))
+    int beta_one;
+    int out_bf16;
+};
+
+template <int FMT, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                   const GemmArgs args) {
+    using C = Cfg<FMT, BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = ptx::smem_addr(smem);
+    const uint32_t bar_full = sbase + C::kOffBar;             // kStages barriers
+    const uint32_t bar_empty = bar_full + kStages * 8;        // kStages barriers
+    const uint32_t bar_tmem_full = bar_empty + kStages * 8;
+    const uint32_t bar_tmem_empty = bar_tmem_full + 8;
+    const uint32_t bar_drain = bar_tmem_empty + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffSlot);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            ptx::mbar_init(bar_full + 8 * s, 1);
+            ptx::mbar_init(bar_empty + 8 * s, 1);
+        }
+        ptx::mbar_init(bar_tmem_full, 1);
+        ptx::mbar_init(bar_tmem_empty, 128);
+        ptx::mbar_init(bar_drain, 1);
+        ptx::fence_barrier_init();
+        ptx::prefetch_tmap(&tmap_a);
+        ptx::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(ptx::smem_addr(tmem_slot), kTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int num_m = args.M / kBM;
+    const int num_n = args.N / BN;
+    const int num_tiles = num_m * num_n;
+    constexpr int kGroup = 8;  // M blocks per raster group (L2 reuse of B)
+
+    auto tile_coords = [&](int t, int& mb, int& nb) {
+        const int per_group = kGroup * num_n;
+        const int g = t / per_group;
+        const int first = g * kGroup;
+        const int gsize = min(num_m - first, kGroup);
+        const int r = t % per_group;
+        mb = first + r % gsize;
+        nb = r / gsize;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued[kStages] = {0};
+            bool alive = true;
+            for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, mb, nb);
+                for (int ks = 0; ks < args.k_stages; ++ks) {
+                    if (!ptx::mbar_wait(bar_empty + 8 * stage, phase ^ 1)) { alive = false; break; }
+                    const uint32_t full = bar_full + 8 * stage;
+                    ptx::mbar_arrive_expect_tx(full, C::kStageTx);
+                    ptx::tma_load_2d(sbase + C::kOffA + stage * C::kABytes, &tmap_a, ks * kBKBytes, mb * kBM, full);
+                    ptx::tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tmap_b, ks * kBKBytes, nb * BN, full);
+                    const int64_t atom0 = int64_t(ks) * C::kAtoms;
+                    ptx::bulk_load(sbase + C::kOffSfa + stage * C::kSfaBytes,
+                                   args.sfa + (int64_t(mb) * args.katoms + atom0) * 512, C::kSfaBytes, full);
+#pragma unroll
+                    for (int g = 0; g < BN / 128; ++g) {
+                        ptx::bulk_load(sbase + C::kOffSfb + stage * C::kSfbBytes + g * C::kAtoms * 512,
+                                       args.sfb + ((int64_t(nb) * (BN / 128) + g) * args.katoms + atom0) * 512,
+                                       C::kAtoms * 512, full);
+                    }
+                    issued[stage] += 1;
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            // Let every copy this thread started land before the CTA can exit.
+            for (int s = 0; s < kStages; ++s)
+                if (issued[s] > 0) ptx::mbar_wait(bar_full + 8 * s, (issued[s] - 1) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            const uint32_t fmt_code = FMT == SW_MX_E4M3 ? 0u : 1u;
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t tile_iter = 0;
+            bool alive = true;
+            for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x, ++tile_iter) {
+                // the epilogue must have drained the accumulator of the previous tile
+                if (!ptx::mbar_wait(bar_tmem_empty, (tile_iter & 1) ^ 1)) break;
+                ptx::tc_fence_after();
+                for (int ks = 0; ks < args.k_stages; ++ks) {
+                    if (!ptx::mbar_wait(bar_full + 8 * stage, phase)) { alive = false; break; }
+                    ptx::tc_fence_after();
+                    const uint32_t sf_col = tmem + C::kSfCol0 + stage * C::kSfColsPerStage;
+                    const uint32_t sfa_col = sf_col;
+                    const uint32_t sfb_col = sf_col + C::kSfaCols;
+                    // scale atoms: shared memory -> TMEM (replicated per sub-partition)
+#pragma unroll
+                    for (int a = 0; a < C::kAtoms; ++a) {
+                        ptx::tc_cp_32x128b_x4(sfa_col + 4 * a,
+                                              ptx::smem_desc(sbase + C::kOffSfa + stage * C::kSfaBytes + a * 512, 0,
+                                                             128, ptx::kLayoutNone));
+#pragma unroll
+                        for (int g = 0; g < BN / 128; ++g)
+                            ptx::tc_cp_32x128b_x4(
+                                sfb_col + a * 4 * (BN / 128) + 4 * g,
+                                ptx::smem_desc(sbase + C::kOffSfb + stage * C::kSfbBytes + (g * C::kAtoms + a) * 512,
+                                               0, 128, ptx::kLayoutNone));
+                    }
+                    const uint32_t a_addr = sbase + C::kOffA + stage * C::kABytes;
+                    const uint32_t b_addr = sbase + C::kOffB + stage * C::kBBytes;
+#pragma unroll
+                    for (int j = 0; j < C::kMmaPerStage; ++j) {
+                        // 32 payload bytes of K per MMA in both formats
+                        const uint64_t adesc = ptx::smem_desc(a_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
+                        const uint64_t bdesc = ptx::smem_desc(b_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
+                        const uint32_t accumulate = (ks > 0 || j > 0) ? 1u : 0u;
+                        if (FMT == SW_MX_E4M3) {
+                            const uint32_t idesc = make_idesc(fmt_code, kBM, BN, uint32_t(j), uint32_t(j));
+                            ptx::mma_mxf8f6f4(tmem + C::kAccCol, adesc, bdesc, idesc, accumulate, sfa_col, sfb_col);
+                        } else {
+                            const int atom = j / 2;
+                            const uint32_t sf_id = uint32_t((2 * j) % 4);
+                            const uint32_t idesc = make_idesc(fmt_code, kBM, BN, sf_id, sf_id);
+                            ptx::mma_mxf4(tmem + C::kAccCol, adesc, bdesc, idesc, accumulate, sfa_col + 4 * atom,
+                                          sfb_col + atom * 4 * (BN / 128));
+                        }
+                    }
+                    ptx::tc_commit(bar_empty + 8 * stage);  // frees the smem stage and its scale columns
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+                if (!alive) break;
+                ptx::tc_commit(bar_tmem_full);
+            }
+            // Drain every MMA this thread issued before TMEM is released.
+            ptx::tc_commit(bar_drain);
+            ptx::mbar_wait(bar_drain, 0);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;  // TMEM sub-partition this warp may access
+        const int row_in_tile = quarter * 32 + lane;
+        uint32_t tile_iter = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
+            int mb, nb;
+            tile_coords(t, mb, nb);
+            if (!ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) break;
+            ptx::tc_fence_after();
+            const int64_t m = int64_t(mb) * kBM + row_in_tile;
+#pragma unroll 1
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                uint32_t r[32];
+                ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + chunk * 32, r);
+                ptx::tmem_ld_wait();
+                const int64_t n0 = int64_t(nb) * BN + chunk * 32;
+                if (args.out_bf16) {
+                    __nv_bfloat16* cptr = static_cast<__nv_bfloat16*>(args.c);
+                    if (args.ldc_n == 1 && (((m * args.ldc_m + n0) & 7) == 0) &&
+                        ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
+                        uint4* dst = reinterpret_cast<uint4*>(cptr + m * args.ldc_m + n0);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            float f[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                f[e] = __uint_as_float(r[8 * v + e]);
+                                if (args.beta_one) f[e] += __bfloat162float(cptr[m * args.ldc_m + n0 + 8 * v + e]);
+                            }
+                            __nv_bfloat162 h[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+                            dst[v] = *reinterpret_cast<uint4*>(h);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            __nv_bfloat16* p = cptr + m * args.ldc_m + (n0 + e) * args.ldc_n;
+                            float f = __uint_as_float(r[e]);
+                            if (args.beta_one) f += __bfloat162float(*p);
+                            *p = __float2bfloat16_rn(f);
+                        }
+                    }
+                } else {
+                    float* cptr = static_cast<float*>(args.c);
+                    if (args.ldc_n == 1 && (((m * args.ldc_m + n0) & 3) == 0) &&
+                        ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
+                        float4* dst = reinterpret_cast<float4*>(cptr + m * args.ldc_m + n0);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                            if (args.beta_one) {
+                                const float4 old = dst[v];
+                                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+                            }
+                            dst[v] = o;
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            float* p = cptr + m * args.ldc_m + (n0 + e) * args.ldc_n;
+                            float f = __uint_as_float(r[e]);
+                            if (args.beta_one) f += *p;
+                            *p = f;
+                        }
+                    }
+                }
+            }
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(bar_tmem_empty);
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    if (warp == 1) ptx::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---- host side -------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// 2-D uint8 map over rows x row_bytes (pitch ld), box 128 bytes x box_rows,
+// 128-byte swizzle (the canonical K-major layout of the UMMA descriptors).
+int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int64_t ld,
+                     uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return fail(SW_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld};
+    cuuint32_t box[2] = {(cuuint32_t)kBKBytes, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SW_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SW_OK;
+}
+
+template <int FMT, int BN>
+int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t* b, int64_t ldb,
+                const uint8_t* sfb, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N,
+                int64_t K, int beta_one, cudaStream_t stream) {
+    using Cf = Cfg<FMT, BN>;
+    const int64_t row_bytes = FMT == SW_MX_E4M3 ? K : K / 2;
+    CUtensorMap ma, mb;
+    int rc = make_operand_map(&ma, a, M, row_bytes, lda, kBM);
+    if (rc != SW_OK) return rc;
+    rc = make_operand_map(&mb, b, N, row_bytes, ldb, BN);
+    if (rc != SW_OK) return rc;
+    GemmArgs args;
+    args.sfa = sfa;
+    args.sfb = sfb;
+    args.c = c;
+    args.ldc_m = ldc_m;
+    args.ldc_n = ldc_n;
+    args.M = (int)M;
+    args.N = (int)N;
+    args.K = (int)K;
+    args.k_stages = (int)(row_bytes / kBKBytes);
+    args.katoms = (int)((K / 32 + 3) / 4);
+    args.beta_one = beta_one;
+    args.out_bf16 = out_dtype == SW_OUT_BF16;
+    auto kernel = mx_gemm_kernel<FMT, BN>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
+                    "set gemm smem");
+        attr_set = true;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t tiles = (M / kBM) * (N / BN);
+    const int grid = (int)std::min<int64_t>(tiles, sms);
+    kernel<<<grid, kThreads, Cf::kSmemBytes, stream>>>(ma, mb, args);
+    SW_LAUNCH_CHECK("mx_gemm launch");
+    return SW_OK;
+}
+
+}  // namespace
+}  // namespace sw
+
+extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
+                          const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
+                          int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
+                          void* stream) {
+    using namespace sw;
+    if (fmt_a != fmt_b) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: mixed operand formats are not supported");
+    if (fmt_a != SW_MX_E4M3 && fmt_a != SW_MX_E2M1) return fail(SW_ERR_INVALID, "sw_mx_gemm: unknown format %d", fmt_a);
+    if (out_dtype != SW_OUT_F32 && out_dtype != SW_OUT_BF16)
+        return fail(SW_ERR_INVALID, "sw_mx_gemm: unknown output dtype %d", out_dtype);
+    if (M < 0 || N < 0 || K < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: negative extent");
+    if (M == 0 || N == 0) return ok();
+    if (!a || !b || !scales_a || !scales_b || !c) return fail(SW_ERR_INVALID, "sw_mx_gemm: null pointer");
+    const int64_t kq = fmt_a == SW_MX_E4M3 ? 128 : 256;
+    if (M % 128 != 0 || N % 128 != 0 || K % kq != 0 || K == 0)
+        return fail(SW_ERR_UNSUPPORTED,
+                    "sw_mx_gemm: needs M %% 128 == 0, N %% 128 == 0, K %% %lld == 0 (got %lld x %lld x %lld)",
+                    (long long)kq, (long long)M, (long long)N, (long long)K);
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: extent too large");
+    const int64_t row_bytes = fmt_a == SW_MX_E4M3 ? K : K / 2;
+    if (lda < row_bytes || ldb < row_bytes || lda % 16 != 0 || ldb % 16 != 0)
+        return fail(SW_ERR_INVALID, "sw_mx_gemm: payload pitches must cover a row and be multiples of 16 bytes");
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(scales_a) |
+         reinterpret_cast<uintptr_t>(scales_b)) & 15)
+        return fail(SW_ERR_INVALID, "sw_mx_gemm: payload and scale planes must be 16-byte aligned");
+    if (ldc_m < 1 || ldc_n < 1) return fail(SW_ERR_INVALID, "sw_mx_gemm: output pitches must be positive");
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc;
+    if (fmt_a == SW_MX_E4M3) {
+        rc = (N % 256 == 0) ? launch_gemm<SW_MX_E4M3, 256>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
+                                                            ldc_n, M, N, K, beta_one, s)
+                            : launch_gemm<SW_MX_E4M3, 128>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
+                                                            ldc_n, M, N, K, beta_one, s);
+    } else {
+        rc = (N % 256 == 0) ? launch_gemm<SW_MX_E2M1, 256>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
+                                                            ldc_n, M, N, K, beta_one, s)
+                            : launch_gemm<SW_MX_E2M1, 128>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
+                                                            ldc_n, M, N, K, beta_one, s);
+    }
+    if (rc != SW_OK) return rc;
+    return ok();
+}

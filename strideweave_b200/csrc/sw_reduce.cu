@@ -1,0 +1,617 @@
+// sw_reduce.cu - layout-aware Float32 reductions (sum, max, argmax) over the
+// second mode of a two-mode view, for any hierarchical strides and an optional
+// carrier-level XOR swizzle.
+//
+// Semantics follow the reference CPU carrier exactly where it pins them:
+//   max    (src/strideweave/carriers/cpu/native/_cpu_reduction.hpp:21-32): the
+//          first NaN in logical order wins with its payload; two zeros of any
+//          sign give +0; otherwise the larger value.  This rule is associative
+//          and commutative once NaNs carry their ordinal, so a tree over any
+//          partition of the fibre reproduces the sequential fold bit for bit.
+//   argmax (_cpu_reduction.hpp:76-93): NaN beats every number, the first NaN
+//          wins, otherwise the first ordinal holding the largest value
+//          (-0 == +0).  Ordered by (is-NaN, value, -ordinal), so again any
+//          tree order gives the sequential answer.
+//   sum    (ops/reduce_sum.cpp:12-28): Float32 accumulation; the tree order
+//          differs from the sequential one, within the path's tolerance.
+//
+// Kernels (chosen on the host from the lowered plan):
+//   rows_vec  - the reduced mode has a unit-stride leaf: one warp per kept
+//               ordinal streams 16-byte vectors along it.
+//   cols_vec  - the kept mode has a unit-stride leaf: each thread owns four
+//               adjacent kept ordinals; the fibre is split over the 8 warps
+//               of a CTA and over the CTAs of a thread-block cluster, whose
+//               partials meet in distributed shared memory (no scratch
+//               memory, no second launch).
+//   gather    - anything else: one warp per kept ordinal, scalar loads.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "sw_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace sw {
+namespace {
+
+struct LeafSet {
+    int rank;
+    int64_t shape[SW_MAX_LEAVES];
+    int64_t stride[SW_MAX_LEAVES];
+    int64_t weight[SW_MAX_LEAVES];  // logical ordinal weight (colexicographic)
+};
+
+struct Swz {
+    int rank;
+    int bits[SW_MAX_SWIZZLE];
+    int base[SW_MAX_SWIZZLE];
+    int shift[SW_MAX_SWIZZLE];
+};
+
+struct DevPlan {
+    int64_t offset;
+    int64_t x_size;
+    int64_t n_kept;
+    int64_t n_red;
+    LeafSet kept;
+    LeafSet red;
+    Swz swz;
+};
+
+__device__ __forceinline__ int64_t swizzle(const Swz& s, int64_t r) {
+#pragma unroll
+    for (int i = 0; i < SW_MAX_SWIZZLE; ++i) {
+        if (i < s.rank) {
+            const int64_t mask = (int64_t(1) << s.bits[i]) - 1;
+            if (s.shift[i] > 0) {
+                r ^= ((r >> (s.base[i] + s.shift[i])) & mask) << s.base[i];
+            } else {
+                r ^= ((r >> s.base[i]) & mask) << (s.base[i] - s.shift[i]);
+            }
+        }
+    }
+    return r;
+}
+
+// Offset of kept ordinal i (decomposed first-leaf-fastest over the kept leaves
+// in their logical order).
+__device__ __forceinline__ int64_t kept_offset(const LeafSet& k, int64_t i) {
+    int64_t off = 0;
+    for (int l = 0; l < k.rank; ++l) {
+        const int64_t c = i % k.shape[l];
+        i /= k.shape[l];
+        off += c * k.stride[l];
+    }
+    return off;
+}
+
+// ---- reduction states ------------------------------------------------------
+
+struct SumOp {
+    struct S { float v; };
+    static __device__ __forceinline__ S identity() { return {0.0f}; }
+    static __device__ __forceinline__ void add(S& s, float v, int64_t) { s.v += v; }
+    static __device__ __forceinline__ void merge(S& a, const S& b) { a.v += b.v; }
+    static __device__ __forceinline__ S shfl(const S& s, int lane_mask) {
+        return {__shfl_xor_sync(0xffffffffu, s.v, lane_mask)};
+    }
+};
+
+struct MaxOp {
+    struct S { float v; int64_t j; };  // j only orders NaNs
+    static __device__ __forceinline__ S identity() { return {-INFINITY, INT64_MAX}; }
+    static __device__ __forceinline__ void add(S& s, float v, int64_t j) { merge(s, S{v, j}); }
+    static __device__ __forceinline__ void merge(S& a, const S& b) {
+        const bool na = isnan(a.v), nb = isnan(b.v);
+        if (na || nb) {
+            if (nb && (!na || b.j < a.j)) a = b;
+            return;
+        }
+        if (a.v == b.v && a.v == 0.0f) {
+            a.v = 0.0f;  // two zeros of any sign give +0
+            return;
+        }
+        if (b.v > a.v) a = b;
+    }
+    static __device__ __forceinline__ S shfl(const S& s, int m) {
+        return {__shfl_xor_sync(0xffffffffu, s.v, m),
+                (int64_t)__shfl_xor_sync(0xffffffffu, (long long)s.j, m)};
+    }
+};
+
+struct ArgmaxOp {
+    struct S { float v; int64_t j; };
+    static __device__ __forceinline__ S identity() { return {-INFINITY, INT64_MAX}; }
+    static __device__ __forceinline__ void add(S& s, float v, int64_t j) { merge(s, S{v, j}); }
+    static __device__ __forceinline__ void merge(S& a, const S& b) {
+        const bool na = isnan(a.v), nb = isnan(b.v);
+        bool take;
+        if (na != nb) take = nb;
+        else if (na) take = b.j < a.j;
+        else take = b.v > a.v || (b.v == a.v && b.j < a.j);
+        if (take) a = b;
+    }
+    static __device__ __forceinline__ S shfl(const S& s, int m) {
+        return {__shfl_xor_sync(0xffffffffu, s.v, m),
+                (int64_t)__shfl_xor_sync(0xffffffffu, (long long)s.j, m)};
+    }
+};
+
+template <class Op>
+__device__ __forceinline__ void store_result(void* out, int64_t i, const typename Op::S& s);
+
+template <>
+__device__ __forceinline__ void store_result<SumOp>(void* out, int64_t i, const SumOp::S& s) {
+    static_cast<float*>(out)[i] = s.v;
+}
+template <>
+__device__ __forceinline__ void store_result<MaxOp>(void* out, int64_t i, const MaxOp::S& s) {
+    static_cast<float*>(out)[i] = s.v;
+}
+template <>
+__device__ __forceinline__ void store_result<ArgmaxOp>(void* out, int64_t i, const ArgmaxOp::S& s) {
+    static_cast<int32_t*>(out)[i] = (int32_t)s.j;
+}
+
+template <class Op>
+__device__ __forceinline__ typename Op::S warp_reduce(typename Op::S s) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) Op::merge(s, Op::shfl(s, m));
+    return s;
+}
+
+__device__ __forceinline__ float4 load_stream4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float load_stream1(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+// Odometer over the reduced leaves 1..rank-1 (leaf 0 is walked separately).
+struct OuterCursor {
+    int64_t key[SW_MAX_LEAVES];
+    int64_t off;   // flat offset contribution
+    int64_t ord;   // logical ordinal contribution
+};
+
+__device__ __forceinline__ void cursor_set(OuterCursor& c, const LeafSet& r, int64_t o) {
+    c.off = 0;
+    c.ord = 0;
+    for (int l = 1; l < r.rank; ++l) {
+        c.key[l] = o % r.shape[l];
+        o /= r.shape[l];
+        c.off += c.key[l] * r.stride[l];
+        c.ord += c.key[l] * r.weight[l];
+    }
+}
+
+__device__ __forceinline__ void cursor_step(OuterCursor& c, const LeafSet& r) {
+    for (int l = 1; l < r.rank; ++l) {
+        c.key[l] += 1;
+        c.off += r.stride[l];
+        c.ord += r.weight[l];
+        if (c.key[l] < r.shape[l]) return;
+        c.off -= r.stride[l] * r.shape[l];
+        c.ord -= r.weight[l] * r.shape[l];
+        c.key[l] = 0;
+    }
+}
+
+// ---- rows_vec ----------------------------------------------------------------
+// Reduced leaf 0 has stride 1 and a length divisible by 4; every other stride,
+// the offset and the swizzle keep 16-byte vectors intact (checked on the host).
+template <class Op>
+__global__ void __launch_bounds__(256) reduce_rows_vec(const float* __restrict__ x, DevPlan p, void* out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    const int64_t nv0 = p.red.shape[0] >> 2;          // vectors per leaf-0 run
+    const int64_t nvec = p.n_red >> 2;                // vectors per fibre
+    constexpr int U = 8;
+    for (int64_t i = warp; i < p.n_kept; i += nwarps) {
+        const int64_t row = p.offset + kept_offset(p.kept, i);
+        typename Op::S acc[4] = {Op::identity(), Op::identity(), Op::identity(), Op::identity()};
+        int64_t q = lane;
+        int64_t v0 = q % nv0;
+        OuterCursor cur;
+        cursor_set(cur, p.red, q / nv0);
+        while (q < nvec) {
+            float4 val[U];
+            int64_t ord[U];
+            bool live[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                live[u] = q < nvec;
+                if (live[u]) {
+                    const int64_t f = swizzle(p.swz, row + v0 * 4 + cur.off);
+                    val[u] = load_stream4(x + f);
+                    ord[u] = v0 * 4 * p.red.weight[0] + cur.ord;
+                    q += 32;
+                    v0 += 32;
+                    while (v0 >= nv0) {
+                        v0 -= nv0;
+                        cursor_step(cur, p.red);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (live[u]) {
+                    const int64_t w = p.red.weight[0];
+                    Op::add(acc[0], val[u].x, ord[u]);
+                    Op::add(acc[1], val[u].y, ord[u] + w);
+                    Op::add(acc[2], val[u].z, ord[u] + 2 * w);
+                    Op::add(acc[3], val[u].w, ord[u] + 3 * w);
+                }
+            }
+        }
+        Op::merge(acc[0], acc[1]);
+        Op::merge(acc[2], acc[3]);
+        Op::merge(acc[0], acc[2]);
+        typename Op::S r = warp_reduce<Op>(acc[0]);
+        if (lane == 0) store_result<Op>(out, i, r);
+    }
+}
+
+// ---- cols_vec ----------------------------------------------------------------
+// Kept leaf 0 has stride 1 and a length divisible by 4.  Block = 256 threads:
+// 32 lanes x 4 kept ordinals = 128 kept ordinals per CTA, 8 warps split the
+// fibre; `gridDim.y` CTAs of one cluster split it further.
+constexpr int kColsThreads = 256;
+constexpr int kColsWarps = kColsThreads / 32;
+
+template <class Op>
+__global__ void __launch_bounds__(kColsThreads) reduce_cols_vec(const float* __restrict__ x, DevPlan p, void* out) {
+    __shared__ typename Op::S part[kColsWarps][32][4];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int splits = (int)cluster.num_blocks();
+    const int split = (int)cluster.block_rank();
+    const int64_t kv = int64_t(blockIdx.x) * 32 + lane;     // kept vector index
+    const int64_t nkv = p.n_kept >> 2;
+    const bool live_col = kv < nkv;
+    int64_t col = 0;
+    if (live_col) col = p.offset + kept_offset(p.kept, kv * 4);
+    typename Op::S acc[4] = {Op::identity(), Op::identity(), Op::identity(), Op::identity()};
+    // Fibre slice of this (split, warp).
+    const int64_t per = (p.n_red + splits - 1) / splits;
+    const int64_t j0 = per * split;
+    const int64_t j1 = min(p.n_red, j0 + per);
+    if (live_col && j0 < j1) {
+        // Reduced leaves walked as one odometer; this thread takes every
+        // kColsWarps-th ordinal of its split.
+        int64_t j = j0 + warp;
+        int64_t key[SW_MAX_LEAVES];
+        int64_t off = 0, ord = 0;
+        {
+            int64_t t = j;
+            for (int l = 0; l < p.red.rank; ++l) {
+                key[l] = t % p.red.shape[l];
+                t /= p.red.shape[l];
+                off += key[l] * p.red.stride[l];
+                ord += key[l] * p.red.weight[l];
+            }
+        }
+        constexpr int U = 4;
+        while (j < j1) {
+            float4 val[U];
+            int64_t o[U];
+            bool live[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                live[u] = j < j1;
+                if (live[u]) {
+                    val[u] = load_stream4(x + swizzle(p.swz, col + off));
+                    o[u] = ord;
+                    j += kColsWarps;
+                    // advance the odometer by kColsWarps ordinals
+                    for (int s = 0; s < kColsWarps; ++s) {
+                        for (int l = 0; l < p.red.rank; ++l) {
+                            key[l] += 1;
+                            off += p.red.stride[l];
+                            ord += p.red.weight[l];
+                            if (key[l] < p.red.shape[l]) break;
+                            off -= p.red.stride[l] * p.red.shape[l];
+                            ord -= p.red.weight[l] * p.red.shape[l];
+                            key[l] = 0;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (live[u]) {
+                    Op::add(acc[0], val[u].x, o[u]);
+                    Op::add(acc[1], val[u].y, o[u]);
+                    Op::add(acc[2], val[u].z, o[u]);
+                    Op::add(acc[3], val[u].w, o[u]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) part[warp][lane][e] = acc[e];
+    __syncthreads();
+    // Fold the 8 warps into warp 0's slot.
+    if (warp == 0) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            typename Op::S s = part[0][lane][e];
+            for (int w = 1; w < kColsWarps; ++w) Op::merge(s, part[w][lane][e]);
+            part[0][lane][e] = s;
+        }
+    }
+    cluster.sync();
+    // Rank 0 folds every CTA's partial through distributed shared memory.
+    if (split == 0 && warp == 0 && live_col) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            typename Op::S s = part[0][lane][e];
+            for (int r = 1; r < splits; ++r) {
+                typename Op::S(*peer)[32][4] = cluster.map_shared_rank(part, r);
+                Op::merge(s, peer[0][lane][e]);
+            }
+            store_result<Op>(out, kv * 4 + e, s);
+        }
+    }
+    cluster.sync();  // peers keep their shared memory alive until rank 0 read it
+}
+
+// ---- gather ------------------------------------------------------------------
+template <class Op>
+__global__ void __launch_bounds__(256) reduce_gather(const float* __restrict__ x, DevPlan p, void* out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t i = warp; i < p.n_kept; i += nwarps) {
+        const int64_t row = p.offset + kept_offset(p.kept, i);
+        typename Op::S acc = Op::identity();
+        for (int64_t j = lane; j < p.n_red; j += 32) {
+            int64_t t = j, off = 0, ord = 0;
+            for (int l = 0; l < p.red.rank; ++l) {
+                const int64_t c = t % p.red.shape[l];
+                t /= p.red.shape[l];
+                off += c * p.red.stride[l];
+                ord += c * p.red.weight[l];
+            }
+            const int64_t f = swizzle(p.swz, row + off);
+            if (f < 0 || f >= p.x_size) {
+                report_device_error(SW_ERR_INVALID);
+                continue;
+            }
+            Op::add(acc, load_stream1(x + f), ord);
+        }
+        acc = warp_reduce<Op>(acc);
+        if (lane == 0) store_result<Op>(out, i, acc);
+    }
+}
+
+// ---- host-side lowering --------------------------------------------------------
+
+int sm_count() {
+    static int count = -1;
+    if (count < 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            count = 148;
+        }
+    }
+    return count;
+}
+
+// Drops unit leaves, records logical weights, merges leaves that walk memory
+// contiguously and keep logical order (weight[l+1] == shape[l]*weight[l]).
+void lower_leaves(int rank, const int64_t* shape, const int64_t* stride, LeafSet& out, int64_t& numel) {
+    out.rank = 0;
+    numel = 1;
+    int64_t weight = 1;
+    for (int l = 0; l < rank; ++l) {
+        if (shape[l] != 1) {
+            int r = out.rank;
+            if (r > 0 && out.stride[r - 1] * out.shape[r - 1] == stride[l] &&
+                out.weight[r - 1] * out.shape[r - 1] == weight) {
+                out.shape[r - 1] *= shape[l];
+            } else {
+                out.shape[r] = shape[l];
+                out.stride[r] = stride[l];
+                out.weight[r] = weight;
+                out.rank = r + 1;
+            }
+        }
+        weight *= shape[l];
+        numel *= shape[l];
+    }
+}
+
+// Moves leaf `l` to position 0 (traversal order only; weights keep the
+// logical ordinal).
+void leaf_to_front(LeafSet& s, int l) {
+    if (l <= 0) return;
+    LeafSet t = s;
+    s.shape[0] = t.shape[l];
+    s.stride[0] = t.stride[l];
+    s.weight[0] = t.weight[l];
+    int w = 1;
+    for (int i = 0; i < t.rank; ++i) {
+        if (i == l) continue;
+        s.shape[w] = t.shape[i];
+        s.stride[w] = t.stride[i];
+        s.weight[w] = t.weight[i];
+        ++w;
+    }
+}
+
+int unit_leaf(const LeafSet& s) {
+    for (int l = 0; l < s.rank; ++l)
+        if (s.stride[l] == 1 && s.shape[l] % 4 == 0) return l;
+    return -1;
+}
+
+bool strides_mult4(const LeafSet& s, int skip) {
+    for (int l = 0; l < s.rank; ++l)
+        if (l != skip && s.stride[l] % 4 != 0) return false;
+    return true;
+}
+
+// A swizzle keeps 4-element vectors intact when no stage reads or writes
+// bits 0..1 of the flat index.
+bool swizzle_keeps_vec4(const Swz& s) {
+    for (int i = 0; i < s.rank; ++i) {
+        const int tgt = s.shift[i] > 0 ? s.base[i] : s.base[i] - s.shift[i];
+        const int src = s.shift[i] > 0 ? s.base[i] + s.shift[i] : s.base[i];
+        if (tgt < 2 || src < 2) return false;
+    }
+    return true;
+}
+
+int64_t swizzle_host(const Swz& s, int64_t r) {
+    for (int i = 0; i < s.rank; ++i) {
+        const int64_t mask = (int64_t(1) << s.bits[i]) - 1;
+        if (s.shift[i] > 0) r ^= ((r >> (s.base[i] + s.shift[i])) & mask) << s.base[i];
+        else r ^= ((r >> s.base[i]) & mask) << (s.base[i] - s.shift[i]);
+    }
+    return r;
+}
+
+// Highest bit a swizzle may set.
+int swizzle_top_bit(const Swz& s) {
+    int top = -1;
+    for (int i = 0; i < s.rank; ++i) {
+        const int tgt = s.shift[i] > 0 ? s.base[i] : s.base[i] - s.shift[i];
+        top = std::max(top, tgt + s.bits[i] - 1);
+    }
+    return top;
+}
+
+template <class Op>
+int launch_for(int kernel, const float* x, const DevPlan& p, void* out, cudaStream_t stream, int splits) {
+    if (kernel == 0) {
+        const int64_t warps_needed = p.n_kept;
+        int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, int64_t(sm_count()) * 8);
+        reduce_rows_vec<Op><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(x, p, out);
+    } else if (kernel == 1) {
+        cudaLaunchConfig_t cfg = {};
+        const int64_t kept_vecs = p.n_kept / 4;
+        cfg.gridDim = dim3((unsigned)((kept_vecs + 31) / 32), (unsigned)splits, 1);
+        cfg.blockDim = dim3(kColsThreads, 1, 1);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = (unsigned)splits;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t err = cudaLaunchKernelEx(&cfg, reduce_cols_vec<Op>, x, p, out);
+        if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_vec launch");
+    } else {
+        int64_t blocks = std::min<int64_t>((p.n_kept + 7) / 8, int64_t(sm_count()) * 8);
+        reduce_gather<Op><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(x, p, out);
+    }
+    SW_LAUNCH_CHECK("reduction launch");
+    return SW_OK;
+}
+
+}  // namespace
+}  // namespace sw
+
+extern "C" int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
+                             void* out, void* stream) {
+    using namespace sw;
+    if (!plan || !out) return fail(SW_ERR_INVALID, "sw_reduce_f32: null plan or output");
+    if (plan->kind < SW_REDUCE_SUM || plan->kind > SW_REDUCE_ARGMAX)
+        return fail(SW_ERR_INVALID, "sw_reduce_f32: unknown reduction kind %d", plan->kind);
+    if (plan->kept_rank < 0 || plan->kept_rank > SW_MAX_LEAVES || plan->reduced_rank < 0 ||
+        plan->reduced_rank > SW_MAX_LEAVES || plan->swizzle_rank < 0 || plan->swizzle_rank > SW_MAX_SWIZZLE)
+        return fail(SW_ERR_INVALID, "sw_reduce_f32: leaf or swizzle rank out of range");
+    DevPlan p;
+    std::memset(&p, 0, sizeof(p));
+    p.offset = plan->offset;
+    p.x_size = x_size;
+    for (int l = 0; l < plan->kept_rank; ++l)
+        if (plan->kept_shape[l] < 0) return fail(SW_ERR_INVALID, "sw_reduce_f32: negative extent");
+    for (int l = 0; l < plan->reduced_rank; ++l)
+        if (plan->reduced_shape[l] < 0) return fail(SW_ERR_INVALID, "sw_reduce_f32: negative extent");
+    lower_leaves(plan->kept_rank, plan->kept_shape, plan->kept_stride, p.kept, p.n_kept);
+    lower_leaves(plan->reduced_rank, plan->reduced_shape, plan->reduced_stride, p.red, p.n_red);
+    p.swz.rank = plan->swizzle_rank;
+    for (int i = 0; i < plan->swizzle_rank; ++i) {
+        p.swz.bits[i] = plan->swizzle_bits[i];
+        p.swz.base[i] = plan->swizzle_base[i];
+        p.swz.shift[i] = plan->swizzle_shift[i];
+        if (p.swz.bits[i] < 0 || p.swz.base[i] < 0 || p.swz.shift[i] == 0 ||
+            p.swz.base[i] - p.swz.shift[i] < 0 || p.swz.bits[i] + p.swz.base[i] + std::abs(p.swz.shift[i]) > 62)
+            return fail(SW_ERR_INVALID, "sw_reduce_f32: invalid swizzle stage %d", i);
+    }
+    if (p.n_kept == 0) return ok();
+    if (p.n_red == 0) {
+        if (plan->kind != SW_REDUCE_SUM) return fail(SW_ERR_INVALID, "reduction fibers must be non-empty");
+        SW_CUDA_TRY(cudaMemsetAsync(out, 0, size_t(p.n_kept) * 4, (cudaStream_t)stream), "zero sum");
+        return ok();
+    }
+    if (!x) return fail(SW_ERR_INVALID, "sw_reduce_f32: null input");
+    // Address range of the view (before the swizzle).
+    int64_t lo = p.offset, hi = p.offset;
+    for (int l = 0; l < p.kept.rank; ++l) {
+        const int64_t span = (p.kept.shape[l] - 1) * p.kept.stride[l];
+        if (span < 0) lo += span; else hi += span;
+    }
+    for (int l = 0; l < p.red.rank; ++l) {
+        const int64_t span = (p.red.shape[l] - 1) * p.red.stride[l];
+        if (span < 0) lo += span; else hi += span;
+    }
+    if (lo < 0 || hi >= x_size)
+        return fail(SW_ERR_INVALID, "sw_reduce_f32: view addresses [%lld, %lld] outside carrier of %lld elements",
+                    (long long)lo, (long long)hi, (long long)x_size);
+    if (p.swz.rank > 0) {
+        // The swizzle only rewrites bits up to `top`: every address stays in the
+        // enclosing aligned 2^(top+1) window, which must lie inside the carrier.
+        const int top = swizzle_top_bit(p.swz);
+        const int64_t win = int64_t(1) << (top + 1);
+        const int64_t hi_window = (hi / win + 1) * win - 1;
+        if (hi_window >= x_size)
+            return fail(SW_ERR_INVALID, "sw_reduce_f32: swizzle may address past the carrier end");
+    }
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (p.offset % 4 == 0) &&
+                         swizzle_keeps_vec4(p.swz);
+    int kernel = 2;
+    int splits = 1;
+    const int ru = unit_leaf(p.red);
+    const int ku = unit_leaf(p.kept);
+    if (aligned && ru >= 0 && strides_mult4(p.red, ru) && strides_mult4(p.kept, -1)) {
+        leaf_to_front(p.red, ru);
+        kernel = 0;
+    } else if (aligned && ku == 0 && p.n_kept % 4 == 0 && strides_mult4(p.kept, 0) &&
+               strides_mult4(p.red, -1)) {
+        kernel = 1;
+        // Enough CTAs to fill every SM about four times over; at most 8 per
+        // cluster (the portable cluster size) and never more than the fibre.
+        const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
+        const int64_t want = (int64_t(sm_count()) * 4 + col_blocks - 1) / col_blocks;
+        splits = (int)std::max<int64_t>(1, std::min<int64_t>({want, 8, p.n_red}));
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc;
+    switch (plan->kind) {
+        case SW_REDUCE_SUM: rc = launch_for<SumOp>(kernel, x, p, out, s, splits); break;
+        case SW_REDUCE_MAX: rc = launch_for<MaxOp>(kernel, x, p, out, s, splits); break;
+        default: rc = launch_for<ArgmaxOp>(kernel, x, p, out, s, splits); break;
+    }
+    if (rc != SW_OK) return rc;
+    return ok();
+}

@@ -1,0 +1,160 @@
+// sw_runtime.cu - device storage, copies, streams and the status plumbing of
+// the C ABI (include/strideweave_b200.h).
+#include <cstring>
+
+#include "sw_common.cuh"
+
+namespace sw {
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+__device__ int g_device_error = 0;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int ok() {
+    t_last_error.clear();
+    return SW_OK;
+}
+
+}  // namespace sw
+
+using sw::fail;
+using sw::ok;
+
+extern "C" {
+
+const char* sw_last_error(void) { return sw::t_last_error.c_str(); }
+
+int sw_abi_version(void) { return 1; }
+
+int sw_device_count(int* count) {
+    if (!count) return fail(SW_ERR_INVALID, "sw_device_count: null output");
+    *count = 0;
+    cudaError_t err = cudaGetDeviceCount(count);
+    if (err == cudaErrorNoDevice || err == cudaErrorInsufficientDriver) {
+        cudaGetLastError();
+        *count = 0;
+        return ok();
+    }
+    SW_CUDA_TRY(err, "cudaGetDeviceCount");
+    return ok();
+}
+
+int sw_set_device(int device) {
+    SW_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+    return ok();
+}
+
+int sw_get_device(int* device) {
+    if (!device) return fail(SW_ERR_INVALID, "sw_get_device: null output");
+    SW_CUDA_TRY(cudaGetDevice(device), "cudaGetDevice");
+    return ok();
+}
+
+int sw_alloc(void** ptr, int64_t bytes) {
+    if (!ptr) return fail(SW_ERR_INVALID, "sw_alloc: null output");
+    *ptr = nullptr;
+    if (bytes < 0) return fail(SW_ERR_INVALID, "sw_alloc: negative size %lld", (long long)bytes);
+    if (bytes == 0) return ok();
+    cudaError_t err = cudaMalloc(ptr, (size_t)bytes);
+    if (err == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return fail(SW_ERR_NOMEM, "sw_alloc: out of device memory (%lld bytes)", (long long)bytes);
+    }
+    SW_CUDA_TRY(err, "cudaMalloc");
+    return ok();
+}
+
+int sw_free(void* ptr) {
+    if (!ptr) return ok();
+    SW_CUDA_TRY(cudaFree(ptr), "cudaFree");
+    return ok();
+}
+
+static int copy(void* dst, const void* src, int64_t bytes, cudaMemcpyKind kind,
+                void* stream, const char* what) {
+    if (bytes < 0) return fail(SW_ERR_INVALID, "%s: negative size", what);
+    if (bytes == 0) return ok();
+    if (!dst || !src) return fail(SW_ERR_INVALID, "%s: null pointer", what);
+    SW_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)bytes, kind, (cudaStream_t)stream), what);
+    return ok();
+}
+
+int sw_memcpy_h2d(void* dst, const void* src, int64_t bytes, void* stream) {
+    return copy(dst, src, bytes, cudaMemcpyHostToDevice, stream, "sw_memcpy_h2d");
+}
+
+int sw_memcpy_d2h(void* dst, const void* src, int64_t bytes, void* stream) {
+    int rc = copy(dst, src, bytes, cudaMemcpyDeviceToHost, stream, "sw_memcpy_d2h");
+    if (rc != SW_OK) return rc;
+    // A pageable destination is only valid once the copy has landed.
+    SW_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream), "sw_memcpy_d2h sync");
+    return ok();
+}
+
+int sw_memcpy_d2d(void* dst, const void* src, int64_t bytes, void* stream) {
+    return copy(dst, src, bytes, cudaMemcpyDeviceToDevice, stream, "sw_memcpy_d2d");
+}
+
+int sw_memset(void* dst, int value, int64_t bytes, void* stream) {
+    if (bytes < 0) return fail(SW_ERR_INVALID, "sw_memset: negative size");
+    if (bytes == 0) return ok();
+    SW_CUDA_TRY(cudaMemsetAsync(dst, value, (size_t)bytes, (cudaStream_t)stream), "cudaMemsetAsync");
+    return ok();
+}
+
+int sw_host_alloc(void** ptr, int64_t bytes) {
+    if (!ptr || bytes < 0) return fail(SW_ERR_INVALID, "sw_host_alloc: bad argument");
+    *ptr = nullptr;
+    if (bytes == 0) return ok();
+    SW_CUDA_TRY(cudaMallocHost(ptr, (size_t)bytes), "cudaMallocHost");
+    return ok();
+}
+
+int sw_host_free(void* ptr) {
+    if (!ptr) return ok();
+    SW_CUDA_TRY(cudaFreeHost(ptr), "cudaFreeHost");
+    return ok();
+}
+
+int sw_stream_create(void** stream) {
+    if (!stream) return fail(SW_ERR_INVALID, "sw_stream_create: null output");
+    cudaStream_t s;
+    SW_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+    *stream = (void*)s;
+    return ok();
+}
+
+int sw_stream_destroy(void* stream) {
+    if (!stream) return ok();
+    SW_CUDA_TRY(cudaStreamDestroy((cudaStream_t)stream), "cudaStreamDestroy");
+    return ok();
+}
+
+int sw_stream_synchronize(void* stream) {
+    SW_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream), "cudaStreamSynchronize");
+    return ok();
+}
+
+int sw_device_status(int* status) {
+    if (!status) return fail(SW_ERR_INVALID, "sw_device_status: null output");
+    SW_CUDA_TRY(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    int value = 0, zero = 0;
+    SW_CUDA_TRY(cudaMemcpyFromSymbol(&value, sw::g_device_error, sizeof(int)), "read device status");
+    SW_CUDA_TRY(cudaMemcpyToSymbol(sw::g_device_error, &zero, sizeof(int)), "clear device status");
+    *status = value;
+    return ok();
+}
+
+}  // extern "C"

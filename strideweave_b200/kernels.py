@@ -1,0 +1,106 @@
+"""Host wrappers of the C ABI kernels, on raw device addresses.
+
+These are the calls the CUDA carrier's operations make; they validate what
+Python can see cheaply, build the POD plan structs and raise the exception the
+library's status maps to.  Addresses are plain integers (``sw_alloc``
+results, or any CUDA device address); ``stream`` is a ``cudaStream_t`` value
+(0 = the legacy default stream).
+"""
+
+from __future__ import annotations
+
+from ctypes import byref, c_void_p
+from typing import Sequence
+
+from . import _native as N
+
+Leaf = tuple[int, int]  # (extent, stride)
+SwizzleStage = tuple[int, int, int]  # (bits, base, shift)
+
+REDUCE_KINDS = {"reduce_sum": N.SW_REDUCE_SUM, "reduce_max": N.SW_REDUCE_MAX, "argmax": N.SW_REDUCE_ARGMAX}
+
+
+def make_reduce_plan(kind: str, offset: int, kept: Sequence[Leaf], reduced: Sequence[Leaf],
+                     swizzle: Sequence[SwizzleStage] = ()) -> N.ReducePlan:
+    """Build an ``sw_reduce_plan`` from (extent, stride) leaves, first leaf fastest."""
+    if kind not in REDUCE_KINDS:
+        raise ValueError(f"unknown reduction {kind!r}")
+    if len(kept) > N.SW_MAX_LEAVES or len(reduced) > N.SW_MAX_LEAVES:
+        raise NotImplementedError(f"more than {N.SW_MAX_LEAVES} leaves in one mode")
+    if len(swizzle) > N.SW_MAX_SWIZZLE:
+        raise NotImplementedError(f"more than {N.SW_MAX_SWIZZLE} swizzle stages")
+    plan = N.ReducePlan()
+    plan.kind = REDUCE_KINDS[kind]
+    plan.kept_rank = len(kept)
+    plan.reduced_rank = len(reduced)
+    plan.swizzle_rank = len(swizzle)
+    plan.offset = int(offset)
+    for i, (extent, stride) in enumerate(kept):
+        plan.kept_shape[i] = int(extent)
+        plan.kept_stride[i] = int(stride)
+    for i, (extent, stride) in enumerate(reduced):
+        plan.reduced_shape[i] = int(extent)
+        plan.reduced_stride[i] = int(stride)
+    for i, (bits, base, shift) in enumerate(swizzle):
+        plan.swizzle_bits[i] = int(bits)
+        plan.swizzle_base[i] = int(base)
+        plan.swizzle_shift[i] = int(shift)
+    return plan
+
+
+def reduce_f32(kind: str, x_ptr: int, x_size: int, offset: int, kept: Sequence[Leaf], reduced: Sequence[Leaf],
+               out_ptr: int, *, swizzle: Sequence[SwizzleStage] = (), stream: int = 0) -> None:
+    """out[i] = reduction over the reduced leaves of kept ordinal i (see sw_reduce_f32)."""
+    plan = make_reduce_plan(kind, offset, kept, reduced, swizzle)
+    N.check(N.lib.sw_reduce_f32(byref(plan), c_void_p(x_ptr), int(x_size), c_void_p(out_ptr), c_void_p(stream)))
+
+
+def mx_format(name: str) -> int:
+    formats = {"E4M3": N.SW_MX_E4M3, "MXFP8_E4M3": N.SW_MX_E4M3, "E2M1": N.SW_MX_E2M1, "MXFP4": N.SW_MX_E2M1}
+    try:
+        return formats[name]
+    except KeyError:
+        raise NotImplementedError(f"MX format {name!r} has no kernel") from None
+
+
+def mx_row_bytes(fmt: int, cols: int) -> int:
+    return cols if fmt == N.SW_MX_E4M3 else (cols + 1) // 2
+
+
+def scale_bytes_tc128(rows: int, kblocks: int) -> int:
+    return int(N.lib.sw_mx_scale_bytes_tc128(int(rows), int(kblocks)))
+
+
+def scale_index_tc128(r: int, kb: int, kblocks: int) -> int:
+    return int(N.lib.sw_mx_scale_index(int(r), int(kb), int(kblocks)))
+
+
+def mx_quantize(fmt: int, x_ptr: int, rows: int, cols: int, ld_row: int, ld_col: int, payload_ptr: int,
+                ld_payload: int, scales_ptr: int, *, scale_layout: int = N.SW_SCALES_TC128, ld_scales: int = 0,
+                stream: int = 0) -> None:
+    N.check(N.lib.sw_mx_quantize(fmt, c_void_p(x_ptr), rows, cols, ld_row, ld_col, c_void_p(payload_ptr),
+                                 ld_payload, c_void_p(scales_ptr), scale_layout, ld_scales, c_void_p(stream)))
+
+
+def mx_dequantize(fmt: int, payload_ptr: int, ld_payload: int, scales_ptr: int, rows: int, cols: int, out_ptr: int,
+                  ld_out: int, *, scale_layout: int = N.SW_SCALES_TC128, ld_scales: int = 0,
+                  stream: int = 0) -> None:
+    N.check(N.lib.sw_mx_dequantize(fmt, c_void_p(payload_ptr), ld_payload, c_void_p(scales_ptr), scale_layout,
+                                   ld_scales, rows, cols, c_void_p(out_ptr), ld_out, c_void_p(stream)))
+
+
+def mx_gemm(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int, c_ptr: int,
+            M: int, N_: int, K: int, *, out_bf16: bool = False, ldc_m: int | None = None, ldc_n: int = 1,
+            beta_one: bool = False, stream: int = 0) -> None:
+    """C[m, n] = sum_k A[m, k] B[n, k] over MX operands (see sw_mx_gemm)."""
+    if ldc_m is None:
+        ldc_m = N_
+    N.check(N.lib.sw_mx_gemm(fmt, fmt, c_void_p(a_ptr), lda, c_void_p(sfa_ptr), c_void_p(b_ptr), ldb,
+                             c_void_p(sfb_ptr), c_void_p(c_ptr), N.SW_OUT_BF16 if out_bf16 else N.SW_OUT_F32,
+                             ldc_m, ldc_n, M, N_, K, int(beta_one), c_void_p(stream)))
+
+
+def matmul_f32(a_ptr: int, sam: int, sak: int, b_ptr: int, sbn: int, sbk: int, c_ptr: int, scm: int, scn: int,
+               M: int, N_: int, K: int, *, stream: int = 0) -> None:
+    N.check(N.lib.sw_matmul_f32(c_void_p(a_ptr), sam, sak, c_void_p(b_ptr), sbn, sbk, c_void_p(c_ptr), scm, scn,
+                                M, N_, K, c_void_p(stream)))

@@ -1,0 +1,88 @@
+"""The C ABI library loads and exports every symbol the header declares.
+
+No GPU is needed: only host-side entry points run here (argument validation
+that rejects before any CUDA call, and the scale-placement arithmetic).
+"""
+
+from __future__ import annotations
+
+import re
+from ctypes import c_void_p
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "strideweave_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^[A-Za-z_][\w\s\*]*?\b(sw_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def native():
+    from strideweave_b200 import build
+
+    build.build()
+    from strideweave_b200 import _native
+
+    return _native
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for required in ("sw_reduce_f32", "sw_mx_quantize", "sw_mx_dequantize", "sw_mx_gemm", "sw_alloc",
+                     "sw_last_error", "sw_matmul_f32"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(native):
+    names = declared_functions()
+    assert set(names) == set(native.SIGNATURES), "ctypes table and header disagree"
+    for name in names:
+        assert getattr(native.lib, name) is not None
+
+
+def test_abi_version(native):
+    assert native.lib.sw_abi_version() == 1
+
+
+def test_scale_placement_matches_the_oracle(native):
+    from oracle import oracle as O
+    from strideweave_b200 import kernels
+
+    for rows, kblocks in ((128, 4), (256, 8), (384, 32), (130, 5)):
+        assert kernels.scale_bytes_tc128(rows, kblocks) == O.scale_bytes_tc128(rows, kblocks)
+        for r in range(0, rows, 7):
+            for kb in range(kblocks):
+                assert kernels.scale_index_tc128(r, kb, kblocks) == O.scale_index_tc128(r, kb, kblocks)
+
+
+def test_invalid_arguments_are_rejected_before_any_device_work(native):
+    from strideweave_b200 import kernels
+
+    with pytest.raises(NotImplementedError, match="M % 128"):
+        kernels.mx_gemm(1, 16, 1024, 16, 16, 1024, 16, 16, 100, 128, 1024)
+    with pytest.raises(NotImplementedError, match="mixed operand formats"):
+        native.check(native.lib.sw_mx_gemm(1, 2, c_void_p(16), 1024, c_void_p(16), c_void_p(16), 1024,
+                                           c_void_p(16), c_void_p(16), 0, 128, 1, 128, 128, 1024, 0, None))
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        kernels.mx_gemm(1, 17, 1024, 16, 16, 1024, 16, 16, 128, 128, 1024)
+    with pytest.raises(ValueError, match="unknown format"):
+        kernels.mx_quantize(7, 16, 4, 32, 32, 1, 16, 32, 16)
+    with pytest.raises(ValueError, match="payload pitch"):
+        kernels.mx_quantize(1, 16, 4, 64, 64, 1, 16, 32, 16)
+    with pytest.raises(ValueError, match="unknown reduction kind"):
+        plan = kernels.make_reduce_plan("reduce_sum", 0, [(4, 1)], [(4, 4)])
+        plan.kind = 9
+        from ctypes import byref
+
+        native.check(native.lib.sw_reduce_f32(byref(plan), c_void_p(16), 16, c_void_p(16), None))
+    with pytest.raises(ValueError, match="outside carrier"):
+        kernels.reduce_f32("reduce_max", 16, 15, 0, [(4, 1)], [(4, 4)], 16)
+    with pytest.raises(ValueError, match="fibers must be non-empty"):
+        kernels.reduce_f32("argmax", 16, 16, 0, [(4, 1)], [(0, 4)], 16)
+    assert native.last_error() != ""
