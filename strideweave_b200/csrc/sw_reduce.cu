@@ -478,15 +478,6 @@ bool swizzle_keeps_vec4(const Swz& s) {
     return true;
 }
 
-int64_t swizzle_host(const Swz& s, int64_t r) {
-    for (int i = 0; i < s.rank; ++i) {
-        const int64_t mask = (int64_t(1) << s.bits[i]) - 1;
-        if (s.shift[i] > 0) r ^= ((r >> (s.base[i] + s.shift[i])) & mask) << s.base[i];
-        else r ^= ((r >> s.base[i]) & mask) << (s.base[i] - s.shift[i]);
-    }
-    return r;
-}
-
 // Highest bit a swizzle may set.
 int swizzle_top_bit(const Swz& s) {
     int top = -1;
@@ -554,8 +545,9 @@ extern "C" int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t
         p.swz.bits[i] = plan->swizzle_bits[i];
         p.swz.base[i] = plan->swizzle_base[i];
         p.swz.shift[i] = plan->swizzle_shift[i];
-        if (p.swz.bits[i] < 0 || p.swz.base[i] < 0 || p.swz.shift[i] == 0 ||
-            p.swz.base[i] - p.swz.shift[i] < 0 || p.swz.bits[i] + p.swz.base[i] + std::abs(p.swz.shift[i]) > 62)
+        // the constraints of SwizzleStage (src/strideweave/core/swizzle.py:44-60)
+        if (p.swz.bits[i] <= 0 || p.swz.base[i] < 0 || p.swz.shift[i] == 0 ||
+            std::abs(p.swz.shift[i]) < p.swz.bits[i] || p.swz.bits[i] + p.swz.base[i] + std::abs(p.swz.shift[i]) > 62)
             return fail(SW_ERR_INVALID, "sw_reduce_f32: invalid swizzle stage %d", i);
     }
     if (p.n_kept == 0) return ok();

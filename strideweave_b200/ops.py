@@ -1,0 +1,248 @@
+"""Operations the CUDA carrier dispatches.
+
+Each class is a ``strideweave`` ``Operation`` (the Python face of
+src/strideweave/core/native/_operation.hpp:44-242): ``_forward`` resolves the
+shared operation plan and the carrier's capability before allocating anything
+(the reference's CPP001 rule), lowers the operand layouts to flat leaf plans
+and enqueues one kernel through the C ABI; ``backward`` returns the gradients
+in the injective canonical layout of each input, as the CPU carrier does
+(src/strideweave/carriers/cpu/native/_cpu_carrier.hpp:711-717).
+
+Layout views (rearrange, permute, reshape, ...) are the reference's own
+zero-copy shared operations; the CUDA carrier returns fresh instances of them.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+from . import kernels
+from ._host import (
+    DType,
+    Operation,
+    Tensor,
+    UnsupportedOperationPlan,
+    require_capability,
+    resolve_operation_plan,
+)
+from .layout_plan import canonical_layout, injective_layout_for, mode_leaves, mode_size, single_stride, swizzle_stages
+
+
+def _cuda_tensor(value: Any, name: str) -> Tensor:
+    from .carrier import CUDA
+
+    if not isinstance(value, Tensor):
+        raise TypeError(f"{name} must be a Tensor")
+    value._require_single_subtensor("CUDA operation")
+    if not isinstance(value.carrier, CUDA):
+        raise TypeError(f"{name} must be backed by a CUDA carrier")
+    if value.carrier.is_released():
+        raise RuntimeError(f"{name} carrier is released")
+    return value
+
+
+def _two_mode(value: Any, name: str) -> Tensor:
+    t = _cuda_tensor(value, name)
+    if len(t.layout) != 2:
+        raise ValueError(f"{name} must have a two-mode layout")
+    return t
+
+
+def _new_result(like: Any, layout: Any, dtype: Any, *, zero: bool = False) -> Tensor:
+    from .carrier import CUDA
+
+    carrier = CUDA(layout.cosize, dtype=dtype, empty=not zero, device=like.carrier.device)
+    return Tensor(carrier, 0, layout)
+
+
+class CudaOperation(Operation):
+    """Common base: the executing carrier class for plan checks."""
+
+    @staticmethod
+    def _carrier_class() -> type:
+        from .carrier import CUDA
+
+        return CUDA
+
+
+# ---- reductions -----------------------------------------------------------------
+
+
+class CudaReduction(CudaOperation):
+    """reduce_sum / reduce_max / argmax over mode 1 of a two-mode tensor.
+
+    Replaces CpuReduceSumOperation (src/strideweave/carriers/cpu/native/ops/
+    reduce_sum.cpp:30-118) and CpuFloatReductionOperation<Kind>
+    (src/strideweave/carriers/cpu/native/_cpu_reduction.hpp:47-196).
+    """
+
+    kind = ""
+
+    def _forward(self, tensor: Any) -> Tensor:
+        tensor = _two_mode(tensor, "tensor")
+        layout = tensor.layout
+        n = mode_size(layout, 0)
+        m = mode_size(layout, 1)
+        if m <= 0 and self.kind != "reduce_sum":
+            raise ValueError("reduction fibers must be non-empty")
+        output_layout = canonical_layout(layout.shape.top_level[0])
+        self.ctx["output_layout"] = output_layout
+        plan = resolve_operation_plan(self.kind, tensor.carrier.dtype(), options=self._execution_options)
+        require_capability(self._carrier_class(), plan)
+        result = _new_result(tensor, output_layout, plan.output)
+        if n:
+            kernels.reduce_f32(self.kind, tensor.carrier.data_ptr, tensor.carrier.size(), tensor.offset,
+                               mode_leaves(layout, 0), mode_leaves(layout, 1), result.carrier.data_ptr,
+                               swizzle=swizzle_stages(tensor.carrier))
+        return result
+
+    def backward(self, gradient: Any) -> tuple[Any, ...]:
+        if self.kind == "argmax":
+            return ()
+        (tensor,) = self.inputs()
+        gradient = _cuda_tensor(gradient, "gradient")
+        if gradient.layout != self.ctx["output_layout"]:
+            raise ValueError("Tensor layouts must match")
+        grad_layout = injective_layout_for(tensor.layout)
+        result = _new_result(tensor, grad_layout, DType.Float32)
+        kernels.reduce_backward_f32(
+            self.kind, tensor.carrier.data_ptr if self.kind == "reduce_max" else 0, tensor.carrier.size(),
+            tensor.offset, mode_leaves(tensor.layout, 0), mode_leaves(tensor.layout, 1),
+            swizzle_stages(tensor.carrier), gradient.carrier.data_ptr, result.carrier.data_ptr,
+            mode_leaves(grad_layout, 0), mode_leaves(grad_layout, 1))
+        return (result,)
+
+
+class CudaReduceSum(CudaReduction):
+    kind = "reduce_sum"
+
+
+class CudaReduceMax(CudaReduction):
+    kind = "reduce_max"
+
+
+class CudaArgmax(CudaReduction):
+    kind = "argmax"
+
+
+# ---- Float32 contraction ----------------------------------------------------------
+
+
+def _mode_single(t: Tensor, mode: int, name: str) -> tuple[int, int]:
+    s = single_stride(mode_leaves(t.layout, mode))
+    if s is None:
+        raise NotImplementedError(f"{name} mode {mode} does not walk memory with a single stride on the CUDA carrier")
+    if swizzle_stages(t.carrier):
+        raise NotImplementedError(f"{name}: swizzled carriers are not contracted by the CUDA carrier")
+    return s
+
+
+class CudaMatmul(CudaOperation):
+    """Float32 contraction out[i, j] = sum_k lhs[i, k] rhs[j, k].
+
+    Replaces CpuMatmulOperation (src/strideweave/carriers/cpu/native/ops/
+    matmul.cpp:45-191): the same BINARY32 / FLOATING / Float32 plan, the result
+    in the canonical column-major layout of (lhs mode 0, rhs mode 0).
+    """
+
+    def _forward(self, lhs: Any, rhs: Any) -> Tensor:
+        lhs = _two_mode(lhs, "lhs")
+        rhs = _two_mode(rhs, "rhs")
+        M, K = mode_size(lhs.layout, 0), mode_size(lhs.layout, 1)
+        Nn, K2 = mode_size(rhs.layout, 0), mode_size(rhs.layout, 1)
+        if K != K2:
+            raise ValueError("Matmul inner dimensions must match")
+        output_layout = canonical_layout(lhs.layout.shape.top_level[0], rhs.layout.shape.top_level[0])
+        self.ctx["output_layout"] = output_layout
+        plan = resolve_operation_plan("matmul", lhs.carrier.dtype(), rhs.carrier.dtype(),
+                                      options=self._execution_options)
+        require_capability(self._carrier_class(), plan)
+        (_, sam), (_, sak) = _mode_single(lhs, 0, "lhs"), _mode_single(lhs, 1, "lhs")
+        (_, sbn), (_, sbk) = _mode_single(rhs, 0, "rhs"), _mode_single(rhs, 1, "rhs")
+        result = _new_result(lhs, output_layout, DType.Float32)
+        a = lhs.carrier.data_ptr + 4 * lhs.offset
+        b = rhs.carrier.data_ptr + 4 * rhs.offset
+        kernels.matmul_f32(a, sam, sak, b, sbn, sbk, result.carrier.data_ptr, 1, M, M, Nn, K)
+        return result
+
+    def backward(self, gradient: Any) -> tuple[Any, Any]:
+        lhs, rhs = self.inputs()
+        gradient = _cuda_tensor(gradient, "gradient")
+        if gradient.layout != self.ctx["output_layout"]:
+            raise ValueError("Tensor layouts must match")
+        M, K = mode_size(lhs.layout, 0), mode_size(lhs.layout, 1)
+        Nn = mode_size(rhs.layout, 0)
+        (_, sam), (_, sak) = _mode_single(lhs, 0, "lhs"), _mode_single(lhs, 1, "lhs")
+        (_, sbn), (_, sbk) = _mode_single(rhs, 0, "rhs"), _mode_single(rhs, 1, "rhs")
+        g = gradient.carrier.data_ptr + 4 * gradient.offset
+        (_, sgm), (_, sgn) = _mode_single(gradient, 0, "gradient"), _mode_single(gradient, 1, "gradient")
+        a = lhs.carrier.data_ptr + 4 * lhs.offset
+        b = rhs.carrier.data_ptr + 4 * rhs.offset
+        dl_layout = injective_layout_for(lhs.layout)
+        dr_layout = injective_layout_for(rhs.layout)
+        dl = _new_result(lhs, dl_layout, DType.Float32)
+        dr = _new_result(rhs, dr_layout, DType.Float32)
+        (_, dlm), (_, dlk) = single_stride(mode_leaves(dl_layout, 0)), single_stride(mode_leaves(dl_layout, 1))
+        (_, drn), (_, drk) = single_stride(mode_leaves(dr_layout, 0)), single_stride(mode_leaves(dr_layout, 1))
+        # dlhs[m, k] = sum_n g[m, n] rhs[n, k]  (contract n: rhs viewed as [k, n])
+        kernels.matmul_f32(g, sgm, sgn, b, sbk, sbn, dl.carrier.data_ptr + 0, dlm, dlk, M, K, Nn)
+        # drhs[n, k] = sum_m g[m, n] lhs[m, k]
+        kernels.matmul_f32(g, sgn, sgm, a, sak, sam, dr.carrier.data_ptr + 0, drn, drk, Nn, K, M)
+        return (dl, dr)
+
+
+# ---- dispatch table ----------------------------------------------------------------
+
+
+def _shared(name: str) -> Any:
+    from strideweave.carriers import shared_ops
+    from strideweave.carriers.generic.as_strided_ops import GenericAsStridedOperation
+
+    table = {
+        "broadcast_to": shared_ops.BroadcastOperation,
+        "permute": shared_ops.PermuteOperation,
+        "rearrange": shared_ops.RearrangeOperation,
+        "reshape": shared_ops.ReshapeOperation,
+        "squeeze": shared_ops.SqueezeOperation,
+        "unsqueeze": shared_ops.UnsqueezeOperation,
+        "view": shared_ops.GenericViewOperation,
+        "as_strided": GenericAsStridedOperation,
+    }
+    return table.get(name)
+
+
+_OPS = {
+    "reduce_sum": CudaReduceSum,
+    "reduce_max": CudaReduceMax,
+    "argmax": CudaArgmax,
+    "matmul": CudaMatmul,
+}
+
+
+def make_operation(name: str) -> Any:
+    """A fresh operation instance for ``name`` (``Carrier._dispatch_op``)."""
+    if name in _OPS:
+        return _OPS[name]()
+    from .mx import MX_OPERATIONS
+
+    if name in MX_OPERATIONS:
+        return MX_OPERATIONS[name]()
+    shared = _shared(name)
+    if shared is not None:
+        return shared()
+    raise NotImplementedError(f"CUDA carrier does not support operation '{name}'")
+
+
+def declared_plans() -> list[Any]:
+    """The plan shapes this carrier executes (declared at import)."""
+    f32 = DType.Float32
+    return [
+        resolve_operation_plan("reduce_sum", f32),
+        resolve_operation_plan("reduce_max", f32),
+        resolve_operation_plan("argmax", f32),
+        resolve_operation_plan("matmul", f32, f32),
+    ]
+
+
+__all__ = ["CudaArgmax", "CudaMatmul", "CudaReduceMax", "CudaReduceSum", "UnsupportedOperationPlan",
+           "declared_plans", "make_operation"]
