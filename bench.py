@@ -247,7 +247,7 @@ def cpu_baseline_sample() -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
@@ -290,10 +290,17 @@ def main() -> None:
         kept, red, swz = plan_of(lay)
         kernels.reduce_f32(op, dev[lay].ptr, R * C, 0, kept, red, outs[(op, lay)].ptr, swizzle=swz, stream=s)
 
+    clocks = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
         for op, lay in order:
             launch(op, lay)
     torch.cuda.synchronize()
+    # keep the device busy ~1 s under the clock sampler before timing
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:
+        for op, lay in order:
+            launch(op, lay)
+        torch.cuda.synchronize()
 
     # -------- timed region: device-resident inputs --------
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in order]
@@ -302,15 +309,16 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for it in range(args.steps):
-            for i, (op, lay) in enumerate(order):
-                evs[it][i][0].record(stream)
-                launch(op, lay)
-                evs[it][i][1].record(stream)
-        end.record(stream)
-        torch.cuda.synchronize()
+    start.record(stream)
+    for it in range(args.steps):
+        for i, (op, lay) in enumerate(order):
+            evs[it][i][0].record(stream)
+            launch(op, lay)
+            evs[it][i][1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    time.sleep(0.25)
+    clocks.__exit__(None, None, None)
     if world > 1:
         dist.barrier()
     total_ms = start.elapsed_time(end)
@@ -391,7 +399,9 @@ def main() -> None:
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"], "traffic": None,
                          "per_layout_gbs": {lay: round(3 * RED_BYTES / (by_layout[lay] / 1e3) / 1e9, 1)
-                                            for lay in LAYOUTS}},
+                                            for lay in LAYOUTS},
+                         "per_kernel_gbs": {f"{op}/{lay}": round(RED_BYTES / (per_kernel[(op, lay)] / 1e3) / 1e9, 1)
+                                            for op, lay in order}},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 3 * X_BYTES,
                     "d2h_bytes_per_step": 9 * R * 4},
             "gpu_launches": 9 * args.steps,

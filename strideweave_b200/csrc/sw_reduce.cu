@@ -91,7 +91,10 @@ __device__ __forceinline__ int64_t kept_offset(const LeafSet& k, int64_t i) {
 
 // ---- reduction states ------------------------------------------------------
 
+enum class Kind { kSum, kMax, kArgmax };
+
 struct SumOp {
+    static constexpr Kind kKind = Kind::kSum;
     struct S { float v; };
     static __device__ __forceinline__ S identity() { return {0.0f}; }
     static __device__ __forceinline__ void add(S& s, float v, int64_t) { s.v += v; }
@@ -102,6 +105,7 @@ struct SumOp {
 };
 
 struct MaxOp {
+    static constexpr Kind kKind = Kind::kMax;
     struct S { float v; int64_t j; };  // j only orders NaNs
     static __device__ __forceinline__ S identity() { return {-INFINITY, INT64_MAX}; }
     static __device__ __forceinline__ void add(S& s, float v, int64_t j) { merge(s, S{v, j}); }
@@ -124,6 +128,7 @@ struct MaxOp {
 };
 
 struct ArgmaxOp {
+    static constexpr Kind kKind = Kind::kArgmax;
     struct S { float v; int64_t j; };
     static __device__ __forceinline__ S identity() { return {-INFINITY, INT64_MAX}; }
     static __device__ __forceinline__ void add(S& s, float v, int64_t j) { merge(s, S{v, j}); }
@@ -369,6 +374,246 @@ __global__ void __launch_bounds__(kColsThreads) reduce_cols_vec(const float* __r
     cluster.sync();  // peers keep their shared memory alive until rank 0 read it
 }
 
+// ---- affine walks -------------------------------------------------------------
+// When a lane's (or a thread's) share of a fibre is an arithmetic progression
+// of 16-byte vectors, step t reads start + t * delta.  When the carrier's
+// swizzle only rewrites bits below the lowest set bit of delta, the swizzle
+// commutes with the step and is applied once, to the start: the loop is a
+// pointer increment and a load.  The loop runs a cheap fold that is exact
+// whenever the lane saw only finite values (and, for max, a non-zero result);
+// otherwise the lane walks its share again with the exact merge.  Lanes then
+// combine with the exact merge, so results stay bit-exact.
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// Fast fold of four independent component streams, each visited in
+// increasing ordinal order.
+template <class Op, class Ord>
+struct FastFold {
+    float v[4];
+    Ord j[4];
+    float nanp;  // max.NaN of every value seen (argmax): NaN iff a NaN was seen
+    __device__ __forceinline__ void init(const float4& q, Ord ord, Ord w0) {
+        const float c[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            v[e] = c[e];
+            j[e] = ord + Ord(e) * w0;
+        }
+        nanp = max_nan(max_nan(c[0], c[1]), max_nan(c[2], c[3]));
+    }
+    __device__ __forceinline__ void step(const float4& q, Ord ord, Ord w0) {
+        const float c[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (Op::kKind == Kind::kSum) {
+                v[e] += c[e];
+            } else if (Op::kKind == Kind::kMax) {
+                v[e] = max_nan(v[e], c[e]);  // a NaN sticks and forces the exact walk
+            } else if (c[e] > v[e]) {
+                v[e] = c[e];
+                j[e] = ord + Ord(e) * w0;
+            }
+        }
+        if (Op::kKind == Kind::kArgmax) nanp = max_nan(nanp, max_nan(max_nan(c[0], c[1]), max_nan(c[2], c[3])));
+    }
+    __device__ __forceinline__ bool needs_exact() const {
+        if (Op::kKind == Kind::kSum) return false;
+        if (Op::kKind == Kind::kArgmax) return isnan(nanp);
+        bool bad = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) bad |= isnan(v[e]) || v[e] == 0.0f;
+        return bad;
+    }
+    __device__ __forceinline__ typename Op::S component(int e) const {
+        typename Op::S t;
+        if constexpr (Op::kKind == Kind::kSum) {
+            t.v = v[e];
+        } else {
+            t.v = v[e];
+            t.j = Op::kKind == Kind::kMax ? INT64_MAX : int64_t(j[e]);
+        }
+        return t;
+    }
+};
+
+template <bool kSwz>
+__device__ __forceinline__ int64_t phys(const Swz& s, int64_t f) {
+    if constexpr (kSwz) return swizzle(s, f);
+    else return f;
+}
+
+// A progression of `iters` vectors: flat offset off0 + t*doff, first component
+// ordinal ord0 + t*dord, components w0 ordinals apart.
+template <class Ord>
+struct LaneWalk {
+    int64_t off0, doff;
+    Ord ord0, dord, w0;
+    int iters;
+};
+
+// Exact fold of a progression (used when the fast fold cannot vouch).
+template <class Op, bool kSwz, class Ord>
+__device__ __forceinline__ void exact_walk(const float* __restrict__ x, const Swz& swz, int64_t base,
+                                        const LaneWalk<Ord>& w, typename Op::S (&acc)[4], bool columns) {
+    for (int t = 0; t < w.iters; ++t) {
+        const float4 q = load_stream4(x + phys<kSwz>(swz, base + w.off0 + int64_t(t) * w.doff));
+        const int64_t o = int64_t(w.ord0) + int64_t(t) * int64_t(w.dord);
+        const int64_t d = columns ? 0 : int64_t(w.w0);
+        Op::add(acc[0], q.x, o);
+        Op::add(acc[1], q.y, o + d);
+        Op::add(acc[2], q.z, o + 2 * d);
+        Op::add(acc[3], q.w, o + 3 * d);
+    }
+}
+
+// Fast fold of a progression whose physical addresses are affine (the
+// swizzle, if any, commutes with doff).  U loads in flight per batch.
+template <class Op, class Ord, int U>
+__device__ __forceinline__ bool fast_walk(const float* ptr, int64_t doff, int iters, Ord ord0, Ord dord, Ord w0,
+                                          FastFold<Op, Ord>& f) {
+    for (int t0 = 0; t0 < iters; t0 += U) {
+        float4 val[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (t0 + u < iters) val[u] = load_stream4(ptr + int64_t(t0 + u) * doff);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (t0 + u < iters) {
+                if (t0 + u == 0) f.init(val[u], ord0, w0);
+                else f.step(val[u], ord0 + Ord(t0 + u) * dord, w0);
+            }
+        }
+    }
+    return !f.needs_exact();
+}
+
+// Row walk shared by all lanes: the reduced mode is a unit-stride run of
+// `run` elements (run % 4 == 0) repeated `nruns` times at stride `rstride`
+// (ordinal weight `rweight`); leaf ordinal weight of the run is `w0`.
+struct RowWalk {
+    int64_t run, nruns, rstride, rweight, w0;
+};
+
+constexpr int kRowsAffThreads = 256;
+constexpr int kRowsAffWarps = kRowsAffThreads / 32;
+
+// One warp reduces whole rows: warp w owns the contiguous kept ordinals
+// [w * rpw, (w + 1) * rpw).  The host sizes the grid so that every warp is
+// resident at once and all carry the same number of rows: no tail wave.
+template <class Op, bool kSwz, class Ord>
+__global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const float* __restrict__ x, DevPlan p,
+                                                                         RowWalk rw, int64_t rpw, void* out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nv0 = rw.run >> 2;
+    LaneWalk<Ord> w;
+    w.w0 = Ord(rw.w0);
+    if (nv0 >= 32) {  // one run, 32 vectors per step
+        w.off0 = int64_t(lane) * 4;
+        w.ord0 = Ord(lane * 4) * w.w0;
+        w.doff = 128;
+        w.dord = Ord(128) * w.w0;
+        w.iters = int(nv0 / 32);
+    } else {  // 32 / nv0 runs per step
+        const int64_t per = 32 / nv0;
+        w.off0 = (lane % nv0) * 4 + (lane / nv0) * rw.rstride;
+        w.ord0 = Ord((lane % nv0) * 4 * rw.w0 + (lane / nv0) * rw.rweight);
+        w.doff = per * rw.rstride;
+        w.dord = Ord(per * rw.rweight);
+        w.iters = int(rw.nruns / per);
+    }
+    const int64_t r0 = warp * rpw;
+    const int64_t r1 = min(p.n_kept, r0 + rpw);
+    for (int64_t i = r0; i < r1; ++i) {
+        const int64_t row = p.offset + kept_offset(p.kept, i);
+        typename Op::S r = Op::identity();
+        FastFold<Op, Ord> f;
+        const float* ptr = x + phys<kSwz>(p.swz, row + w.off0);
+        if (fast_walk<Op, Ord, 4>(ptr, w.doff, w.iters, w.ord0, w.dord, w.w0, f)) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) Op::merge(r, f.component(e));
+        } else {
+            typename Op::S acc[4] = {Op::identity(), Op::identity(), Op::identity(), Op::identity()};
+            exact_walk<Op, kSwz, Ord>(x, p.swz, row, w, acc, false);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) Op::merge(r, acc[e]);
+        }
+        r = warp_reduce<Op>(r);
+        if (lane == 0) store_result<Op>(out, i, r);
+    }
+}
+
+// Column walk: kept leaf 0 is unit-stride; the reduced mode is one leaf
+// (extent n_red, stride `stride`, ordinal weight `weight`).  A CTA owns 128
+// kept ordinals (32 lanes x 4); its warps and the CTAs of its cluster split
+// the fibre, and the partials meet in distributed shared memory.
+constexpr int kColsAffThreads = 256;
+constexpr int kColsAffWarps = kColsAffThreads / 32;
+
+template <class Op, bool kSwz, class Ord>
+__global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const float* __restrict__ x, DevPlan p,
+                                                                         int64_t stride, int64_t weight, void* out) {
+    __shared__ typename Op::S part[kColsAffWarps][32][4];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int splits = (int)cluster.num_blocks();
+    const int split = (int)cluster.block_rank();
+    const int64_t kv = int64_t(blockIdx.x) * 32 + lane;
+    const bool live_col = kv < (p.n_kept >> 2);
+    const int64_t col = live_col ? p.offset + kept_offset(p.kept, kv * 4) : 0;
+    const int64_t per = (p.n_red + splits - 1) / splits;
+    const int64_t j0 = per * split + warp;
+    const int64_t j1 = min(p.n_red, per * (split + 1));
+    typename Op::S acc[4] = {Op::identity(), Op::identity(), Op::identity(), Op::identity()};
+    if (live_col && j0 < j1) {
+        LaneWalk<Ord> w;
+        w.off0 = j0 * stride;
+        w.doff = int64_t(kColsAffWarps) * stride;
+        w.ord0 = Ord(j0 * weight);
+        w.dord = Ord(kColsAffWarps * weight);
+        w.w0 = 0;  // the four components are four columns at the same ordinal
+        w.iters = int((j1 - j0 + kColsAffWarps - 1) / kColsAffWarps);
+        FastFold<Op, Ord> f;
+        const float* ptr = x + phys<kSwz>(p.swz, col + w.off0);
+        if (fast_walk<Op, Ord, 8>(ptr, w.doff, w.iters, w.ord0, w.dord, Ord(0), f)) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] = f.component(e);
+        } else {
+            exact_walk<Op, kSwz, Ord>(x, p.swz, col, w, acc, true);
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) part[warp][lane][e] = acc[e];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            typename Op::S s = part[0][lane][e];
+            for (int w = 1; w < kColsAffWarps; ++w) Op::merge(s, part[w][lane][e]);
+            part[0][lane][e] = s;
+        }
+    }
+    cluster.sync();
+    if (split == 0 && warp == 0 && live_col) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            typename Op::S s = part[0][lane][e];
+            for (int r = 1; r < splits; ++r) {
+                typename Op::S(*peer)[32][4] = cluster.map_shared_rank(part, r);
+                Op::merge(s, peer[0][lane][e]);
+            }
+            store_result<Op>(out, kv * 4 + e, s);
+        }
+    }
+    cluster.sync();
+}
+
 // ---- gather ------------------------------------------------------------------
 template <class Op>
 __global__ void __launch_bounds__(256) reduce_gather(const float* __restrict__ x, DevPlan p, void* out) {
@@ -478,6 +723,22 @@ bool swizzle_keeps_vec4(const Swz& s) {
     return true;
 }
 
+// Whether swizzle(f + k*step) == swizzle(f) + k*step for all f, k: true when
+// every bit a stage reads or writes lies below the lowest set bit of step.
+bool swizzle_commutes(const Swz& s, int64_t step) {
+    if (s.rank == 0) return true;
+    if (step == 0) return false;
+    int64_t a = step < 0 ? -step : step;
+    int low = 0;
+    while (((a >> low) & 1) == 0) ++low;
+    for (int i = 0; i < s.rank; ++i) {
+        const int tgt = s.shift[i] > 0 ? s.base[i] : s.base[i] - s.shift[i];
+        const int src = s.shift[i] > 0 ? s.base[i] + s.shift[i] : s.base[i];
+        if (std::max(tgt, src) + s.bits[i] - 1 >= low) return false;
+    }
+    return true;
+}
+
 // Highest bit a swizzle may set.
 int swizzle_top_bit(const Swz& s) {
     int top = -1;
@@ -488,23 +749,74 @@ int swizzle_top_bit(const Swz& s) {
     return top;
 }
 
+struct Launch {
+    int kernel = 2;  // 0 rows_vec, 1 cols_vec, 2 gather, 3 rows_affine, 4 cols_affine
+    int splits = 1;
+    int wpr = 1;     // warps per row of rows_affine
+    RowWalk rw{};
+    int64_t cstride = 0, cweight = 0;
+};
+
+template <class Op, bool kSwz, class Ord>
+int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
+    if (L.kernel == 3) {
+        // every warp resident at once, each with the same number of rows
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reduce_rows_affine<Op, kSwz, Ord>,
+                                                          kRowsAffThreads, 0) != cudaSuccess || per_sm < 1) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        const int64_t capacity = int64_t(sm_count()) * per_sm * kRowsAffWarps;
+        const int64_t rpw = (p.n_kept + capacity - 1) / capacity;
+        const int64_t warps = (p.n_kept + rpw - 1) / rpw;
+        const int64_t blocks = (warps + kRowsAffWarps - 1) / kRowsAffWarps;
+        reduce_rows_affine<Op, kSwz, Ord><<<(unsigned)blocks, kRowsAffThreads, 0, stream>>>(x, p, L.rw, rpw, out);
+        return SW_OK;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((p.n_kept / 4 + 31) / 32), (unsigned)L.splits, 1);
+    cfg.blockDim = dim3(kColsAffThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)L.splits;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, reduce_cols_affine<Op, kSwz, Ord>, x, p, L.cstride, L.cweight, out);
+    if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_affine launch");
+    return SW_OK;
+}
+
+template <class Op, class Ord>
+int launch_affine_swz(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
+    return p.swz.rank > 0 ? launch_affine<Op, true, Ord>(x, p, L, out, stream)
+                          : launch_affine<Op, false, Ord>(x, p, L, out, stream);
+}
+
 template <class Op>
-int launch_for(int kernel, const float* x, const DevPlan& p, void* out, cudaStream_t stream, int splits) {
-    if (kernel == 0) {
-        const int64_t warps_needed = p.n_kept;
-        int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, int64_t(sm_count()) * 8);
+int launch_for(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
+    if (L.kernel == 3 || L.kernel == 4) {
+        // 32-bit ordinals whenever every ordinal of the fibre fits
+        int rc = p.n_red < (int64_t(1) << 30) ? launch_affine_swz<Op, int32_t>(x, p, L, out, stream)
+                                              : launch_affine_swz<Op, int64_t>(x, p, L, out, stream);
+        if (rc != SW_OK) return rc;
+    } else if (L.kernel == 0) {
+        const int64_t blocks = std::min<int64_t>((p.n_kept + 7) / 8, int64_t(sm_count()) * 8);
         reduce_rows_vec<Op><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(x, p, out);
-    } else if (kernel == 1) {
+    } else if (L.kernel == 1) {
         cudaLaunchConfig_t cfg = {};
         const int64_t kept_vecs = p.n_kept / 4;
-        cfg.gridDim = dim3((unsigned)((kept_vecs + 31) / 32), (unsigned)splits, 1);
+        cfg.gridDim = dim3((unsigned)((kept_vecs + 31) / 32), (unsigned)L.splits, 1);
         cfg.blockDim = dim3(kColsThreads, 1, 1);
         cfg.dynamicSmemBytes = 0;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = (unsigned)splits;
+        attr[0].val.clusterDim.y = (unsigned)L.splits;
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
@@ -516,6 +828,58 @@ int launch_for(int kernel, const float* x, const DevPlan& p, void* out, cudaStre
     }
     SW_LAUNCH_CHECK("reduction launch");
     return SW_OK;
+}
+
+// Chooses the kernel for a lowered plan (see the file header).
+Launch choose(DevPlan& p, int kind, bool aligned) {
+    Launch L;
+    const int ru = unit_leaf(p.red);
+    const int ku = unit_leaf(p.kept);
+    if (aligned && ru >= 0 && strides_mult4(p.red, ru) && strides_mult4(p.kept, -1)) {
+        // rows: try the affine walk first
+        const int64_t run = p.red.shape[ru];
+        const int64_t nv0 = run / 4;
+        const int others = p.red.rank - 1;
+        int ol = -1;
+        for (int l = 0; l < p.red.rank; ++l)
+            if (l != ru) ol = l;
+        bool affine = false;
+        RowWalk rw{run, 1, 0, 0, p.red.weight[ru]};
+        if (others == 0 && nv0 % 32 == 0) {
+            affine = true;
+        } else if (others == 1 && 32 % nv0 == 0 && p.red.shape[ol] % (32 / nv0) == 0) {
+            rw.nruns = p.red.shape[ol];
+            rw.rstride = p.red.stride[ol];
+            rw.rweight = p.red.weight[ol];
+            // argmax folds each lane in increasing ordinal order
+            affine = kind != SW_REDUCE_ARGMAX || rw.rweight >= run * rw.w0;
+        }
+        // the lane step must commute with the swizzle
+        const int64_t step = nv0 >= 32 ? 128 : (32 / nv0) * rw.rstride;
+        if (affine && swizzle_commutes(p.swz, step)) {
+            L.kernel = 3;
+            L.rw = rw;
+            return L;
+        }
+        leaf_to_front(p.red, ru);
+        L.kernel = 0;
+        return L;
+    }
+    if (aligned && ku == 0 && p.n_kept % 4 == 0 && strides_mult4(p.kept, 0) && strides_mult4(p.red, -1)) {
+        const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
+        // every CTA resident at once (4 per SM): no second, partial wave
+        const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * 4 / col_blocks);
+        L.splits = (int)std::max<int64_t>(1, std::min<int64_t>({want, 8, p.n_red}));
+        if (p.red.rank == 1 && swizzle_commutes(p.swz, int64_t(kColsAffWarps) * p.red.stride[0])) {
+            L.kernel = 4;
+            L.cstride = p.red.stride[0];
+            L.cweight = p.red.weight[0];
+        } else {
+            L.kernel = 1;
+        }
+        return L;
+    }
+    return L;
 }
 
 }  // namespace
@@ -581,28 +945,13 @@ extern "C" int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t
     }
     const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (p.offset % 4 == 0) &&
                          swizzle_keeps_vec4(p.swz);
-    int kernel = 2;
-    int splits = 1;
-    const int ru = unit_leaf(p.red);
-    const int ku = unit_leaf(p.kept);
-    if (aligned && ru >= 0 && strides_mult4(p.red, ru) && strides_mult4(p.kept, -1)) {
-        leaf_to_front(p.red, ru);
-        kernel = 0;
-    } else if (aligned && ku == 0 && p.n_kept % 4 == 0 && strides_mult4(p.kept, 0) &&
-               strides_mult4(p.red, -1)) {
-        kernel = 1;
-        // Enough CTAs to fill every SM about four times over; at most 8 per
-        // cluster (the portable cluster size) and never more than the fibre.
-        const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
-        const int64_t want = (int64_t(sm_count()) * 4 + col_blocks - 1) / col_blocks;
-        splits = (int)std::max<int64_t>(1, std::min<int64_t>({want, 8, p.n_red}));
-    }
+    const Launch L = choose(p, plan->kind, aligned);
     cudaStream_t s = (cudaStream_t)stream;
     int rc;
     switch (plan->kind) {
-        case SW_REDUCE_SUM: rc = launch_for<SumOp>(kernel, x, p, out, s, splits); break;
-        case SW_REDUCE_MAX: rc = launch_for<MaxOp>(kernel, x, p, out, s, splits); break;
-        default: rc = launch_for<ArgmaxOp>(kernel, x, p, out, s, splits); break;
+        case SW_REDUCE_SUM: rc = launch_for<SumOp>(x, p, L, out, s); break;
+        case SW_REDUCE_MAX: rc = launch_for<MaxOp>(x, p, L, out, s); break;
+        default: rc = launch_for<ArgmaxOp>(x, p, L, out, s); break;
     }
     if (rc != SW_OK) return rc;
     return ok();
