@@ -116,6 +116,33 @@ typedef struct sw_reduce_plan {
 int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
                   void* out, void* stream);
 
+/* Gradient of sw_reduce_f32 with respect to its input (the VJP of
+ * CpuReduceSumOperation::backward, ops/reduce_sum.cpp:120-150, and of
+ * CpuFloatReductionOperation<Kind>::backward for reduce_max,
+ * _cpu_reduction.hpp:135-196):
+ *   SUM: grad_in[i, j] = grad_out[i] for every j;
+ *   MAX: grad_in[i, j] = grad_out[i] / w_i where x[i, j] equals the row's
+ *        maximum (w_i = how many do), 0 elsewhere; every element of a row
+ *        whose maximum is NaN gets NaN.
+ * `plan` describes the forward input view x (`x` may be NULL for SUM);
+ * `grad_plan` has the same leaf extents and places grad_in (kind ignored).
+ * grad_out holds one float per kept ordinal (the canonical result layout). */
+int sw_reduce_backward_f32(const sw_reduce_plan* plan, const float* x,
+                           int64_t x_size, const float* grad_out,
+                           float* grad_in, const sw_reduce_plan* grad_plan,
+                           int64_t grad_size, void* stream);
+
+/* Copies a two-mode Float32 view into another two-mode placement:
+ * dst[dst.offset + kept_d(i) + reduced_d(j)] = src at (i, j) of `src_plan`
+ * (through its swizzle), for every (i, j).  Both plans' leaves must have the
+ * same mode sizes; `kind` fields are ignored.  This is how the carrier
+ * materialises views no kernel walks directly (the reference's
+ * _physical_values_for_layout / _detached_tensor_like,
+ * src/strideweave/carriers/operation_helpers.py:194-245). */
+int sw_copy_view_f32(const sw_reduce_plan* src_plan, const float* src,
+                     int64_t src_size, const sw_reduce_plan* dst_plan,
+                     float* dst, int64_t dst_size, void* stream);
+
 /* ---- MX (OCP Microscaling v1.0) quantise / dequantise ------------------- */
 
 #define SW_MX_E4M3 1 /* MXFP8_E4M3: 1 byte per element              */

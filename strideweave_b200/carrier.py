@@ -396,3 +396,17 @@ class CUDA(Carrier):
     def __repr__(self) -> str:
         extra = f", swizzle={self._swizzle!r}" if self._swizzle is not None else ""
         return f"CUDA(size={self._size}, dtype={self._dtype.name}, device={self._device}{extra})"
+
+
+def _declare_capabilities() -> None:
+    """Declare, at import, the exact plan shapes the CUDA carrier executes
+    (register_operation_capabilities, src/strideweave/carriers/
+    operation_capability.py:567-655): Float32 reduce_sum / reduce_max / argmax
+    and the Float32 matmul plan."""
+    from ._host import OperationCapability, register_operation_capabilities
+    from .ops import declared_plans
+
+    register_operation_capabilities(CUDA, [OperationCapability.from_plan(p) for p in declared_plans()])
+
+
+_declare_capabilities()

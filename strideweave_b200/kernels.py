@@ -55,6 +55,28 @@ def reduce_f32(kind: str, x_ptr: int, x_size: int, offset: int, kept: Sequence[L
     N.check(N.lib.sw_reduce_f32(byref(plan), c_void_p(x_ptr), int(x_size), c_void_p(out_ptr), c_void_p(stream)))
 
 
+def reduce_backward_f32(kind: str, x_ptr: int, x_size: int, x_offset: int, kept: Sequence[Leaf],
+                        reduced: Sequence[Leaf], swizzle: Sequence[SwizzleStage], grad_out_ptr: int, grad_in_ptr: int,
+                        grad_kept: Sequence[Leaf], grad_reduced: Sequence[Leaf], grad_size: int,
+                        grad_offset: int = 0, *, stream: int = 0) -> None:
+    """grad_in = VJP of a reduce_sum / reduce_max (see sw_reduce_backward_f32)."""
+    plan = make_reduce_plan(kind, x_offset, kept, reduced, swizzle)
+    gplan = make_reduce_plan(kind, grad_offset, grad_kept, grad_reduced)
+    N.check(N.lib.sw_reduce_backward_f32(byref(plan), c_void_p(x_ptr or None), int(x_size), c_void_p(grad_out_ptr),
+                                         c_void_p(grad_in_ptr), byref(gplan), int(grad_size), c_void_p(stream)))
+
+
+def copy_view_f32(src_ptr: int, src_size: int, src_offset: int, src_kept: Sequence[Leaf],
+                  src_reduced: Sequence[Leaf], dst_ptr: int, dst_size: int, dst_offset: int,
+                  dst_kept: Sequence[Leaf], dst_reduced: Sequence[Leaf], *, swizzle: Sequence[SwizzleStage] = (),
+                  stream: int = 0) -> None:
+    """Copy a two-mode Float32 view into another placement (see sw_copy_view_f32)."""
+    sp = make_reduce_plan("reduce_sum", src_offset, src_kept, src_reduced, swizzle)
+    dp = make_reduce_plan("reduce_sum", dst_offset, dst_kept, dst_reduced)
+    N.check(N.lib.sw_copy_view_f32(byref(sp), c_void_p(src_ptr), int(src_size), byref(dp), c_void_p(dst_ptr),
+                                   int(dst_size), c_void_p(stream)))
+
+
 def mx_format(name: str) -> int:
     formats = {"E4M3": N.SW_MX_E4M3, "MXFP8_E4M3": N.SW_MX_E4M3, "E2M1": N.SW_MX_E2M1, "MXFP4": N.SW_MX_E2M1}
     try:

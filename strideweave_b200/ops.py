@@ -108,8 +108,9 @@ class CudaReduction(CudaOperation):
         kernels.reduce_backward_f32(
             self.kind, tensor.carrier.data_ptr if self.kind == "reduce_max" else 0, tensor.carrier.size(),
             tensor.offset, mode_leaves(tensor.layout, 0), mode_leaves(tensor.layout, 1),
-            swizzle_stages(tensor.carrier), gradient.carrier.data_ptr, result.carrier.data_ptr,
-            mode_leaves(grad_layout, 0), mode_leaves(grad_layout, 1))
+            swizzle_stages(tensor.carrier), gradient.carrier.data_ptr + 4 * gradient.offset,
+            result.carrier.data_ptr, mode_leaves(grad_layout, 0), mode_leaves(grad_layout, 1),
+            result.carrier.size())
         return (result,)
 
 
@@ -128,13 +129,47 @@ class CudaArgmax(CudaReduction):
 # ---- Float32 contraction ----------------------------------------------------------
 
 
-def _mode_single(t: Tensor, mode: int, name: str) -> tuple[int, int]:
-    s = single_stride(mode_leaves(t.layout, mode))
-    if s is None:
-        raise NotImplementedError(f"{name} mode {mode} does not walk memory with a single stride on the CUDA carrier")
-    if swizzle_stages(t.carrier):
-        raise NotImplementedError(f"{name}: swizzled carriers are not contracted by the CUDA carrier")
-    return s
+def _strided(t: Tensor) -> tuple[int, int, int, Any]:
+    """(address, stride of mode 0, stride of mode 1, keep-alive) of a Float32
+    CUDA matrix; views that do not walk memory with one stride per mode (or
+    that sit behind a swizzle) are first gathered into a row-major copy."""
+    from .carrier import CUDA
+
+    s0 = single_stride(mode_leaves(t.layout, 0))
+    s1 = single_stride(mode_leaves(t.layout, 1))
+    if s0 is not None and s1 is not None and not swizzle_stages(t.carrier):
+        return t.carrier.data_ptr + 4 * t.offset, s0[1], s1[1], None
+    n0, n1 = mode_size(t.layout, 0), mode_size(t.layout, 1)
+    tmp = CUDA(max(n0 * n1, 1), dtype=DType.Float32, empty=True, device=t.carrier.device)
+    kernels.copy_view_f32(t.carrier.data_ptr, t.carrier.size(), t.offset, mode_leaves(t.layout, 0),
+                          mode_leaves(t.layout, 1), tmp.data_ptr, tmp.size(), 0, [(n0, n1)], [(n1, 1)],
+                          swizzle=swizzle_stages(t.carrier))
+    return tmp.data_ptr, n1, 1, tmp
+
+
+def _output(layout: Any, like: Tensor) -> tuple[Tensor, int, int, Any]:
+    """A fresh Float32 result placed by `layout` and the (address, strides) a
+    kernel writes; hierarchical placements are written through a row-major
+    staging copy that `_finish` scatters."""
+    from .carrier import CUDA
+
+    result = _new_result(like, layout, DType.Float32)
+    s0 = single_stride(mode_leaves(layout, 0))
+    s1 = single_stride(mode_leaves(layout, 1))
+    if s0 is not None and s1 is not None:
+        return result, result.carrier.data_ptr, s0[1], s1[1], None
+    n0, n1 = mode_size(layout, 0), mode_size(layout, 1)
+    tmp = CUDA(max(n0 * n1, 1), dtype=DType.Float32, empty=True, device=like.carrier.device)
+    return result, tmp.data_ptr, n1, 1, tmp
+
+
+def _finish(result: Tensor, staging: Any) -> Tensor:
+    if staging is not None:
+        lay = result.layout
+        n0, n1 = mode_size(lay, 0), mode_size(lay, 1)
+        kernels.copy_view_f32(staging.data_ptr, staging.size(), 0, [(n0, n1)], [(n1, 1)], result.carrier.data_ptr,
+                              result.carrier.size(), result.offset, mode_leaves(lay, 0), mode_leaves(lay, 1))
+    return result
 
 
 class CudaMatmul(CudaOperation):
@@ -148,6 +183,8 @@ class CudaMatmul(CudaOperation):
     def _forward(self, lhs: Any, rhs: Any) -> Tensor:
         lhs = _two_mode(lhs, "lhs")
         rhs = _two_mode(rhs, "rhs")
+        if type(lhs.carrier) is not type(rhs.carrier):
+            raise TypeError("Tensor backing carriers must match")
         M, K = mode_size(lhs.layout, 0), mode_size(lhs.layout, 1)
         Nn, K2 = mode_size(rhs.layout, 0), mode_size(rhs.layout, 1)
         if K != K2:
@@ -157,11 +194,9 @@ class CudaMatmul(CudaOperation):
         plan = resolve_operation_plan("matmul", lhs.carrier.dtype(), rhs.carrier.dtype(),
                                       options=self._execution_options)
         require_capability(self._carrier_class(), plan)
-        (_, sam), (_, sak) = _mode_single(lhs, 0, "lhs"), _mode_single(lhs, 1, "lhs")
-        (_, sbn), (_, sbk) = _mode_single(rhs, 0, "rhs"), _mode_single(rhs, 1, "rhs")
+        a, sam, sak, _ka = _strided(lhs)
+        b, sbn, sbk, _kb = _strided(rhs)
         result = _new_result(lhs, output_layout, DType.Float32)
-        a = lhs.carrier.data_ptr + 4 * lhs.offset
-        b = rhs.carrier.data_ptr + 4 * rhs.offset
         kernels.matmul_f32(a, sam, sak, b, sbn, sbk, result.carrier.data_ptr, 1, M, M, Nn, K)
         return result
 
@@ -172,23 +207,16 @@ class CudaMatmul(CudaOperation):
             raise ValueError("Tensor layouts must match")
         M, K = mode_size(lhs.layout, 0), mode_size(lhs.layout, 1)
         Nn = mode_size(rhs.layout, 0)
-        (_, sam), (_, sak) = _mode_single(lhs, 0, "lhs"), _mode_single(lhs, 1, "lhs")
-        (_, sbn), (_, sbk) = _mode_single(rhs, 0, "rhs"), _mode_single(rhs, 1, "rhs")
-        g = gradient.carrier.data_ptr + 4 * gradient.offset
-        (_, sgm), (_, sgn) = _mode_single(gradient, 0, "gradient"), _mode_single(gradient, 1, "gradient")
-        a = lhs.carrier.data_ptr + 4 * lhs.offset
-        b = rhs.carrier.data_ptr + 4 * rhs.offset
-        dl_layout = injective_layout_for(lhs.layout)
-        dr_layout = injective_layout_for(rhs.layout)
-        dl = _new_result(lhs, dl_layout, DType.Float32)
-        dr = _new_result(rhs, dr_layout, DType.Float32)
-        (_, dlm), (_, dlk) = single_stride(mode_leaves(dl_layout, 0)), single_stride(mode_leaves(dl_layout, 1))
-        (_, drn), (_, drk) = single_stride(mode_leaves(dr_layout, 0)), single_stride(mode_leaves(dr_layout, 1))
-        # dlhs[m, k] = sum_n g[m, n] rhs[n, k]  (contract n: rhs viewed as [k, n])
-        kernels.matmul_f32(g, sgm, sgn, b, sbk, sbn, dl.carrier.data_ptr + 0, dlm, dlk, M, K, Nn)
-        # drhs[n, k] = sum_m g[m, n] lhs[m, k]
-        kernels.matmul_f32(g, sgn, sgm, a, sak, sam, dr.carrier.data_ptr + 0, drn, drk, Nn, K, M)
-        return (dl, dr)
+        a, sam, sak, _ka = _strided(lhs)
+        b, sbn, sbk, _kb = _strided(rhs)
+        g, sgm, sgn, _kg = _strided(gradient)
+        dl, dlp, dlm, dlk, dls = _output(injective_layout_for(lhs.layout), lhs)
+        dr, drp, drn, drk, drs = _output(injective_layout_for(rhs.layout), rhs)
+        # dlhs[m, k] = sum_n g[m, n] rhs[n, k]  (rhs viewed as [k, n])
+        kernels.matmul_f32(g, sgm, sgn, b, sbk, sbn, dlp, dlm, dlk, M, K, Nn)
+        # drhs[n, k] = sum_m g[m, n] lhs[m, k]  (g viewed as [n, m], lhs as [k, m])
+        kernels.matmul_f32(g, sgn, sgm, a, sak, sam, drp, drn, drk, Nn, K, M)
+        return (_finish(dl, dls), _finish(dr, drs))
 
 
 # ---- dispatch table ----------------------------------------------------------------
