@@ -251,7 +251,15 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
+    ap.add_argument("--soak-seconds", type=float, default=1.0,
+                    help="untimed busy time under the clock sampler before the timed region")
+    ap.add_argument("--profile-case", choices=["reduce", "mxfp8", "mxfp4"],
+                    help="run a short, fixed sequence of launches for ncu and exit (no timing)")
+    ap.add_argument("--reps", type=int, default=2, help="rounds of launches of --profile-case")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case, args.reps)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
@@ -286,9 +294,18 @@ def main() -> None:
     # consecutive launches read different 128 MiB buffers (> L2)
     order = [(op, lay) for op in OPS for lay in LAYOUTS]
 
+    # plans are built once: the timed loop is one C call per launch, so the
+    # host stays ahead of the device
+    plans = {}
+    for op in OPS:
+        for lay in LAYOUTS:
+            kept, red, swz = plan_of(lay)
+            plans[(op, lay)] = kernels.make_reduce_plan(op, 0, kept, red, swz)
+    stream_arg = N.c_void_p(s)
+
     def launch(op, lay):
-        kept, red, swz = plan_of(lay)
-        kernels.reduce_f32(op, dev[lay].ptr, R * C, 0, kept, red, outs[(op, lay)].ptr, swizzle=swz, stream=s)
+        N.check(N.lib.sw_reduce_f32(N.ctypes.byref(plans[(op, lay)]), N.c_void_p(dev[lay].ptr), R * C,
+                                    N.c_void_p(outs[(op, lay)].ptr), stream_arg))
 
     clocks = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
@@ -297,7 +314,7 @@ def main() -> None:
     torch.cuda.synchronize()
     # keep the device busy ~1 s under the clock sampler before timing
     t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < 1.0:
+    while time.perf_counter() - t_soak < args.soak_seconds:
         for op, lay in order:
             launch(op, lay)
         torch.cuda.synchronize()
@@ -455,6 +472,52 @@ def bench_gemm(torch, N, kernels, s, stream) -> dict:
         del pa, pb, sa, sb, c
     N.raise_device_status()
     return out
+
+
+def profile_case(case: str, reps: int) -> None:
+    """A fixed, small sequence of launches for an ncu capture.
+
+    reduce: the three layouts of X[8192 x 4096] x (sum, max, argmax), `reps`
+    rounds (9 launches per round).  mxfp8 / mxfp4: quantise two 8192 x 8192
+    operands, then `reps` contractions at M = N = K = 8192 (bf16 C).
+    """
+    from strideweave_b200 import _native as N
+    from strideweave_b200 import kernels
+
+    N.set_device(0)
+    if case == "reduce":
+        x = np.random.default_rng(0).uniform(-1, 1, size=(R, C)).astype(np.float32)
+        bufs = {}
+        for lay in LAYOUTS:
+            bufs[lay] = N.DeviceBuffer(X_BYTES)
+            bufs[lay].upload(storage_of(lay, x))
+        out = N.DeviceBuffer(R * 4)
+        for _ in range(reps):
+            for lay in LAYOUTS:
+                for op in OPS:
+                    kept, red, swz = plan_of(lay)
+                    kernels.reduce_f32(op, bufs[lay].ptr, R * C, 0, kept, red, out.ptr, swizzle=swz)
+    else:
+        fmt = N.SW_MX_E4M3 if case == "mxfp8" else N.SW_MX_E2M1
+        M = Nn = K = 8192
+        rb = K if fmt == N.SW_MX_E4M3 else K // 2
+        rng = np.random.default_rng(0)
+        planes = []
+        for rows, sigma in ((M, 1.0), (Nn, 0.02)):
+            src = N.DeviceBuffer(rows * K * 4)
+            src.upload((rng.standard_normal((rows, K)) * sigma).astype(np.float32))
+            pay = N.DeviceBuffer(rows * rb)
+            sc = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, K // 32))
+            kernels.mx_quantize(fmt, src.ptr, rows, K, K, 1, pay.ptr, rb, sc.ptr)
+            N.synchronize()
+            src.free()
+            planes.append((pay, sc))
+        c = N.DeviceBuffer(M * Nn * 2)
+        for _ in range(reps):
+            kernels.mx_gemm(fmt, planes[0][0].ptr, rb, planes[0][1].ptr, planes[1][0].ptr, rb, planes[1][1].ptr,
+                            c.ptr, M, Nn, K, out_bf16=True)
+    N.raise_device_status()
+    print(f"profile case {case}: ok")
 
 
 if __name__ == "__main__":

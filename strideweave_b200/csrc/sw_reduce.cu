@@ -397,16 +397,18 @@ struct FastFold {
     float v[4];
     Ord j[4];
     float nanp;  // max.NaN of every value seen (argmax): NaN iff a NaN was seen
-    __device__ __forceinline__ void init(const float4& q, Ord ord, Ord w0) {
+    // j[e] holds the step index of the current winner; the ordinal is
+    // rebuilt once, in component().
+    __device__ __forceinline__ void init(const float4& q) {
         const float c[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             v[e] = c[e];
-            j[e] = ord + Ord(e) * w0;
+            j[e] = 0;
         }
         nanp = max_nan(max_nan(c[0], c[1]), max_nan(c[2], c[3]));
     }
-    __device__ __forceinline__ void step(const float4& q, Ord ord, Ord w0) {
+    __device__ __forceinline__ void step(const float4& q, int t) {
         const float c[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -416,7 +418,7 @@ struct FastFold {
                 v[e] = max_nan(v[e], c[e]);  // a NaN sticks and forces the exact walk
             } else if (c[e] > v[e]) {
                 v[e] = c[e];
-                j[e] = ord + Ord(e) * w0;
+                j[e] = Ord(t);
             }
         }
         if (Op::kKind == Kind::kArgmax) nanp = max_nan(nanp, max_nan(max_nan(c[0], c[1]), max_nan(c[2], c[3])));
@@ -429,13 +431,14 @@ struct FastFold {
         for (int e = 0; e < 4; ++e) bad |= isnan(v[e]) || v[e] == 0.0f;
         return bad;
     }
-    __device__ __forceinline__ typename Op::S component(int e) const {
+    __device__ __forceinline__ typename Op::S component(int e, Ord ord0, Ord dord, Ord w0) const {
         typename Op::S t;
         if constexpr (Op::kKind == Kind::kSum) {
             t.v = v[e];
         } else {
             t.v = v[e];
-            t.j = Op::kKind == Kind::kMax ? INT64_MAX : int64_t(j[e]);
+            t.j = Op::kKind == Kind::kMax ? INT64_MAX
+                                          : int64_t(ord0) + int64_t(j[e]) * int64_t(dord) + int64_t(e) * int64_t(w0);
         }
         return t;
     }
@@ -474,8 +477,7 @@ __device__ __forceinline__ void exact_walk(const float* __restrict__ x, const Sw
 // Fast fold of a progression whose physical addresses are affine (the
 // swizzle, if any, commutes with doff).  U loads in flight per batch.
 template <class Op, class Ord, int U>
-__device__ __forceinline__ bool fast_walk(const float* ptr, int64_t doff, int iters, Ord ord0, Ord dord, Ord w0,
-                                          FastFold<Op, Ord>& f) {
+__device__ __forceinline__ bool fast_walk(const float* ptr, int64_t doff, int iters, FastFold<Op, Ord>& f) {
     for (int t0 = 0; t0 < iters; t0 += U) {
         float4 val[U];
 #pragma unroll
@@ -484,8 +486,8 @@ __device__ __forceinline__ bool fast_walk(const float* ptr, int64_t doff, int it
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             if (t0 + u < iters) {
-                if (t0 + u == 0) f.init(val[u], ord0, w0);
-                else f.step(val[u], ord0 + Ord(t0 + u) * dord, w0);
+                if (t0 + u == 0) f.init(val[u]);
+                else f.step(val[u], t0 + u);
             }
         }
     }
@@ -534,9 +536,9 @@ __global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const f
         typename Op::S r = Op::identity();
         FastFold<Op, Ord> f;
         const float* ptr = x + phys<kSwz>(p.swz, row + w.off0);
-        if (fast_walk<Op, Ord, 4>(ptr, w.doff, w.iters, w.ord0, w.dord, w.w0, f)) {
+        if (fast_walk<Op, Ord, 4>(ptr, w.doff, w.iters, f)) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) Op::merge(r, f.component(e));
+            for (int e = 0; e < 4; ++e) Op::merge(r, f.component(e, w.ord0, w.dord, w.w0));
         } else {
             typename Op::S acc[4] = {Op::identity(), Op::identity(), Op::identity(), Op::identity()};
             exact_walk<Op, kSwz, Ord>(x, p.swz, row, w, acc, false);
@@ -581,9 +583,9 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
         w.iters = int((j1 - j0 + kColsAffWarps - 1) / kColsAffWarps);
         FastFold<Op, Ord> f;
         const float* ptr = x + phys<kSwz>(p.swz, col + w.off0);
-        if (fast_walk<Op, Ord, 8>(ptr, w.doff, w.iters, w.ord0, w.dord, Ord(0), f)) {
+        if (fast_walk<Op, Ord, 8>(ptr, w.doff, w.iters, f)) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[e] = f.component(e);
+            for (int e = 0; e < 4; ++e) acc[e] = f.component(e, w.ord0, w.dord, Ord(0));
         } else {
             exact_walk<Op, kSwz, Ord>(x, p.swz, col, w, acc, true);
         }
@@ -591,25 +593,25 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
 #pragma unroll
     for (int e = 0; e < 4; ++e) part[warp][lane][e] = acc[e];
     __syncthreads();
-    if (warp == 0) {
+    // warps 0..3 fold component `warp` of the 8 warps' partials
+    if (warp < 4) {
+        typename Op::S v = part[0][lane][warp];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            typename Op::S s = part[0][lane][e];
-            for (int w = 1; w < kColsAffWarps; ++w) Op::merge(s, part[w][lane][e]);
-            part[0][lane][e] = s;
-        }
+        for (int w = 1; w < kColsAffWarps; ++w) Op::merge(v, part[w][lane][warp]);
+        part[0][lane][warp] = v;
     }
     cluster.sync();
-    if (split == 0 && warp == 0 && live_col) {
+    // rank 0: warps 0..3 read every peer's partial at once, then fold
+    if (split == 0 && warp < 4 && live_col) {
+        typename Op::S v = part[0][lane][warp];
+        typename Op::S peer[7];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            typename Op::S s = part[0][lane][e];
-            for (int r = 1; r < splits; ++r) {
-                typename Op::S(*peer)[32][4] = cluster.map_shared_rank(part, r);
-                Op::merge(s, peer[0][lane][e]);
-            }
-            store_result<Op>(out, kv * 4 + e, s);
-        }
+        for (int r = 1; r < 8; ++r)
+            if (r < splits) peer[r - 1] = cluster.map_shared_rank(part, r)[0][lane][warp];
+#pragma unroll
+        for (int r = 1; r < 8; ++r)
+            if (r < splits) Op::merge(v, peer[r - 1]);
+        store_result<Op>(out, kv * 4 + warp, v);
     }
     cluster.sync();
 }
@@ -761,11 +763,15 @@ template <class Op, bool kSwz, class Ord>
 int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
     if (L.kernel == 3) {
         // every warp resident at once, each with the same number of rows
-        int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reduce_rows_affine<Op, kSwz, Ord>,
-                                                          kRowsAffThreads, 0) != cudaSuccess || per_sm < 1) {
-            cudaGetLastError();
-            per_sm = 1;
+        static int per_sm = 0;  // one query per kernel instantiation
+        if (per_sm == 0) {
+            int q = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&q, reduce_rows_affine<Op, kSwz, Ord>,
+                                                              kRowsAffThreads, 0) != cudaSuccess || q < 1) {
+                cudaGetLastError();
+                q = 1;
+            }
+            per_sm = q;
         }
         const int64_t capacity = int64_t(sm_count()) * per_sm * kRowsAffWarps;
         const int64_t rpw = (p.n_kept + capacity - 1) / capacity;
