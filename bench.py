@@ -387,8 +387,11 @@ def main() -> None:
 
     # -------- contractions (configs 1 and 3) on this device --------
     contraction = None
+    sharded = None
     if not args.no_gemm:
         contraction = bench_gemm(torch, N, kernels, s, stream)
+        # config 5 at this world size (strong scaling of a fixed contraction)
+        sharded = {m: bench_sharded(torch, dist, N, kernels, m, world, rank) for m in ("m", "k")}
 
     if rank == 0:
         peaks = load_peaks()
@@ -426,6 +429,8 @@ def main() -> None:
         }
         if contraction:
             line["contraction"] = contraction
+        if sharded:
+            line["sharded_contraction"] = {"m_split": sharded["m"], "k_split": sharded["k"]}
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line))
@@ -472,6 +477,62 @@ def bench_gemm(torch, N, kernels, s, stream) -> dict:
         del pa, pb, sa, sb, c
     N.raise_device_status()
     return out
+
+
+def quantize_generated(torch, N, kernels, fmt, rows, cols, seed, sigma=1.0, block=8192):
+    """Device planes of a seeded N(0, sigma^2) [rows, cols] operand, generated
+    and quantised in row blocks (bounded Float32 staging)."""
+    rb = kernels.mx_row_bytes(fmt, cols)
+    katoms = (cols // 32 + 3) // 4
+    pay = N.DeviceBuffer(rows * rb)
+    sc = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, cols // 32))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    s = torch.cuda.current_stream().cuda_stream
+    for r0 in range(0, rows, block):
+        n = min(block, rows - r0)
+        x = torch.randn((n, cols), generator=gen, device="cuda", dtype=torch.float32) * sigma
+        kernels.mx_quantize(fmt, x.data_ptr(), n, cols, cols, 1, pay.ptr + r0 * rb, rb,
+                            sc.ptr + (r0 // 128) * katoms * 512, stream=s)
+        del x
+    return pay, sc
+
+
+def bench_sharded(torch, dist, N, kernels, mode, world, rank, steps=5, warmup=2) -> dict:
+    """Config 5: sharded MXFP8 contraction M=65536, N=16384, K=16384, inputs
+    N(0,1), at `world` GPUs; M-split (B replicated, no collective) or K-split
+    (NCCL reduce-scatter of Float32 partials, overlapped over 4 N-chunks)."""
+    from strideweave_b200.sharding import MXShardedContraction, ShardPlan
+
+    M, Nn, K = 65536, 16384, 16384
+    fmt = N.SW_MX_E4M3
+    plan = ShardPlan(mode, world, rank, M, Nn, K, k_quantum=128, chunks=4 if mode == "k" else 1)
+    rows = plan.rows_local if mode == "m" else M
+    a = quantize_generated(torch, N, kernels, fmt, rows, plan.k_local, seed=7000 + rank)
+    b = quantize_generated(torch, N, kernels, fmt, Nn, plan.k_local, seed=9000 + (rank if mode == "k" else 0))
+    op = MXShardedContraction(plan, fmt, a, b)
+    for _ in range(warmup):
+        op.run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        op.run()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tflops = 2.0 * M * Nn * K / (ms / 1e3) / 1e12
+    N.raise_device_status()
+    del op, a, b
+    torch.cuda.empty_cache()
+    return {"tflops": round(tflops, 1), "ms": round(ms, 3), "n_gpus": world, "scaling": "strong",
+            "config": f"MXFP8 M=65536 N=16384 K=16384, {'M-split' if mode == 'm' else 'K-split + NCCL reduce-scatter, 4 N-chunks'}"}
 
 
 def profile_case(case: str, reps: int) -> None:
