@@ -253,7 +253,7 @@ def main() -> None:
     ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed busy time under the clock sampler before the timed region")
-    ap.add_argument("--profile-case", choices=["reduce", "mxfp8", "mxfp4"],
+    ap.add_argument("--profile-case", choices=["reduce", "mxfp8", "mxfp4", "mlp"],
                     help="run a short, fixed sequence of launches for ncu and exit (no timing)")
     ap.add_argument("--reps", type=int, default=2, help="rounds of launches of --profile-case")
     args = ap.parse_args()
@@ -388,10 +388,12 @@ def main() -> None:
     # -------- contractions (configs 1 and 3) on this device --------
     contraction = None
     sharded = None
+    mlp = None
     if not args.no_gemm:
         contraction = bench_gemm(torch, N, kernels, s, stream)
         # config 5 at this world size (strong scaling of a fixed contraction)
         sharded = {m: bench_sharded(torch, dist, N, kernels, m, world, rank) for m in ("m", "k")}
+        mlp = bench_mlp(torch, N)
 
     if rank == 0:
         peaks = load_peaks()
@@ -431,6 +433,8 @@ def main() -> None:
             line["contraction"] = contraction
         if sharded:
             line["sharded_contraction"] = {"m_split": sharded["m"], "k_split": sharded["k"]}
+        if mlp:
+            line["mlp_step"] = mlp
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line))
@@ -535,6 +539,50 @@ def bench_sharded(torch, dist, N, kernels, mode, world, rank, steps=5, warmup=2)
             "config": f"MXFP8 M=65536 N=16384 K=16384, {'M-split' if mode == 'm' else 'K-split + NCCL reduce-scatter, 4 N-chunks'}"}
 
 
+def bench_mlp(torch, N, steps=5, warmup=2) -> dict:
+    """Config 4: one MXFP8 MLP training step - 1024 -> 4096 -> 4096 -> 1024 with
+    GELU, batch 8192, fp32 master weights N(0, 0.02), inputs and targets N(0, 1),
+    MSE loss; forward, reference-autograd backward (dgrad and wgrad with MX
+    re-quantisation along each contraction's K), SGD update."""
+    sys.path.append(str(ROOT / "baseline" / "_ref"))
+    from strideweave import Layout, Shape, Stride, Tensor
+
+    from strideweave_b200 import CUDA, nn
+
+    B, dims = 8192, [1024, 4096, 4096, 1024]
+    rng = np.random.default_rng(0)
+    model = nn.MLP(dims, fmt="MXFP8_E4M3", seed=0, std=0.02)
+    x = rng.standard_normal((B, dims[0])).astype(np.float32)
+    t = rng.standard_normal((B, dims[-1])).astype(np.float32)
+    xt = Tensor(CUDA.from_numpy(x.ravel()), 0, Layout(Shape([B, dims[0]]), Stride([dims[0], 1])))
+    tt = Tensor(CUDA.from_numpy(t.T.ravel().copy()), 0, Layout(Shape([B, dims[-1]]), Stride([1, B])))
+    losses = []
+
+    def step():
+        # the fused step: the same kernels as the autograd path, scheduled
+        # explicitly (the reference's leaf-gradient copy is per element)
+        return model.train_step(xt, tt, lr=1e-3)
+
+    for _ in range(warmup):
+        losses.append(step())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        losses.append(step())
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    per_gemm = [2.0 * B * dims[i] * dims[i + 1] for i in range(len(dims) - 1)]
+    flops = 3 * sum(per_gemm) - per_gemm[0]  # forward + wgrad for all layers, dgrad for layers 2..3
+    N.raise_device_status()
+    first, last = float(losses[0][0]), float(losses[-1][0])
+    return {"tflops": round(flops / (ms / 1e3) / 1e12, 1), "ms_per_step": round(ms, 3),
+            "flop_per_step": flops, "loss_first": round(first, 5), "loss_last": round(last, 5),
+            "config": "MXFP8 MLP 1024-4096-4096-1024, GELU, batch 8192, MSE, SGD lr 1e-3 (fwd + bwd + step, "
+                      "no first-layer dgrad)"}
+
+
 def profile_case(case: str, reps: int) -> None:
     """A fixed, small sequence of launches for an ncu capture.
 
@@ -546,6 +594,11 @@ def profile_case(case: str, reps: int) -> None:
     from strideweave_b200 import kernels
 
     N.set_device(0)
+    if case == "mlp":
+        import torch
+
+        print(bench_mlp(torch, N, steps=reps, warmup=1))
+        return
     if case == "reduce":
         x = np.random.default_rng(0).uniform(-1, 1, size=(R, C)).astype(np.float32)
         bufs = {}

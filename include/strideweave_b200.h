@@ -52,7 +52,9 @@ int sw_device_count(int* count);
 int sw_set_device(int device);
 int sw_get_device(int* device);
 
-/* Device storage of a carrier's flat index space.
+/* Device storage of a carrier's flat index space, from the device's stream-ordered
+ * memory pool in the order of the legacy default stream (allocation and release
+ * never synchronise the device; memory is reused without returning to the driver).
  * Replaces the owned storage of CPU(size, ...) in
  * src/strideweave/carriers/cpu/native/_cpu_carrier.hpp:38-67. */
 int sw_alloc(void** ptr, int64_t bytes);
@@ -142,6 +144,27 @@ int sw_reduce_backward_f32(const sw_reduce_plan* plan, const float* x,
 int sw_copy_view_f32(const sw_reduce_plan* src_plan, const float* src,
                      int64_t src_size, const sw_reduce_plan* dst_plan,
                      float* dst, int64_t dst_size, void* stream);
+
+/* ---- elementwise work around the contractions (the MLP step) ------------- */
+
+#define SW_EW_GELU 0      /* out = a * Phi(a), the erf GELU                    */
+#define SW_EW_GELU_GRAD 1 /* out = b * d/da (a * Phi(a)); b = upstream grad    */
+#define SW_EW_AXPY 2      /* out = a + alpha * b (out may alias a: SGD update) */
+
+/* Elementwise Float32 map over n contiguous elements.  GELU follows the
+ * reference's erf form, gelu(x) = x / 2 * (1 + erf(x / sqrt 2))
+ * (src/strideweave/carriers/cpu/native/_cpu_operation.hpp:33-40); AXPY is the
+ * SGD update the reference applies element by element
+ * (src/strideweave/nn/optim.py:45-80). */
+int sw_elementwise_f32(int op, int64_t n, const float* a, const float* b,
+                       float* out, float alpha, void* stream);
+
+/* Mean squared error of n contiguous pairs: loss[0] = sum((p - t)^2) / n
+ * (float accumulation; MSELoss, src/strideweave/nn/modules.py:129-200).
+ * With grad != NULL also grad[i] = u * 2 * (p[i] - t[i]) / n, where u is
+ * upstream[0] (the loss gradient on the device) or 1 when upstream is NULL. */
+int sw_mse_f32(int64_t n, const float* pred, const float* target, float* loss,
+               const float* upstream, float* grad, void* stream);
 
 /* ---- MX (OCP Microscaling v1.0) quantise / dequantise ------------------- */
 

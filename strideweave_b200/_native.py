@@ -37,6 +37,9 @@ SW_SCALES_ROWMAJOR = 0
 SW_SCALES_TC128 = 1
 SW_OUT_F32 = 0
 SW_OUT_BF16 = 1
+SW_EW_GELU = 0
+SW_EW_GELU_GRAD = 1
+SW_EW_AXPY = 2
 
 
 class DeviceTimeout(RuntimeError):
@@ -88,6 +91,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_copy_view_f32": (
         c_int, [POINTER(ReducePlan), c_void_p, c_int64, POINTER(ReducePlan), c_void_p, c_int64, c_void_p],
     ),
+    "sw_elementwise_f32": (c_int, [c_int, c_int64, c_void_p, c_void_p, c_void_p, ctypes.c_float, c_void_p]),
+    "sw_mse_f32": (c_int, [c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "sw_mx_scale_index": (c_int64, [c_int64, c_int64, c_int64]),
     "sw_mx_scale_bytes_tc128": (c_int64, [c_int64, c_int64]),
     "sw_mx_quantize": (

@@ -161,8 +161,9 @@ class CUDA(Carrier):
         self._dtype = dtype
         self._mutable = bool(mutable)
         self._swizzle = swizzle
-        self._device = N.current_device() if device is None else int(device)
-        if device is not None:
+        current = N.current_device()
+        self._device = current if device is None else int(device)
+        if self._device != current:
             N.set_device(self._device)
         self._nbytes = storage_bytes(dtype, size)
         self._buffer: N.DeviceBuffer | None = N.DeviceBuffer(self._nbytes)

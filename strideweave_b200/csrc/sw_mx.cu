@@ -176,21 +176,25 @@ __global__ void __launch_bounds__(256) quantize_strided(const float* __restrict_
         for (int i = 0; i < 32; ++i) v[i] = special ? 0.0f : __fmul_rn(v[i], inv);
         if (FMT == SW_MX_E4M3) {
             uint8_t* dst = payload + r * ldp + c0;
+            uint32_t w[8];
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                const uint32_t w = e4m3x4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-                for (int i = 0; i < 4; ++i)
-                    if (4 * g + i < len) dst[4 * g + i] = uint8_t((w >> (8 * i)) & 0xFF);
+            for (int g = 0; g < 8; ++g) w[g] = e4m3x4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+            if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+                for (int c = 0; c < len; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
             }
         } else {
             uint8_t* dst = payload + r * ldp + c0 / 2;
+            uint32_t w[4];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-                const uint32_t w = e2m1x8(v + 8 * g);
-                for (int i = 0; i < 8; i += 2) {
-                    const int c = 8 * g + i;
-                    if (c >= len) break;
-                    const uint8_t byte = uint8_t((w >> (4 * i)) & 0xFF);
+            for (int g = 0; g < 4; ++g) w[g] = e2m1x8(v + 8 * g);
+            if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+            } else {
+                for (int c = 0; c < len; c += 2) {
+                    const uint8_t byte = uint8_t((w[c / 8] >> (4 * (c % 8))) & 0xFF);
                     if (c + 1 < len) dst[c / 2] = byte;
                     else dst[c / 2] = uint8_t((dst[c / 2] & 0xF0) | (byte & 0x0F));
                 }

@@ -62,23 +62,42 @@ int sw_get_device(int* device) {
     return ok();
 }
 
+// Carrier storage comes from the device's stream-ordered memory pool on the
+// legacy default stream (the stream every carrier operation is ordered on):
+// allocation and release neither synchronise the device nor return memory to
+// the driver between steps.
+static int ensure_pool(int device) {
+    static bool configured[64] = {};
+    if (device < 0 || device >= 64 || configured[device]) return SW_OK;
+    cudaMemPool_t pool;
+    SW_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device), "cudaDeviceGetDefaultMemPool");
+    uint64_t keep = ~uint64_t(0);
+    SW_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep), "pool release threshold");
+    configured[device] = true;
+    return SW_OK;
+}
+
 int sw_alloc(void** ptr, int64_t bytes) {
     if (!ptr) return fail(SW_ERR_INVALID, "sw_alloc: null output");
     *ptr = nullptr;
     if (bytes < 0) return fail(SW_ERR_INVALID, "sw_alloc: negative size %lld", (long long)bytes);
     if (bytes == 0) return ok();
-    cudaError_t err = cudaMalloc(ptr, (size_t)bytes);
+    int dev = 0;
+    SW_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    int rc = ensure_pool(dev);
+    if (rc != SW_OK) return rc;
+    cudaError_t err = cudaMallocAsync(ptr, (size_t)bytes, (cudaStream_t)0);
     if (err == cudaErrorMemoryAllocation) {
         cudaGetLastError();
         return fail(SW_ERR_NOMEM, "sw_alloc: out of device memory (%lld bytes)", (long long)bytes);
     }
-    SW_CUDA_TRY(err, "cudaMalloc");
+    SW_CUDA_TRY(err, "cudaMallocAsync");
     return ok();
 }
 
 int sw_free(void* ptr) {
     if (!ptr) return ok();
-    SW_CUDA_TRY(cudaFree(ptr), "cudaFree");
+    SW_CUDA_TRY(cudaFreeAsync(ptr, (cudaStream_t)0), "cudaFreeAsync");
     return ok();
 }
 

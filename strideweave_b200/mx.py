@@ -222,69 +222,87 @@ def _quantize_view(ptr: int, rows: int, K: int, ldr: int, ldc: int, code: int, d
     return payload, scales
 
 
+def linear_forward(x: Tensor, w: Tensor, fmt: str) -> Tensor:
+    """y = x . w^T with x [B, in], w [out, in] Float32 on CUDA, both quantised
+    along `in`; y [B, out] in the canonical column-major layout."""
+    from .carrier import CUDA
+    from .layout_plan import canonical_layout
+
+    code = FORMATS[fmt][2]
+    xp, B, IN, xr, xc = _f32_operand(x, "x")
+    wp, OUT, IN2, wr, wc = _f32_operand(w, "weight")
+    if IN != IN2:
+        raise ValueError("Matmul inner dimensions must match")
+    q = 256 if code == N.SW_MX_E2M1 else 128
+    for name, n in (("batch", B), ("out", OUT), ("in", IN)):
+        if n % q != 0:
+            raise NotImplementedError(f"mx_linear needs {name} extent {n} to be a multiple of {q}")
+    dev = x.carrier.device
+    qx = _quantize_view(xp, B, IN, xr, xc, code, dev)
+    qw = _quantize_view(wp, OUT, IN, wr, wc, code, dev)
+    layout = canonical_layout(x.layout.shape.top_level[0], w.layout.shape.top_level[0])
+    out = CUDA(B * OUT, dtype=DType.Float32, empty=True, device=dev)
+    rb = kernels.mx_row_bytes(code, IN)
+    kernels.mx_gemm(code, qx[0].data_ptr, rb, qx[1].data_ptr, qw[0].data_ptr, rb, qw[1].data_ptr, out.data_ptr,
+                    B, OUT, IN, ldc_m=1, ldc_n=B)
+    return Tensor(out, 0, layout)
+
+
+def linear_backward(x: Tensor, w: Tensor, gradient: Tensor, fmt: str, *, need_dx: bool = True
+                    ) -> tuple[Tensor | None, Tensor]:
+    """(dx, dw) of y = x . w^T: dx = g . w (K = out), dw = g^T . x (K = batch),
+    each operand re-quantised along its contraction's K; gradients in the
+    injective canonical layouts of x and w."""
+    from .carrier import CUDA
+    from .layout_plan import injective_layout_for
+
+    code = FORMATS[fmt][2]
+    gp, B, OUT, gr_, gc = _f32_operand(gradient, "gradient")
+    xp, _, IN, xr, xc = _f32_operand(x, "x")
+    wp, _, _, wr, wc = _f32_operand(w, "weight")
+    dev = x.carrier.device
+    dx = None
+    if need_dx:
+        # dx[b, i] = sum_o g[b, o] w[o, i]: operands g [B, OUT] and w^T [IN, OUT]
+        qg = _quantize_view(gp, B, OUT, gr_, gc, code, dev)
+        qwt = _quantize_view(wp, IN, OUT, wc, wr, code, dev)
+        dx_layout = injective_layout_for(x.layout)
+        dxc = CUDA(dx_layout.cosize, dtype=DType.Float32, empty=True, device=dev)
+        (_, s0), (_, s1) = single_stride(mode_leaves(dx_layout, 0)), single_stride(mode_leaves(dx_layout, 1))
+        rb = kernels.mx_row_bytes(code, OUT)
+        kernels.mx_gemm(code, qg[0].data_ptr, rb, qg[1].data_ptr, qwt[0].data_ptr, rb, qwt[1].data_ptr, dxc.data_ptr,
+                        B, IN, OUT, ldc_m=s0, ldc_n=s1)
+        dx = Tensor(dxc, 0, dx_layout)
+    # dw[o, i] = sum_b g[b, o] x[b, i]: operands g^T [OUT, B] and x^T [IN, B]
+    qgt = _quantize_view(gp, OUT, B, gc, gr_, code, dev)
+    qxt = _quantize_view(xp, IN, B, xc, xr, code, dev)
+    dw_layout = injective_layout_for(w.layout)
+    dwc = CUDA(dw_layout.cosize, dtype=DType.Float32, empty=True, device=dev)
+    (_, s0), (_, s1) = single_stride(mode_leaves(dw_layout, 0)), single_stride(mode_leaves(dw_layout, 1))
+    rb = kernels.mx_row_bytes(code, B)
+    kernels.mx_gemm(code, qgt[0].data_ptr, rb, qgt[1].data_ptr, qxt[0].data_ptr, rb, qxt[1].data_ptr, dwc.data_ptr,
+                    OUT, IN, B, ldc_m=s0, ldc_n=s1)
+    return dx, Tensor(dwc, 0, dw_layout)
+
+
 class MxLinear(Operation):
     """Differentiable MX contraction y[b, o] = sum_i x[b, i] w[o, i] (the
     ``nn.Linear`` contraction, src/strideweave/nn/modules.py:40-127, with
-    weight [out, in]).  Float32 in and out; the forward quantises x and w along
-    ``in``; the backward re-quantises along each gradient contraction's own K:
-    dx = g . w (K = out) and dw = g^T . x (K = batch).
+    weight [out, in]).  Float32 in and out; see linear_forward and
+    linear_backward for the quantisation of each contraction.
     """
 
     fmt = "MXFP8_E4M3"
 
     def _forward(self, x: Any, w: Any) -> Tensor:
-        from .carrier import CUDA
-        from .layout_plan import canonical_layout
-
-        code = FORMATS[self.fmt][2]
-        xp, B, IN, xr, xc = _f32_operand(x, "x")
-        wp, OUT, IN2, wr, wc = _f32_operand(w, "weight")
-        if IN != IN2:
-            raise ValueError("Matmul inner dimensions must match")
-        for name, n in (("batch", B), ("out", OUT), ("in", IN)):
-            if n % 128 != 0 or (code == N.SW_MX_E2M1 and n % 256 != 0):
-                raise NotImplementedError(f"mx_linear needs {name} extent {n} to be a multiple of "
-                                          f"{256 if code == N.SW_MX_E2M1 else 128}")
-        dev = x.carrier.device
-        qx = _quantize_view(xp, B, IN, xr, xc, code, dev)
-        qw = _quantize_view(wp, OUT, IN, wr, wc, code, dev)
-        layout = canonical_layout(x.layout.shape.top_level[0], w.layout.shape.top_level[0])
-        self.ctx["output_layout"] = layout
-        out = CUDA(B * OUT, dtype=DType.Float32, empty=True, device=dev)
-        rb = kernels.mx_row_bytes(code, IN)
-        kernels.mx_gemm(code, qx[0].data_ptr, rb, qx[1].data_ptr, qw[0].data_ptr, rb, qw[1].data_ptr, out.data_ptr,
-                        B, OUT, IN, ldc_m=1, ldc_n=B)
-        return Tensor(out, 0, layout)
+        out = linear_forward(x, w, self.fmt)
+        self.ctx["output_layout"] = out.layout
+        return out
 
     def backward(self, gradient: Any) -> tuple[Any, Any]:
-        from .carrier import CUDA
-        from .layout_plan import injective_layout_for
-
         x, w = self.inputs()
-        code = FORMATS[self.fmt][2]
-        gp, B, OUT, gr_, gc = _f32_operand(gradient, "gradient")
-        xp, _, IN, xr, xc = _f32_operand(x, "x")
-        wp, _, _, wr, wc = _f32_operand(w, "weight")
-        dev = x.carrier.device
-        # dx[b, i] = sum_o g[b, o] w[o, i]: operands g [B, OUT] and w^T [IN, OUT]
-        qg = _quantize_view(gp, B, OUT, gr_, gc, code, dev)
-        qwt = _quantize_view(wp, IN, OUT, wc, wr, code, dev)
-        dx_layout = injective_layout_for(x.layout)
-        dx = CUDA(dx_layout.cosize, dtype=DType.Float32, empty=True, device=dev)
-        (_, dxr), (_, dxc) = single_stride(mode_leaves(dx_layout, 0)), single_stride(mode_leaves(dx_layout, 1))
-        rb = kernels.mx_row_bytes(code, OUT)
-        kernels.mx_gemm(code, qg[0].data_ptr, rb, qg[1].data_ptr, qwt[0].data_ptr, rb, qwt[1].data_ptr, dx.data_ptr,
-                        B, IN, OUT, ldc_m=dxr, ldc_n=dxc)
-        # dw[o, i] = sum_b g[b, o] x[b, i]: operands g^T [OUT, B] and x^T [IN, B]
-        qgt = _quantize_view(gp, OUT, B, gc, gr_, code, dev)
-        qxt = _quantize_view(xp, IN, B, xc, xr, code, dev)
-        dw_layout = injective_layout_for(w.layout)
-        dw = CUDA(dw_layout.cosize, dtype=DType.Float32, empty=True, device=dev)
-        (_, dwr), (_, dwc) = single_stride(mode_leaves(dw_layout, 0)), single_stride(mode_leaves(dw_layout, 1))
-        rb = kernels.mx_row_bytes(code, B)
-        kernels.mx_gemm(code, qgt[0].data_ptr, rb, qgt[1].data_ptr, qxt[0].data_ptr, rb, qxt[1].data_ptr, dw.data_ptr,
-                        OUT, IN, B, ldc_m=dwr, ldc_n=dwc)
-        return (Tensor(dx, 0, dx_layout), Tensor(dw, 0, dw_layout))
+        dx, dw = linear_backward(x, w, gradient, self.fmt)
+        return (dx, dw)
 
 
 class MxLinearFP4(MxLinear):

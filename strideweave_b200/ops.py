@@ -252,9 +252,12 @@ def make_operation(name: str) -> Any:
     if name in _OPS:
         return _OPS[name]()
     from .mx import MX_OPERATIONS
+    from .nn import NN_OPERATIONS
 
     if name in MX_OPERATIONS:
         return MX_OPERATIONS[name]()
+    if name in NN_OPERATIONS:
+        return NN_OPERATIONS[name]()
     shared = _shared(name)
     if shared is not None:
         return shared()
@@ -269,6 +272,7 @@ def declared_plans() -> list[Any]:
         resolve_operation_plan("reduce_max", f32),
         resolve_operation_plan("argmax", f32),
         resolve_operation_plan("matmul", f32, f32),
+        resolve_operation_plan("gelu", f32),
     ]
 
 

@@ -1,0 +1,125 @@
+"""One MX MLP training step on the CUDA carrier (forward, reference autograd
+backward with MX re-quantisation, SGD) against a float64 numpy emulation
+that quantises every contraction operand with the CPU oracle."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+sw = pytest.importorskip("strideweave")
+from strideweave import Layout, Shape, Stride, Tensor  # noqa: E402
+
+from oracle import oracle as O  # noqa: E402
+from tests.gpu_util import rel_frobenius  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def dq(m: np.ndarray, code: int) -> np.ndarray:
+    """Quantise rows of m (blocks along axis 1) and dequantise, exactly."""
+    m = np.ascontiguousarray(m, dtype=np.float32)
+    p, s = O.mx_quantize(code, m, scale_layout=1)
+    return O.mx_dequantize(code, p, s, m.shape[0], m.shape[1], scale_layout=1).astype(np.float64)
+
+
+def gelu(x):
+    erf = np.vectorize(math.erf)
+    return 0.5 * x * (1.0 + erf(x / math.sqrt(2.0)))
+
+
+def gelu_grad(x):
+    erf = np.vectorize(math.erf)
+    return 0.5 * (1.0 + erf(x / math.sqrt(2.0))) + x * np.exp(-0.5 * x * x) / math.sqrt(2.0 * math.pi)
+
+
+def emulate(x, t, Ws, code, lr):
+    f32 = lambda a: a.astype(np.float32)  # noqa: E731  (device keeps activations in Float32)
+    h, a = [], [x]
+    for i, W in enumerate(Ws):
+        z = f32(dq(a[-1], code) @ dq(W, code).T)
+        h.append(z)
+        a.append(f32(gelu(z.astype(np.float64))) if i + 1 < len(Ws) else z)
+    y = a[-1]
+    n = y.size
+    loss = float(np.mean((y.astype(np.float64) - t) ** 2))
+    g = f32(2.0 * (y.astype(np.float64) - t) / n)
+    dWs = [None] * len(Ws)
+    for i in reversed(range(len(Ws))):
+        dWs[i] = dq(g.T, code) @ dq(a[i].T, code).T
+        if i > 0:
+            da = f32(dq(g, code) @ dq(Ws[i].T, code).T)
+            g = f32(da.astype(np.float64) * gelu_grad(h[i - 1].astype(np.float64)))
+    new = [W - lr * dW for W, dW in zip(Ws, dWs)]
+    return loss, dWs, new
+
+
+@pytest.mark.parametrize("fmt,code", [("MXFP8_E4M3", O.E4M3), ("MXFP4", O.E2M1)])
+def test_mlp_training_step_matches_the_emulation(fmt, code):
+    from strideweave_b200 import CUDA, nn
+
+    B, dims, lr = 256, [256, 512, 512, 256], 0.1
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((B, dims[0])).astype(np.float32)
+    t = rng.standard_normal((B, dims[-1])).astype(np.float32)
+    model = nn.MLP(dims, fmt=fmt, seed=1)
+    Ws = [layer.weight.carrier.to_numpy().reshape(layer.out_features, layer.in_features) for layer in model.layers]
+    xt = Tensor(CUDA.from_numpy(x.ravel()), 0, Layout(Shape([B, dims[0]]), Stride([dims[0], 1])))
+    # targets in the canonical result layout of the last contraction ([B, out] : (1, B))
+    tt = Tensor(CUDA.from_numpy(t.T.ravel().copy()), 0, Layout(Shape([B, dims[-1]]), Stride([1, B])))
+    opt = nn.SGD(model.parameters(), lr=lr)
+    loss = nn.MSELoss()(model(xt), tt)
+    loss.backward()
+    grads = [layer.weight.grad.carrier.to_numpy().reshape(layer.out_features, layer.in_features)
+             for layer in model.layers]
+    opt.step()
+    new = [layer.weight.carrier.to_numpy().reshape(layer.out_features, layer.in_features) for layer in model.layers]
+
+    want_loss, want_grads, want_new = emulate(x, t.astype(np.float64), [W.astype(np.float64) for W in Ws], code, lr)
+    assert abs(loss[0] - want_loss) <= 1e-3 * abs(want_loss)
+    for g, w in zip(grads, want_grads):
+        assert rel_frobenius(g, w) <= 1e-2
+    for a, b in zip(new, want_new):
+        assert rel_frobenius(a, b) <= 1e-4
+    opt.zero_grad()
+    assert all(p.grad is None for p in model.parameters())
+
+
+def test_gelu_and_mse_operations_through_autograd():
+    from strideweave_b200 import CUDA, nn
+
+    x = np.linspace(-4, 4, 64, dtype=np.float32)
+    lay = Layout(Shape([8, 8]), Stride([1, 8]))
+    xt = Tensor(CUDA.from_numpy(x), 0, lay)
+    y = nn.gelu(xt)
+    assert type(y.autograd_ctx).__name__ == "CudaGelu"
+    np.testing.assert_allclose(y.carrier.to_numpy(), gelu(x.astype(np.float64)), rtol=2e-6, atol=2e-7)
+    target = Tensor(CUDA.from_numpy(np.zeros(64, np.float32)), 0, lay)
+    loss = nn.mse_loss(y, target)
+    loss.backward()
+    want = 2.0 * gelu(x.astype(np.float64)) / 64 * gelu_grad(x.astype(np.float64))
+    np.testing.assert_allclose(xt.grad.carrier.to_numpy(), want, rtol=1e-5, atol=1e-7)
+
+
+def test_fused_train_step_equals_the_autograd_step():
+    from strideweave_b200 import CUDA, nn
+
+    B, dims = 256, [256, 384, 256]
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((B, dims[0])).astype(np.float32)
+    t = rng.standard_normal((B, dims[-1])).astype(np.float32)
+    lay_x = Layout(Shape([B, dims[0]]), Stride([dims[0], 1]))
+    lay_t = Layout(Shape([B, dims[-1]]), Stride([1, B]))
+    a, b = nn.MLP(dims, seed=3), nn.MLP(dims, seed=3)
+    xt = Tensor(CUDA.from_numpy(x.ravel()), 0, lay_x)
+    tt = Tensor(CUDA.from_numpy(t.T.ravel().copy()), 0, lay_t)
+    loss_a = nn.MSELoss()(a(xt), tt)
+    loss_a.backward()
+    nn.SGD(a.parameters(), lr=0.05).step()
+    loss_b = b.train_step(xt, tt, lr=0.05)
+    # the loss is an atomic sum over blocks: equal up to summation order
+    assert abs(loss_a[0] - loss_b[0]) <= 1e-6 * abs(loss_a[0])
+    for la, lb in zip(a.layers, b.layers):
+        np.testing.assert_array_equal(la.weight.carrier.to_numpy(), lb.weight.carrier.to_numpy())
