@@ -6,12 +6,16 @@
 // One persistent CTA per SM walks 128 x BN output tiles.  Warp roles:
 //   warp 0 - TMA producer: 2-D tiled loads of the payload tiles (128-byte
 //            swizzled rows) and 1-D bulk loads of the scale atoms into a
-//            4-stage shared-memory ring;
+//            3- or 4-stage shared-memory ring;
 //   warp 1 - allocates TMEM; one thread copies each stage's scale atoms from
 //            shared memory into TMEM (tcgen05.cp .32x128b.warpx4) and issues
 //            the tcgen05.mma block_scale instructions, committing each stage
 //            back to the producer and each finished tile to the epilogue;
-//   warps 2..5 - epilogue: tcgen05.ld of the accumulator, fp32 or bf16 stores.
+//   warps 2..5 - epilogue: tcgen05.ld of the accumulator.  bf16 row-major
+//            results are staged in a 128-byte-swizzled shared-memory tile and
+//            written by TMA bulk stores; the accumulator is released as soon as
+//            it is in registers, so the stores overlap the next tile's MMAs
+//            (3-stage ring).  Other results are stored from registers.
 // The scale atoms are read exactly as the carrier stores them (the
 // SW_SCALES_TC128 placement): a 512-byte atom holds 128 rows x 4 blocks in the
 // order the tcgen05.cp replication expects, so no shuffle is needed.
@@ -28,6 +32,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "sw_common.cuh"
@@ -38,11 +43,13 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // payload bytes of K per stage (one 128B swizzle row)
-constexpr int kStages = 4;
 constexpr int kThreads = 192;  // 6 warps
 constexpr int kTmemCols = 512;
 
-template <int FMT, int BN>
+// kTmaEpi: the accumulator is drained into a 128-byte-swizzled shared-memory
+// tile (bf16, 128 x BN) and written by TMA bulk stores that run while the next
+// tile's MMAs do; the TMEM accumulator is released as soon as it is read.
+template <int FMT, int BN, int kStages, bool kTmaEpi>
 struct Cfg {
     static constexpr int kAtoms = FMT == SW_MX_E4M3 ? 1 : 2;      // scale atoms (4 blocks) per stage
     static constexpr int kABytes = kBM * kBKBytes;                 // 16 KiB
@@ -63,7 +70,10 @@ struct Cfg {
     static constexpr int kOffBar = kOffSfb + kStages * kSfbBytes;
     static constexpr int kNumBars = 2 * kStages + 3;
     static constexpr int kOffSlot = kOffBar + kNumBars * 8;
-    static constexpr int kSmemBytes = kOffSlot + 16 + 1024;        // + alignment slack
+    static constexpr int kStageOutBytes = kTmaEpi ? kBM * BN * 2 : 0;   // bf16 staging tile
+    static constexpr int kOffOut = (kOffSlot + 16 + 1023) / 1024 * 1024;
+    static constexpr int kSmemBytes = kOffOut + kStageOutBytes + 1024;  // + alignment slack
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
     static constexpr uint32_t kStageTx = kABytes + kBBytes + kSfaBytes + kSfbBytes;
 };
 
@@ -85,11 +95,11 @@ struct GemmArgs {
     int out_bf16;
 };
 
-template <int FMT, int BN>
+template <int FMT, int BN, int kStages, bool kTmaEpi>
 __global__ void __launch_bounds__(kThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const GemmArgs args) {
-    using C = Cfg<FMT, BN>;
+                   const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
+    using C = Cfg<FMT, BN, kStages, kTmaEpi>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = ptx::smem_addr(smem);
@@ -114,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::fence_barrier_init();
         ptx::prefetch_tmap(&tmap_a);
         ptx::prefetch_tmap(&tmap_b);
+        if (kTmaEpi) ptx::prefetch_tmap(&tmap_c);
     }
     if (warp == 1) {
         ptx::tmem_alloc(ptx::smem_addr(tmem_slot), kTmemCols);
@@ -232,6 +243,64 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_commit(bar_drain);
             ptx::mbar_wait(bar_drain, 0);
         }
+    } else if (kTmaEpi) {
+        // ---------------- epilogue, staged through shared memory ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;   // row of the tile this thread drains
+        const bool leader = threadIdx.x == 64;  // first epilogue thread issues the stores
+        uint8_t* stage_out = smem + C::kOffOut;
+        const uint32_t stage_addr = sbase + C::kOffOut;
+        // Every epilogue thread runs the same barrier sequence for every tile:
+        // after a bounded wait gives up the thread stops working but keeps
+        // meeting the named barriers, so no thread can wait for one that left.
+        uint32_t tile_iter = 0;
+        bool alive = true;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
+            int mb, nb;
+            tile_coords(t, mb, nb);
+            if (alive && !ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) alive = false;
+            if (alive) ptx::tc_fence_after();
+            // the previous tile's stores must have left the staging tile
+            if (leader && alive) ptx::bulk_wait_group_read0();
+            ptx::named_barrier(1, 128);
+            if (alive) {
+#pragma unroll 1
+                for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                    uint32_t r[32];
+                    ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + chunk * 32, r);
+                    ptx::tmem_ld_wait();
+                    if (chunk == BN / 32 - 1) {
+                        // the accumulator is in registers: the next tile may start
+                        ptx::tc_fence_before();
+                        ptx::mbar_arrive(bar_tmem_empty);
+                    }
+                    // 32 columns = 64 bytes = four 16-byte units of a 128-byte
+                    // row of column group chunk/2, swizzled by row % 8
+                    uint8_t* grp = stage_out + (chunk >> 1) * (kBM * 128) + row * 128;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[8 * u + 2 * e]),
+                                                                     __uint_as_float(r[8 * u + 2 * e + 1]));
+                            w[e] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        const int unit = ((chunk & 1) * 4 + u) ^ (row & 7);
+                        *reinterpret_cast<uint4*>(grp + unit * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
+                ptx::fence_proxy_async_smem();
+            }
+            ptx::named_barrier(1, 128);
+            if (leader && alive) {
+#pragma unroll
+                for (int g = 0; g < BN / 64; ++g)
+                    ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, mb * kBM, stage_addr + g * (kBM * 128));
+                ptx::bulk_commit_group();
+            }
+        }
+        if (leader) ptx::bulk_wait_group0();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int quarter = warp & 3;  // TMEM sub-partition this warp may access
@@ -330,6 +399,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// 2-D bf16 map over C (rows x cols, row pitch ld_bytes), box 64 x 128 with the
+// 128-byte swizzle of the epilogue's staging tile.
+int make_output_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int64_t ld_bytes) {
+    auto fn = encode_fn();
+    if (!fn) return fail(SW_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+    cuuint32_t box[2] = {64, (cuuint32_t)kBM};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SW_ERR_INVALID, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+    return SW_OK;
+}
+
 // 2-D uint8 map over rows x row_bytes (pitch ld), box 128 bytes x box_rows,
 // 128-byte swizzle (the canonical K-major layout of the UMMA descriptors).
 int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int64_t ld,
@@ -347,17 +432,23 @@ int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
     return SW_OK;
 }
 
-template <int FMT, int BN>
+template <int FMT, int BN, int kStages, bool kTmaEpi>
 int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t* b, int64_t ldb,
                 const uint8_t* sfb, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N,
                 int64_t K, int beta_one, cudaStream_t stream) {
-    using Cf = Cfg<FMT, BN>;
+    using Cf = Cfg<FMT, BN, kStages, kTmaEpi>;
     const int64_t row_bytes = FMT == SW_MX_E4M3 ? K : K / 2;
     CUtensorMap ma, mb;
     int rc = make_operand_map(&ma, a, M, row_bytes, lda, kBM);
     if (rc != SW_OK) return rc;
     rc = make_operand_map(&mb, b, N, row_bytes, ldb, BN);
     if (rc != SW_OK) return rc;
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    if (kTmaEpi) {
+        rc = make_output_map(&mc, c, M, N, ldc_m * 2);
+        if (rc != SW_OK) return rc;
+    }
     GemmArgs args;
     args.sfa = sfa;
     args.sfb = sfb;
@@ -371,19 +462,15 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.katoms = (int)((K / 32 + 3) / 4);
     args.beta_one = beta_one;
     args.out_bf16 = out_dtype == SW_OUT_BF16;
-    auto kernel = mx_gemm_kernel<FMT, BN>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
-                    "set gemm smem");
-        attr_set = true;
-    }
+    auto kernel = mx_gemm_kernel<FMT, BN, kStages, kTmaEpi>;
+    SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
+                "set gemm smem");
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t tiles = (M / kBM) * (N / BN);
     const int grid = (int)std::min<int64_t>(tiles, sms);
-    kernel<<<grid, kThreads, Cf::kSmemBytes, stream>>>(ma, mb, args);
+    kernel<<<grid, kThreads, Cf::kSmemBytes, stream>>>(ma, mb, mc, args);
     SW_LAUNCH_CHECK("mx_gemm launch");
     return SW_OK;
 }
@@ -417,18 +504,22 @@ extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, c
         return fail(SW_ERR_INVALID, "sw_mx_gemm: payload and scale planes must be 16-byte aligned");
     if (ldc_m < 1 || ldc_n < 1) return fail(SW_ERR_INVALID, "sw_mx_gemm: output pitches must be positive");
     cudaStream_t s = (cudaStream_t)stream;
+    // bf16 row-major results without accumulation take the staged TMA epilogue
+    // (3 mainloop stages + the 64 KiB staging tile); everything else stores
+    // straight from registers (4 stages).
+    const bool tma_epi = out_dtype == SW_OUT_BF16 && ldc_n == 1 && !beta_one && N % 256 == 0 &&
+                         (ldc_m * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
     int rc;
+#define SW_GEMM(F, BNV, ST, EPI) \
+    launch_gemm<F, BNV, ST, EPI>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K, beta_one, s)
     if (fmt_a == SW_MX_E4M3) {
-        rc = (N % 256 == 0) ? launch_gemm<SW_MX_E4M3, 256>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
-                                                            ldc_n, M, N, K, beta_one, s)
-                            : launch_gemm<SW_MX_E4M3, 128>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
-                                                            ldc_n, M, N, K, beta_one, s);
+        rc = tma_epi ? SW_GEMM(SW_MX_E4M3, 256, 3, true)
+                     : (N % 256 == 0 ? SW_GEMM(SW_MX_E4M3, 256, 4, false) : SW_GEMM(SW_MX_E4M3, 128, 4, false));
     } else {
-        rc = (N % 256 == 0) ? launch_gemm<SW_MX_E2M1, 256>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
-                                                            ldc_n, M, N, K, beta_one, s)
-                            : launch_gemm<SW_MX_E2M1, 128>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m,
-                                                            ldc_n, M, N, K, beta_one, s);
+        rc = tma_epi ? SW_GEMM(SW_MX_E2M1, 256, 3, true)
+                     : (N % 256 == 0 ? SW_GEMM(SW_MX_E2M1, 256, 4, false) : SW_GEMM(SW_MX_E2M1, 128, 4, false));
     }
+#undef SW_GEMM
     if (rc != SW_OK) return rc;
     return ok();
 }

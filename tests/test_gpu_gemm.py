@@ -119,3 +119,16 @@ def test_full_size_8192_sampled_rows(fmt):
     rows = np.random.default_rng(0).choice(M, size=64, replace=False)
     want = da[rows].astype(np.float64) @ db.astype(np.float64).T
     assert rel_frobenius(got[rows], want) <= (4e-3 if fmt == O.E2M1 else 1e-5)
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
+def test_staged_bf16_epilogue_rounds_the_fp32_result(fmt):
+    # bf16 row-major results go through the shared-memory staged TMA-store
+    # epilogue; they must be exactly the fp32 accumulator rounded to nearest even
+    torch = pytest.importorskip("torch")
+    M, N_, K = 512, 768, 1024
+    A, B, _, _ = operands(fmt, M, N_, K, seed=9)
+    f32 = run_gemm(fmt, A, B, M, N_, K)
+    b16 = run_gemm(fmt, A, B, M, N_, K, out_bf16=True)
+    want = torch.from_numpy(f32).to(torch.bfloat16).to(torch.float32).numpy()
+    np.testing.assert_array_equal(b16, want)
