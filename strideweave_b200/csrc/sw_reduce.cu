@@ -23,12 +23,20 @@
 //               of a CTA and over the CTAs of a thread-block cluster, whose
 //               partials meet in distributed shared memory (no scratch
 //               memory, no second launch).
+//   rows_affine - the reduced mode walks memory affinely per lane (one
+//               unit-stride run, or equal runs at a fixed stride): one warp
+//               per kept ordinal, pointer increments only, no index math.
+//   cols_affine - the kept mode is unit-stride and the reduced mode is one
+//               leaf: CTAs own 128 kept ordinals and a slice of the fibre;
+//               slices meet in a small scratch buffer (at most SMs x 4 x 128
+//               partials), folded by the last CTA of each column block.
 //   gather    - anything else: one warp per kept ordinal, scalar loads.
 #include <cooperative_groups.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "sw_common.cuh"
@@ -550,22 +558,45 @@ __global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const f
     }
 }
 
-// Column walk: kept leaf 0 is unit-stride; the reduced mode is one leaf
-// (extent n_red, stride `stride`, ordinal weight `weight`).  A CTA owns 128
-// kept ordinals (32 lanes x 4); its warps and the CTAs of its cluster split
-// the fibre, and the partials meet in distributed shared memory.
 constexpr int kColsAffThreads = 256;
 constexpr int kColsAffWarps = kColsAffThreads / 32;
+constexpr int64_t kMaxColSlices = 256;  // slices of a split column walk
+
+// Column walk: kept leaf 0 is unit-stride; the reduced mode is one leaf
+// (extent n_red, stride `stride`, ordinal weight `weight`).  CTA (bx, by)
+// owns 128 kept ordinals (32 lanes x 4) and slice `by` of the gridDim.y
+// slices of the fibre; its 8 warps split the slice.  With more than one
+// slice every CTA leaves its 128 partials in scratch memory ([slice][kept]),
+// and the last CTA of the column block to finish folds them in slice order.
+// A counter per column block says which CTA is last; that CTA puts it back
+// to zero, so the counters are zero between launches.  No CTA waits for
+// another: the early ones simply exit.
+template <class Op>
+__device__ __forceinline__ typename Op::S load_partial(const typename Op::S* p);
+template <>
+__device__ __forceinline__ SumOp::S load_partial<SumOp>(const SumOp::S* p) {
+    return {__ldcg(&p->v)};
+}
+template <>
+__device__ __forceinline__ MaxOp::S load_partial<MaxOp>(const MaxOp::S* p) {
+    return {__ldcg(&p->v), (int64_t)__ldcg(reinterpret_cast<const long long*>(&p->j))};
+}
+template <>
+__device__ __forceinline__ ArgmaxOp::S load_partial<ArgmaxOp>(const ArgmaxOp::S* p) {
+    return {__ldcg(&p->v), (int64_t)__ldcg(reinterpret_cast<const long long*>(&p->j))};
+}
 
 template <class Op, bool kSwz, class Ord>
 __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const float* __restrict__ x, DevPlan p,
-                                                                         int64_t stride, int64_t weight, void* out) {
+                                                                         int64_t stride, int64_t weight, void* out,
+                                                                         typename Op::S* partials,
+                                                                         unsigned* counters) {
     __shared__ typename Op::S part[kColsAffWarps][32][4];
-    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ unsigned s_last;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int splits = (int)cluster.num_blocks();
-    const int split = (int)cluster.block_rank();
+    const int splits = (int)gridDim.y;
+    const int split = (int)blockIdx.y;
     const int64_t kv = int64_t(blockIdx.x) * 32 + lane;
     const bool live_col = kv < (p.n_kept >> 2);
     const int64_t col = live_col ? p.offset + kept_offset(p.kept, kv * 4) : 0;
@@ -593,27 +624,40 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
 #pragma unroll
     for (int e = 0; e < 4; ++e) part[warp][lane][e] = acc[e];
     __syncthreads();
-    // warps 0..3 fold component `warp` of the 8 warps' partials
+    // warps 0..3 fold component `warp` (kept ordinal kv*4 + warp) of the 8 warps' partials
+    typename Op::S v = Op::identity();
+    const int64_t kept_i = kv * 4 + warp;
     if (warp < 4) {
-        typename Op::S v = part[0][lane][warp];
+        v = part[0][lane][warp];
 #pragma unroll
         for (int w = 1; w < kColsAffWarps; ++w) Op::merge(v, part[w][lane][warp]);
-        part[0][lane][warp] = v;
     }
-    cluster.sync();
-    // rank 0: warps 0..3 read every peer's partial at once, then fold
-    if (split == 0 && warp < 4 && live_col) {
-        typename Op::S v = part[0][lane][warp];
-        typename Op::S peer[7];
-#pragma unroll
-        for (int r = 1; r < 8; ++r)
-            if (r < splits) peer[r - 1] = cluster.map_shared_rank(part, r)[0][lane][warp];
-#pragma unroll
-        for (int r = 1; r < 8; ++r)
-            if (r < splits) Op::merge(v, peer[r - 1]);
-        store_result<Op>(out, kv * 4 + warp, v);
+    if (splits == 1) {
+        if (warp < 4 && live_col) store_result<Op>(out, kept_i, v);
+        return;
     }
-    cluster.sync();
+    if (warp < 4 && live_col) partials[int64_t(split) * p.n_kept + kept_i] = v;
+    __threadfence();  // this CTA's partials are visible before its ticket is
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&counters[blockIdx.x], 1u) == unsigned(splits - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();  // every other slice's partials are visible from here on
+    if (warp < 4 && live_col) {
+        // eight independent loads in flight before each round of merges
+        typename Op::S r = load_partial<Op>(partials + kept_i);
+        for (int s0 = 1; s0 < splits; s0 += 8) {
+            typename Op::S q[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (s0 + u < splits) q[u] = load_partial<Op>(partials + int64_t(s0 + u) * p.n_kept + kept_i);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (s0 + u < splits) Op::merge(r, q[u]);
+        }
+        store_result<Op>(out, kept_i, r);
+    }
+    if (threadIdx.x == 0) counters[blockIdx.x] = 0;
 }
 
 // ---- gather ------------------------------------------------------------------
@@ -751,6 +795,54 @@ int swizzle_top_bit(const Swz& s) {
     return top;
 }
 
+// Scratch memory of the split column walk: one buffer per (device, stream),
+// so the launches of one stream use it in order.  It comes from the device's
+// stream-ordered pool on first use (and is regrown, the old buffer released
+// after the stream's earlier work, when a launch needs more); its counters
+// are zeroed on the same stream and are zero again after every launch.
+struct ScratchSlot {
+    int dev;
+    cudaStream_t stream;
+    void* ptr;
+    size_t bytes;
+};
+std::mutex g_scratch_mu;
+std::vector<ScratchSlot>& scratch_slots() {
+    static std::vector<ScratchSlot> slots;
+    return slots;
+}
+
+int reduce_scratch(size_t need, cudaStream_t stream, void** out) {
+    int dev = 0;
+    SW_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    ScratchSlot* slot = nullptr;
+    for (auto& e : scratch_slots())
+        if (e.dev == dev && e.stream == stream) slot = &e;
+    if (slot && slot->bytes >= need) {
+        *out = slot->ptr;
+        return SW_OK;
+    }
+    const size_t bytes = (need + (size_t(1) << 20) - 1) & ~((size_t(1) << 20) - 1);  // whole MiB
+    void* ptr = nullptr;
+    cudaError_t err = cudaMallocAsync(&ptr, bytes, stream);
+    if (err == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return fail(SW_ERR_NOMEM, "sw_reduce_f32: out of device memory for %zu bytes of scratch", bytes);
+    }
+    SW_CUDA_TRY(err, "cudaMallocAsync (reduction scratch)");
+    SW_CUDA_TRY(cudaMemsetAsync(ptr, 0, bytes, stream), "zeroing reduction scratch");
+    if (slot) {
+        SW_CUDA_TRY(cudaFreeAsync(slot->ptr, stream), "cudaFreeAsync (reduction scratch)");
+        slot->ptr = ptr;
+        slot->bytes = bytes;
+    } else {
+        scratch_slots().push_back({dev, stream, ptr, bytes});
+    }
+    *out = ptr;
+    return SW_OK;
+}
+
 struct Launch {
     int kernel = 2;  // 0 rows_vec, 1 cols_vec, 2 gather, 3 rows_affine, 4 cols_affine
     int splits = 1;
@@ -780,19 +872,21 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         reduce_rows_affine<Op, kSwz, Ord><<<(unsigned)blocks, kRowsAffThreads, 0, stream>>>(x, p, L.rw, rpw, out);
         return SW_OK;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((p.n_kept / 4 + 31) / 32), (unsigned)L.splits, 1);
-    cfg.blockDim = dim3(kColsAffThreads, 1, 1);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = (unsigned)L.splits;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, reduce_cols_affine<Op, kSwz, Ord>, x, p, L.cstride, L.cweight, out);
-    if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_affine launch");
+    // split column walk: more than one slice needs scratch for the partials
+    const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
+    typename Op::S* partials = nullptr;
+    unsigned* counters = nullptr;
+    if (L.splits > 1) {
+        const size_t cbytes = (size_t(col_blocks) * sizeof(unsigned) + 255) & ~size_t(255);
+        const size_t need = cbytes + size_t(L.splits) * size_t(p.n_kept) * sizeof(typename Op::S);
+        void* base = nullptr;
+        const int rc = reduce_scratch(need, stream, &base);
+        if (rc != SW_OK) return rc;
+        counters = static_cast<unsigned*>(base);
+        partials = reinterpret_cast<typename Op::S*>(static_cast<char*>(base) + cbytes);
+    }
+    reduce_cols_affine<Op, kSwz, Ord><<<dim3((unsigned)col_blocks, (unsigned)L.splits), kColsAffThreads, 0, stream>>>(
+        x, p, L.cstride, L.cweight, out, partials, counters);
     return SW_OK;
 }
 
@@ -875,13 +969,16 @@ Launch choose(DevPlan& p, int kind, bool aligned) {
         const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
         // every CTA resident at once (4 per SM): no second, partial wave
         const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * 4 / col_blocks);
-        L.splits = (int)std::max<int64_t>(1, std::min<int64_t>({want, 8, p.n_red}));
         if (p.red.rank == 1 && swizzle_commutes(p.swz, int64_t(kColsAffWarps) * p.red.stride[0])) {
+            // slices meet in scratch memory: no cap from the cluster size
             L.kernel = 4;
+            L.splits = (int)std::max<int64_t>(1, std::min<int64_t>({want, kMaxColSlices, p.n_red}));
             L.cstride = p.red.stride[0];
             L.cweight = p.red.weight[0];
         } else {
+            // slices meet in distributed shared memory: at most one portable cluster
             L.kernel = 1;
+            L.splits = (int)std::max<int64_t>(1, std::min<int64_t>({want, 8, p.n_red}));
         }
         return L;
     }

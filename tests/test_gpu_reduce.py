@@ -164,3 +164,18 @@ def test_empty_kept_mode_is_a_no_op():
     x = to_device(np.zeros(16, dtype=np.float32))
     out = empty(16)
     kernels.reduce_f32("reduce_sum", x.ptr, 16, 0, [(0, 1)], [(4, 4)], out.ptr)
+
+
+@pytest.mark.parametrize("n_kept,n_red", [(1000, 4099), (8192, 517), (64, 100000)])
+def test_split_column_walk_repeats_and_regrows_its_scratch(n_kept, n_red):
+    # transposed storage: the fibre is split into slices whose partials meet in
+    # scratch memory; each launch must leave its counters at zero for the next
+    # one, and a kind with wider partials regrows the buffer
+    rng = np.random.default_rng(n_kept + n_red)
+    x = rng.uniform(-1, 1, size=(n_kept, n_red)).astype(np.float32)
+    x[::7, (np.arange(0, n_kept, 7) * 13) % n_red] = 2.0      # ties across slices
+    x[::7, (np.arange(0, n_kept, 7) * 29 + 1) % n_red] = 2.0
+    storage = x.T.ravel().copy()
+    kept, reduced = [(n_kept, 1)], [(n_red, n_kept)]
+    for kind in ("sum", "max", "argmax", "sum", "argmax", "max"):
+        check(kind, gpu_reduce(kind, storage, 0, kept, reduced), O.reduce(kind, storage, 0, kept, reduced))
