@@ -118,6 +118,23 @@ typedef struct sw_reduce_plan {
 int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
                   void* out, void* stream);
 
+/* sw_reduce_f32 without any device allocation.  This entry point has no
+ * counterpart in the reference: it exists for callers that cannot let a
+ * library allocate device memory, such as an engine that has already divided
+ * the whole device among its own pools, or a process whose memory budget is
+ * fixed and audited per allocation.  Same plans, results and errors as
+ * sw_reduce_f32, except that the scratch of a split column reduction lives in
+ * a 2 MiB array compiled into the library, which every GPU that loads the
+ * library keeps until the process exits; a reduction needing more scratch
+ * (only possible on devices with more than 255 SMs) fails with
+ * SW_ERR_UNSUPPORTED.  The first call on each device looks up the array's
+ * device address, so make that first call before any stream capture.  All
+ * calls share the one array and each clears its counters on its own stream:
+ * calls that overlap on the GPU (other streams, other host threads) race and
+ * produce wrong results, so order them on one stream. */
+int sw_reduce_f32_noalloc(const sw_reduce_plan* plan, const float* x, int64_t x_size,
+                          void* out, void* stream);
+
 /* Gradient of sw_reduce_f32 with respect to its input (the VJP of
  * CpuReduceSumOperation::backward, ops/reduce_sum.cpp:120-150, and of
  * CpuFloatReductionOperation<Kind>::backward for reduce_max,

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_stream_synchronize": (c_int, [c_void_p]),
     "sw_device_status": (c_int, [POINTER(c_int)]),
     "sw_reduce_f32": (c_int, [POINTER(ReducePlan), c_void_p, c_int64, c_void_p, c_void_p]),
+    "sw_reduce_f32_noalloc": (c_int, [POINTER(ReducePlan), c_void_p, c_int64, c_void_p, c_void_p]),
     "sw_reduce_backward_f32": (
         c_int, [POINTER(ReducePlan), c_void_p, c_int64, c_void_p, c_void_p, POINTER(ReducePlan), c_int64, c_void_p],
     ),

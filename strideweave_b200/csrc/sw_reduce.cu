@@ -795,6 +795,14 @@ int swizzle_top_bit(const Swz& s) {
     return top;
 }
 
+// Where the split column walk takes its scratch from: the library's
+// per-(device, stream) buffer (base == nullptr), or a fixed region the caller
+// of the entry point chose (base, bytes) whose counters are cleared per launch.
+struct ScratchSource {
+    void* base = nullptr;
+    size_t bytes = 0;
+};
+
 // Scratch memory of the split column walk: one buffer per (device, stream),
 // so the launches of one stream use it in order.  It comes from the device's
 // stream-ordered pool on first use (and is regrown, the old buffer released
@@ -852,7 +860,8 @@ struct Launch {
 };
 
 template <class Op, bool kSwz, class Ord>
-int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
+int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream,
+                  const ScratchSource& src) {
     if (L.kernel == 3) {
         // every warp resident at once, each with the same number of rows
         static int per_sm = 0;  // one query per kernel instantiation
@@ -880,8 +889,19 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         const size_t cbytes = (size_t(col_blocks) * sizeof(unsigned) + 255) & ~size_t(255);
         const size_t need = cbytes + size_t(L.splits) * size_t(p.n_kept) * sizeof(typename Op::S);
         void* base = nullptr;
-        const int rc = reduce_scratch(need, stream, &base);
-        if (rc != SW_OK) return rc;
+        if (src.base) {
+            if (need > src.bytes)
+                return fail(SW_ERR_UNSUPPORTED,
+                            "sw_reduce_f32_noalloc: this reduction needs %zu bytes of scratch; the static scratch "
+                            "holds %zu",
+                            need, src.bytes);
+            base = src.base;
+            // the region keeps the previous call's contents: clear the counters
+            SW_CUDA_TRY(cudaMemsetAsync(base, 0, cbytes, stream), "clearing the static scratch counters");
+        } else {
+            const int rc = reduce_scratch(need, stream, &base);
+            if (rc != SW_OK) return rc;
+        }
         counters = static_cast<unsigned*>(base);
         partials = reinterpret_cast<typename Op::S*>(static_cast<char*>(base) + cbytes);
     }
@@ -891,17 +911,19 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
 }
 
 template <class Op, class Ord>
-int launch_affine_swz(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
-    return p.swz.rank > 0 ? launch_affine<Op, true, Ord>(x, p, L, out, stream)
-                          : launch_affine<Op, false, Ord>(x, p, L, out, stream);
+int launch_affine_swz(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream,
+                      const ScratchSource& src) {
+    return p.swz.rank > 0 ? launch_affine<Op, true, Ord>(x, p, L, out, stream, src)
+                          : launch_affine<Op, false, Ord>(x, p, L, out, stream, src);
 }
 
 template <class Op>
-int launch_for(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream) {
+int launch_for(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream,
+               const ScratchSource& src) {
     if (L.kernel == 3 || L.kernel == 4) {
         // 32-bit ordinals whenever every ordinal of the fibre fits
-        int rc = p.n_red < (int64_t(1) << 30) ? launch_affine_swz<Op, int32_t>(x, p, L, out, stream)
-                                              : launch_affine_swz<Op, int64_t>(x, p, L, out, stream);
+        int rc = p.n_red < (int64_t(1) << 30) ? launch_affine_swz<Op, int32_t>(x, p, L, out, stream, src)
+                                              : launch_affine_swz<Op, int64_t>(x, p, L, out, stream, src);
         if (rc != SW_OK) return rc;
     } else if (L.kernel == 0) {
         const int64_t blocks = std::min<int64_t>((p.n_kept + 7) / 8, int64_t(sm_count()) * 8);
@@ -988,9 +1010,13 @@ Launch choose(DevPlan& p, int kind, bool aligned) {
 }  // namespace
 }  // namespace sw
 
-extern "C" int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
-                             void* out, void* stream) {
-    using namespace sw;
+namespace sw {
+namespace {
+
+// Validates and lowers a plan, then launches; `src` says where the split
+// column walk takes its scratch from.
+int reduce_entry(const sw_reduce_plan* plan, const float* x, int64_t x_size, void* out, void* stream,
+                 const ScratchSource& src) {
     if (!plan || !out) return fail(SW_ERR_INVALID, "sw_reduce_f32: null plan or output");
     if (plan->kind < SW_REDUCE_SUM || plan->kind > SW_REDUCE_ARGMAX)
         return fail(SW_ERR_INVALID, "sw_reduce_f32: unknown reduction kind %d", plan->kind);
@@ -1052,10 +1078,69 @@ extern "C" int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t
     cudaStream_t s = (cudaStream_t)stream;
     int rc;
     switch (plan->kind) {
-        case SW_REDUCE_SUM: rc = launch_for<SumOp>(x, p, L, out, s); break;
-        case SW_REDUCE_MAX: rc = launch_for<MaxOp>(x, p, L, out, s); break;
-        default: rc = launch_for<ArgmaxOp>(x, p, L, out, s); break;
+        case SW_REDUCE_SUM: rc = launch_for<SumOp>(x, p, L, out, s, src); break;
+        case SW_REDUCE_MAX: rc = launch_for<MaxOp>(x, p, L, out, s, src); break;
+        default: rc = launch_for<ArgmaxOp>(x, p, L, out, s, src); break;
     }
     if (rc != SW_OK) return rc;
     return ok();
+}
+
+}  // namespace
+}  // namespace sw
+
+extern "C" int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
+                             void* out, void* stream) {
+    return sw::reduce_entry(plan, x, x_size, out, stream, sw::ScratchSource{});
+}
+
+// ---- a reduction that allocates nothing -----------------------------------------
+//
+// sw_reduce_f32 may reserve a small scratch buffer from the device's memory pool
+// the first time a stream runs a split column walk.  Some callers cannot let a
+// library allocate: an engine that has already divided all of the device's
+// memory among its own pools, or a process whose device-memory budget is fixed
+// and audited allocation by allocation.  sw_reduce_f32_noalloc serves them with
+// the split walk's scratch in a fixed array compiled into this library.
+
+namespace {
+
+// Every GPU that loads the library holds these 2 MiB until the process exits.
+// A split column walk needs at most SMs x 4 x 128 partials of 16 bytes plus its
+// counters, so this covers every plan on devices with up to 255 SMs.
+constexpr size_t kStaticScratchBytes = size_t(2) << 20;
+constexpr int kMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// The device address of g_static_scratch on the current device.  In host code
+// the array's name stands for a host-side shadow, never a device address, so
+// it is looked up once per device with that device current.
+int static_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = 0;
+    SW_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices)
+        return sw::fail(SW_ERR_UNSUPPORTED, "sw_reduce_f32_noalloc: device ordinal %d above %d", dev, kMaxDevices - 1);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        SW_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch), "cudaGetSymbolAddress (static reduction scratch)");
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return SW_OK;
+}
+
+}  // namespace
+
+extern "C" int sw_reduce_f32_noalloc(const sw_reduce_plan* plan, const float* x, int64_t x_size, void* out,
+                                     void* stream) {
+    void* base = nullptr;
+    const int rc = static_scratch(&base);
+    if (rc != SW_OK) return rc;
+    sw::ScratchSource src;
+    src.base = base;
+    src.bytes = kStaticScratchBytes;
+    return sw::reduce_entry(plan, x, x_size, out, stream, src);
 }
