@@ -614,7 +614,10 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
         w.iters = int((j1 - j0 + kColsAffWarps - 1) / kColsAffWarps);
         FastFold<Op, Ord> f;
         const float* ptr = x + phys<kSwz>(p.swz, col + w.off0);
-        if (fast_walk<Op, Ord, 8>(ptr, w.doff, w.iters, f)) {
+        // argmax carries an ordinal per component: a shallower unroll keeps
+        // it inside the register budget
+        constexpr int kU = Op::kKind == Kind::kArgmax ? 4 : 8;
+        if (fast_walk<Op, Ord, kU>(ptr, w.doff, w.iters, f)) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[e] = f.component(e, w.ord0, w.dord, Ord(0));
         } else {
@@ -644,15 +647,17 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
     if (!s_last) return;
     __threadfence();  // every other slice's partials are visible from here on
     if (warp < 4 && live_col) {
-        // eight independent loads in flight before each round of merges
-        typename Op::S r = load_partial<Op>(partials + kept_i);
-        for (int s0 = 1; s0 < splits; s0 += 8) {
-            typename Op::S q[8];
+        // a batch of independent loads in flight before each round of merges:
+        // the usual slice counts (about SMs x 4 / column blocks) take one round trip
+        constexpr int kB = sizeof(typename Op::S) > 4 ? 10 : 16;
+        typename Op::S r = Op::identity();
+        for (int s0 = 0; s0 < splits; s0 += kB) {
+            typename Op::S q[kB];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < kB; ++u)
                 if (s0 + u < splits) q[u] = load_partial<Op>(partials + int64_t(s0 + u) * p.n_kept + kept_i);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < kB; ++u)
                 if (s0 + u < splits) Op::merge(r, q[u]);
         }
         store_result<Op>(out, kept_i, r);
