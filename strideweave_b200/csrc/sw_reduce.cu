@@ -452,6 +452,15 @@ struct FastFold {
     }
 };
 
+// Programmatic dependent launch: a grid launched with the attribute may be
+// scheduled while the previous grid on its stream drains.  It waits for that
+// grid (and its memory) before touching global memory, then lets the next
+// grid begin launching.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <bool kSwz>
 __device__ __forceinline__ int64_t phys(const Swz& s, int64_t f) {
     if constexpr (kSwz) return swizzle(s, f);
@@ -518,6 +527,7 @@ constexpr int kRowsAffWarps = kRowsAffThreads / 32;
 template <class Op, bool kSwz, class Ord>
 __global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const float* __restrict__ x, DevPlan p,
                                                                          RowWalk rw, int64_t rpw, void* out) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nv0 = rw.run >> 2;
@@ -593,6 +603,7 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
                                                                          unsigned* counters) {
     __shared__ typename Op::S part[kColsAffWarps][32][4];
     __shared__ unsigned s_last;
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int splits = (int)gridDim.y;
@@ -800,6 +811,22 @@ int swizzle_top_bit(const Swz& s) {
     return top;
 }
 
+// Launches `kernel` with programmatic stream serialization (see pdl_enter).
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Where the split column walk takes its scratch from: the library's
 // per-(device, stream) buffer (base == nullptr), or a fixed region the caller
 // of the entry point chose (base, bytes) whose counters are cleared per launch.
@@ -883,7 +910,9 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         const int64_t rpw = (p.n_kept + capacity - 1) / capacity;
         const int64_t warps = (p.n_kept + rpw - 1) / rpw;
         const int64_t blocks = (warps + kRowsAffWarps - 1) / kRowsAffWarps;
-        reduce_rows_affine<Op, kSwz, Ord><<<(unsigned)blocks, kRowsAffThreads, 0, stream>>>(x, p, L.rw, rpw, out);
+        const cudaError_t err = launch_pdl(reduce_rows_affine<Op, kSwz, Ord>, dim3((unsigned)blocks),
+                                           dim3(kRowsAffThreads), stream, x, p, L.rw, rpw, out);
+        if (err != cudaSuccess) return cuda_fail(err, "reduce_rows_affine launch");
         return SW_OK;
     }
     // split column walk: more than one slice needs scratch for the partials
@@ -910,8 +939,10 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         counters = static_cast<unsigned*>(base);
         partials = reinterpret_cast<typename Op::S*>(static_cast<char*>(base) + cbytes);
     }
-    reduce_cols_affine<Op, kSwz, Ord><<<dim3((unsigned)col_blocks, (unsigned)L.splits), kColsAffThreads, 0, stream>>>(
-        x, p, L.cstride, L.cweight, out, partials, counters);
+    const cudaError_t err = launch_pdl(reduce_cols_affine<Op, kSwz, Ord>, dim3((unsigned)col_blocks, (unsigned)L.splits),
+                                       dim3(kColsAffThreads), stream, x, p, L.cstride, L.cweight, out, partials,
+                                       counters);
+    if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_affine launch");
     return SW_OK;
 }
 
