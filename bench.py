@@ -253,7 +253,7 @@ def main() -> None:
     ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed busy time under the clock sampler before the timed region")
-    ap.add_argument("--profile-case", choices=["reduce", "mxfp8", "mxfp4", "mlp"],
+    ap.add_argument("--profile-case", choices=["reduce", "quantize", "mxfp8", "mxfp4", "mlp"],
                     help="run a short, fixed sequence of launches for ncu and exit (no timing)")
     ap.add_argument("--reps", type=int, default=2, help="rounds of launches of --profile-case")
     args = ap.parse_args()
@@ -407,9 +407,11 @@ def main() -> None:
 
     # -------- contractions (configs 1 and 3) on this device --------
     contraction = None
+    quantize = None
     sharded = None
     mlp = None
     if not args.no_gemm:
+        quantize = bench_quantize(torch, N, kernels, s, stream)
         contraction = bench_gemm(torch, N, kernels, s, stream)
         # config 5 at this world size (strong scaling of a fixed contraction)
         sharded = {m: bench_sharded(torch, dist, N, kernels, m, world, rank) for m in ("m", "k")}
@@ -449,6 +451,8 @@ def main() -> None:
             "gpu_launches": 9 * args.steps,
             "clocks": clocks.summary(),
         }
+        if quantize:
+            line["quantize"] = quantize
         if contraction:
             line["contraction"] = contraction
         if sharded:
@@ -499,6 +503,46 @@ def bench_gemm(torch, N, kernels, s, stream) -> dict:
                      "frac_of_clock_adjusted": round(tflops / clock_adj, 4),
                      "config": "M=N=K=8192, A~N(0,1), B~N(0,0.02), bf16 C"}
         del pa, pb, sa, sb, c
+    N.raise_device_status()
+    return out
+
+
+def bench_quantize(torch, N, kernels, s, stream) -> dict:
+    """MX quantisation of a Float32 [8192 x 8192] operand (256 MiB read),
+    along rows (K-major source) and along strided columns (a K x N source
+    quantised along K), back to back over two inputs (512 MiB > L2).
+    Algorithmic bytes: the Float32 read plus the payload and TC128 scale
+    writes."""
+    rows = cols = 8192
+    rng = np.random.default_rng(7)
+    srcs = [torch.from_numpy(rng.standard_normal((rows, cols)).astype(np.float32)).cuda() for _ in range(2)]
+    peaks = load_peaks()
+    out = {}
+    for name, fmt in (("mxfp8", N.SW_MX_E4M3), ("mxfp4", N.SW_MX_E2M1)):
+        rb = kernels.mx_row_bytes(fmt, cols)
+        pay = N.DeviceBuffer(rows * rb)
+        sc = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, cols // 32))
+        moved = rows * cols * 4 + rows * rb + kernels.scale_bytes_tc128(rows, cols // 32)
+        for along, (ld_row, ld_col) in (("rows", (cols, 1)), ("strided_cols", (1, rows))):
+            def q(i):
+                kernels.mx_quantize(fmt, srcs[i % 2].data_ptr(), rows, cols, ld_row, ld_col, pay.ptr, rb, sc.ptr,
+                                    stream=s)
+            for i in range(4):
+                q(i)
+            torch.cuda.synchronize()
+            reps = 20
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(reps):
+                q(i)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            gbs = moved / (us * 1e3)
+            out[f"{name}_{along}"] = {"us": round(us, 2), "gbs": round(gbs, 1),
+                                      "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                                      "bytes": moved}
+        del pay, sc
     N.raise_device_status()
     return out
 
@@ -607,7 +651,9 @@ def profile_case(case: str, reps: int) -> None:
     """A fixed, small sequence of launches for an ncu capture.
 
     reduce: the three layouts of X[8192 x 4096] x (sum, max, argmax), `reps`
-    rounds (9 launches per round).  mxfp8 / mxfp4: quantise two 8192 x 8192
+    rounds (9 launches per round).  quantize: MXFP8 then MXFP4 of a Float32
+    [8192 x 8192] along rows and along strided columns, `reps` rounds (4
+    launches per round).  mxfp8 / mxfp4: quantise two 8192 x 8192
     operands, then `reps` contractions at M = N = K = 8192 (bf16 C).
     """
     from strideweave_b200 import _native as N
@@ -618,6 +664,21 @@ def profile_case(case: str, reps: int) -> None:
         import torch
 
         print(bench_mlp(torch, N, steps=reps, warmup=1))
+        return
+    if case == "quantize":
+        rows = cols = 8192
+        src = N.DeviceBuffer(rows * cols * 4)
+        src.upload(np.random.default_rng(7).standard_normal((rows, cols)).astype(np.float32))
+        for _ in range(reps):
+            for fmt in (N.SW_MX_E4M3, N.SW_MX_E2M1):
+                rb = kernels.mx_row_bytes(fmt, cols)
+                pay = N.DeviceBuffer(rows * rb)
+                sc = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, cols // 32))
+                for ld_row, ld_col in ((cols, 1), (1, rows)):
+                    kernels.mx_quantize(fmt, src.ptr, rows, cols, ld_row, ld_col, pay.ptr, rb, sc.ptr)
+                N.synchronize()
+        N.raise_device_status()
+        print("profile case quantize: ok")
         return
     if case == "reduce":
         x = np.random.default_rng(0).uniform(-1, 1, size=(R, C)).astype(np.float32)

@@ -75,69 +75,116 @@ __host__ __device__ __forceinline__ int64_t scale_offset(int layout, int64_t r, 
     return r * ld + kb;
 }
 
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+__device__ __forceinline__ float max_nan_abs(float m, float v) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(m), "f"(fabsf(v)));
+    return r;
+}
+
+// Byte offset of block (r, kb) in a scale plane, split into a per-row base and a
+// per-block step so that a walk along a row adds instead of recomputing.
+__device__ __forceinline__ int64_t scale_row_base(int layout, int64_t r, int64_t kblocks, int64_t ld) {
+    if (layout == SW_SCALES_TC128) return (r >> 7) * ((kblocks + 3) >> 2) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
+    return r * ld;
+}
+__device__ __forceinline__ int64_t scale_block_step(int layout, int64_t kb) {
+    return layout == SW_SCALES_TC128 ? (kb >> 2) * 512 + (kb & 3) : kb;
+}
+
 // ---- quantise: blocks along a unit-stride axis --------------------------------
-// Four threads per 32-block, eight elements each (two 16-byte loads).  A warp
-// covers eight consecutive blocks of one row.
+// A warp walks a segment of up to 2048 elements of one row, 256 (eight blocks)
+// per step: four lanes per block, eight elements per lane (two 16-byte loads).
+// Row and scale addresses are set up once per segment and then advanced.
+constexpr int64_t kQuantSegment = 2048;
+
 template <int FMT>
 __global__ void __launch_bounds__(256) quantize_rows(const float* __restrict__ x, int64_t rows, int64_t cols,
                                                      int64_t ldx, uint8_t* __restrict__ payload, int64_t ldp,
                                                      uint8_t* __restrict__ scales, int layout, int64_t lds) {
     const int64_t kblocks = (cols + 31) / 32;
-    const int64_t total = rows * kblocks * 4;  // one work item per thread
-    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-    for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < total; t += stride) {
-        const bool live = t < total;
-        const int64_t blk = t >> 2;
-        const int part = int(t & 3);
-        const int64_t r = live ? blk / kblocks : 0;
-        const int64_t kb = live ? blk % kblocks : 0;
-        const int64_t c0 = kb * 32 + part * 8;
-        float v[8];
-        const float* src = x + r * ldx + c0;
-        if (live && c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
-            const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
-            const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    const int64_t segs = (cols + kQuantSegment - 1) / kQuantSegment;
+    const int64_t units = rows * segs;
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t u = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+        int64_t r, sg;
+        if (units <= int64_t(0x7FFFFFFF)) {
+            const uint32_t uu = uint32_t(u), g = uint32_t(segs);
+            const uint32_t q = uu / g;
+            r = q;
+            sg = uu - q * g;
         } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = (live && c0 + i < cols) ? src[i] : 0.0f;
+            r = u / segs;
+            sg = u - r * segs;
         }
-        uint32_t amax = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = max(amax, __float_as_uint(v[i]) & 0x7FFFFFFFu);
-        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        if (!live) continue;
-        uint8_t sc;
-        float inv;
-        bool special;
-        block_scale<FMT>(amax, sc, inv, special);
-        if (part == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
-        float q[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) q[i] = special ? 0.0f : __fmul_rn(v[i], inv);
-        if (FMT == SW_MX_E4M3) {
-            uint8_t* dst = payload + r * ldp + c0;
-            const uint32_t lo = e4m3x4(q[0], q[1], q[2], q[3]);
-            const uint32_t hi = e4m3x4(q[4], q[5], q[6], q[7]);
-            if (c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 7) == 0)) {
-                *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+        const int64_t e_begin = sg * kQuantSegment;
+        const int64_t e_end = min(cols, e_begin + kQuantSegment);
+        const float* src = x + r * ldx + e_begin + lane * 8;
+        uint8_t* dst = payload + r * ldp + (FMT == SW_MX_E4M3 ? e_begin + lane * 8 : (e_begin + lane * 8) / 2);
+        const int64_t srow = scale_row_base(layout, r, kblocks, lds);
+        const bool row_aligned = ((reinterpret_cast<uintptr_t>(x + r * ldx) & 15) == 0);
+        for (int64_t e0 = e_begin; e0 < e_end; e0 += 256, src += 256, dst += (FMT == SW_MX_E4M3 ? 256 : 128)) {
+            const int64_t c0 = e0 + lane * 8;
+            const int64_t kb = (e0 >> 5) + (lane >> 2);
+            float v[8];
+            const bool full = row_aligned && e0 + 256 <= e_end;
+            if (full) {
+                const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+                const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
             } else {
-                for (int i = 0; i < 8 && c0 + i < cols; ++i)
-                    dst[i] = uint8_t(((i < 4 ? lo : hi) >> (8 * (i & 3))) & 0xFF);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = c0 + i < cols ? src[i] : 0.0f;
             }
-        } else {
-            uint8_t* dst = payload + r * ldp + c0 / 2;
-            uint32_t packed = e2m1x8(q);
-            if (c0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(dst) & 3) == 0)) {
-                *reinterpret_cast<uint32_t*>(dst) = packed;
+            float m = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) m = max_nan_abs(m, v[i]);
+            m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            if (kb >= kblocks) continue;
+            uint8_t sc;
+            float inv;
+            bool special;
+            block_scale<FMT>(__float_as_uint(m), sc, inv, special);
+            if ((lane & 3) == 0) scales[srow + scale_block_step(layout, kb)] = sc;
+            uint32_t w0, w1;
+            if (!special) {
+                float q[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(v[i], inv);
+                if (FMT == SW_MX_E4M3) {
+                    w0 = e4m3x4(q[0], q[1], q[2], q[3]);
+                    w1 = e4m3x4(q[4], q[5], q[6], q[7]);
+                } else {
+                    w0 = e2m1x8(q);
+                    w1 = 0;
+                }
             } else {
-                // ragged tail: keep the nibbles beyond `cols` as they were
-                for (int i = 0; i < 8 && c0 + i < cols; i += 2) {
-                    const uint8_t byte = uint8_t((packed >> (4 * i)) & 0xFF);
-                    if (c0 + i + 1 < cols) dst[i / 2] = byte;
-                    else dst[i / 2] = uint8_t((dst[i / 2] & 0xF0) | (byte & 0x0F));
+                w0 = w1 = 0;  // a NaN/Inf block: scale 0xFF, payload codes 0
+            }
+            if (FMT == SW_MX_E4M3) {
+                if (full && ((reinterpret_cast<uintptr_t>(dst) & 7) == 0)) {
+                    *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+                } else {
+                    for (int i = 0; i < 8 && c0 + i < cols; ++i) dst[i] = uint8_t(((i < 4 ? w0 : w1) >> (8 * (i & 3))) & 0xFF);
+                }
+            } else {
+                if (full && ((reinterpret_cast<uintptr_t>(dst) & 3) == 0)) {
+                    *reinterpret_cast<uint32_t*>(dst) = w0;
+                } else {
+                    // ragged tail: keep the nibbles beyond `cols` as they were
+                    for (int i = 0; i < 8 && c0 + i < cols; i += 2) {
+                        const uint8_t byte = uint8_t((w0 >> (4 * i)) & 0xFF);
+                        if (c0 + i + 1 < cols) dst[i / 2] = byte;
+                        else dst[i / 2] = uint8_t((dst[i / 2] & 0xF0) | (byte & 0x0F));
+                    }
                 }
             }
         }
@@ -203,6 +250,100 @@ __global__ void __launch_bounds__(256) quantize_strided(const float* __restrict_
     }
 }
 
+// Scale, payload and store of one block of `len` (<= 32) values of row r.
+template <int FMT>
+__device__ __forceinline__ void quantize_block32(float (&v)[32], int len, int64_t r, int64_t kb, int64_t kblocks,
+                                                 uint8_t* __restrict__ payload, int64_t ldp,
+                                                 uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) m = max_nan_abs(m, v[i]);
+    uint8_t sc;
+    float inv;
+    bool special;
+    block_scale<FMT>(__float_as_uint(m), sc, inv, special);
+    scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+    if (special) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.0f;  // a NaN/Inf block: payload codes 0
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], inv);
+    }
+    const int64_t c0 = kb * 32;
+    if (FMT == SW_MX_E4M3) {
+        uint8_t* dst = payload + r * ldp + c0;
+        uint32_t w[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) w[g] = e4m3x4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+        if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+            for (int c = 0; c < len; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+        }
+    } else {
+        uint8_t* dst = payload + r * ldp + c0 / 2;
+        uint32_t w[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) w[g] = e2m1x8(v + 8 * g);
+        if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+            for (int c = 0; c < len; c += 2) {
+                const uint8_t byte = uint8_t((w[c / 8] >> (4 * (c % 8))) & 0xFF);
+                if (c + 1 < len) dst[c / 2] = byte;
+                else dst[c / 2] = uint8_t((dst[c / 2] & 0xF0) | (byte & 0x0F));
+            }
+        }
+    }
+}
+
+// ---- quantise: blocks along a strided axis with unit row stride ---------------
+// (a K x N operand quantised along K, i.e. the blocks of each of N rows run down
+// a column).  A CTA stages a 32 (block) x 128 (row) tile through shared memory
+// with 16-byte loads along the contiguous rows, then each of its 128 threads
+// quantises one row's block from the tile.  Needs rows % 4 == 0, a 16-byte
+// aligned source and a column pitch that is a multiple of 4 elements.
+constexpr int kTileRows = 128;
+
+template <int FMT>
+__global__ void __launch_bounds__(kTileRows) quantize_cols_tiled(const float* __restrict__ x, int64_t rows,
+                                                                 int64_t cols, int64_t ldc,
+                                                                 uint8_t* __restrict__ payload, int64_t ldp,
+                                                                 uint8_t* __restrict__ scales, int layout,
+                                                                 int64_t lds) {
+    __shared__ __align__(16) float tile[32][kTileRows + 4];
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t rtiles = (rows + kTileRows - 1) / kTileRows;
+    const int64_t ntiles = rtiles * kblocks;
+    const int t = threadIdx.x;
+    for (int64_t tt = blockIdx.x; tt < ntiles; tt += gridDim.x) {
+        const int64_t kb = tt / rtiles;
+        const int64_t r0 = (tt - kb * rtiles) * kTileRows;
+        const int64_t c0 = kb * 32;
+        const int len = int((cols - c0) < 32 ? (cols - c0) : 32);
+        const int rc = (t & 31) * 4;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int kr = (t >> 5) + 4 * i;
+            float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (kr < len && r0 + rc < rows)
+                q = __ldcs(reinterpret_cast<const float4*>(x + (c0 + kr) * ldc + r0 + rc));
+            *reinterpret_cast<float4*>(&tile[kr][rc]) = q;
+        }
+        __syncthreads();
+        const int64_t r = r0 + t;
+        if (r < rows) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = tile[i][t];
+            quantize_block32<FMT>(v, len, r, kb, kblocks, payload, ldp, scales, layout, lds);
+        }
+        __syncthreads();  // the next tile overwrites the staging
+    }
+}
+
 // ---- dequantise ----------------------------------------------------------------
 __device__ __forceinline__ float decode_e4m3(uint32_t c) {
     const uint32_t s = (c >> 7) & 1, f = (c >> 3) & 15, m = c & 7;
@@ -261,15 +402,19 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
     }
 }
 
-int grid_for(int64_t items, int threads) {
+int sm_count_mx() {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
         cudaGetLastError();
         sms = 148;
     }
+    return sms;
+}
+
+int grid_for(int64_t items, int threads) {
     const int64_t blocks = (items + threads - 1) / threads;
-    return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sms) * 16));
+    return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count_mx()) * 16));
 }
 
 }  // namespace
@@ -307,7 +452,7 @@ extern "C" int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t col
                     "scale padding fill");
     }
     if (ld_x_col == 1) {
-        const int64_t items = rows * kblocks * 4;
+        const int64_t items = rows * ((cols + kQuantSegment - 1) / kQuantSegment) * 32;  // a warp per segment
         const int grid = grid_for(items, 256);
         if (fmt == SW_MX_E4M3)
             quantize_rows<SW_MX_E4M3><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, payload, ld_payload, scales,
@@ -315,6 +460,15 @@ extern "C" int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t col
         else
             quantize_rows<SW_MX_E2M1><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, payload, ld_payload, scales,
                                                            scale_layout, ld_scales);
+    } else if (ld_x_row == 1 && rows % 4 == 0 && ld_x_col % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int64_t tiles = ((rows + kTileRows - 1) / kTileRows) * kblocks;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sm_count_mx()) * 8));
+        if (fmt == SW_MX_E4M3)
+            quantize_cols_tiled<SW_MX_E4M3><<<grid, kTileRows, 0, s>>>(x, rows, cols, ld_x_col, payload, ld_payload,
+                                                                       scales, scale_layout, ld_scales);
+        else
+            quantize_cols_tiled<SW_MX_E2M1><<<grid, kTileRows, 0, s>>>(x, rows, cols, ld_x_col, payload, ld_payload,
+                                                                       scales, scale_layout, ld_scales);
     } else {
         const int grid = grid_for(rows * kblocks, 256);
         if (fmt == SW_MX_E4M3)

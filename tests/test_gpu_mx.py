@@ -64,7 +64,8 @@ def gpu_quantize(fmt, x, scale_layout, transposed=False):
 
 @pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
 @pytest.mark.parametrize("scale_layout", [N.SW_SCALES_ROWMAJOR, N.SW_SCALES_TC128])
-@pytest.mark.parametrize("shape", [(128, 256), (256, 1024), (130, 100), (7, 33), (1, 32)])
+# (132, 100) transposed: the staged column path with a partial row tile and a ragged last block
+@pytest.mark.parametrize("shape", [(128, 256), (256, 1024), (130, 100), (132, 100), (7, 33), (1, 32), (264, 2056)])
 @pytest.mark.parametrize("transposed", [False, True])
 def test_quantize_bit_exact(fmt, scale_layout, shape, transposed):
     x = adversarial(*shape, seed=shape[0] * 131 + shape[1])
@@ -75,10 +76,11 @@ def test_quantize_bit_exact(fmt, scale_layout, shape, transposed):
 
 
 @pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
-def test_quantize_full_size_8192(fmt):
+@pytest.mark.parametrize("transposed", [False, True])
+def test_quantize_full_size_8192(fmt, transposed):
     rng = np.random.default_rng(0)
     x = rng.standard_normal((8192, 8192)).astype(np.float32)
-    p, s = gpu_quantize(fmt, x, N.SW_SCALES_TC128)
+    p, s = gpu_quantize(fmt, x, N.SW_SCALES_TC128, transposed)
     pw, sw_ = O.mx_quantize(fmt, x, scale_layout=N.SW_SCALES_TC128)
     np.testing.assert_array_equal(s, sw_)
     np.testing.assert_array_equal(p, pw)
