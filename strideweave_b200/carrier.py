@@ -222,6 +222,26 @@ class CUDA(Carrier):
             out._buffer.upload(np.ascontiguousarray(host))
         return out
 
+    def _allocate(self, size: int) -> None:
+        """Give an empty carrier (``CUDA(0)``) storage for ``size`` elements;
+        ``sw.move`` calls it to size a destination to the moved layout."""
+        size = operator_index(size)
+        if self._size != 0:
+            raise RuntimeError("only an empty CUDA carrier can be allocated")
+        if size < 0:
+            raise ValueError("CUDA size must be non-negative")
+        if self._swizzle is not None:
+            raise ValueError("a swizzled carrier cannot change size")
+        nbytes = storage_bytes(self._dtype, size)
+        buffer = N.DeviceBuffer(nbytes)
+        if nbytes:
+            N.check(N.lib.sw_memset(c_void_p(buffer.ptr), 0, nbytes, None))
+        if self._buffer is not None:
+            self._buffer.free()
+        self._buffer = buffer
+        self._size = size
+        self._nbytes = nbytes
+
     def allocate_like(self, size: int, *, mutable: bool = True, dtype: Any = None, empty: bool = False) -> CUDA:
         size = operator_index(size)
         if size < 0:
@@ -411,3 +431,13 @@ def _declare_capabilities() -> None:
 
 
 _declare_capabilities()
+
+
+def _register_moves() -> None:
+    """CPU <-> CUDA bulk moves in the reference's move registry."""
+    from .move import register
+
+    register()
+
+
+_register_moves()
