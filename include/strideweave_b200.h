@@ -254,6 +254,34 @@ int sw_matmul_f32(const float* a, int64_t sam, int64_t sak, const float* b,
                   int64_t sbn, int64_t sbk, float* c, int64_t scm, int64_t scn,
                   int64_t M, int64_t N, int64_t K, void* stream);
 
+/* A batch of sw_matmul_f32 contractions in one launch: contraction z reads
+ * a + z*sab, b + z*sbb and writes c + z*scb.  Serves batched einsum without
+ * the union product the reference materialises for batch symbols
+ * (src/strideweave/einops/__init__.py:459-475: align over the union index
+ * space, elementwise_mul, reduce_sum). */
+int sw_matmul_f32_batched(const float* a, int64_t sab, int64_t sam, int64_t sak,
+                          const float* b, int64_t sbb, int64_t sbn, int64_t sbk,
+                          float* c, int64_t scb, int64_t scm, int64_t scn,
+                          int64_t batch, int64_t M, int64_t N, int64_t K,
+                          void* stream);
+
+/* ---- binary elementwise -------------------------------------------------- */
+
+#define SW_BIN_MUL 0
+
+/* out[o(i)] = a[a(i)] * b[b(i)] for every logical index i of `rank` leaves
+ * (first leaf fastest, at most 16) shared by the three views, each with its
+ * own strides (0 on a broadcast leaf) and offset; every address is checked
+ * against its carrier's size first.  Replaces the forward of the reference's
+ * elementwise_mul, CpuElementwiseMulOperation::_forward
+ * (src/strideweave/carriers/cpu/native/ops/elementwise_mul.cpp:10-16 via
+ * _cpu_binary.hpp:85-130), products rounded to binary32. */
+int sw_binary_f32(int op, int rank, const int64_t* shape,
+                  const float* a, int64_t a_offset, const int64_t* a_stride, int64_t a_size,
+                  const float* b, int64_t b_offset, const int64_t* b_stride, int64_t b_size,
+                  float* out, int64_t out_offset, const int64_t* out_stride, int64_t out_size,
+                  void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

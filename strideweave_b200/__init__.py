@@ -16,7 +16,7 @@ from __future__ import annotations
 import importlib
 from typing import Any
 
-__all__ = ["BFloat16", "CUDA", "kernels", "mx", "nn", "ops", "sharding"]
+__all__ = ["BFloat16", "CUDA", "dlpack", "einsum", "kernels", "move", "mx", "nn", "ops", "sharding"]
 
 
 def __getattr__(name: str) -> Any:
@@ -24,6 +24,6 @@ def __getattr__(name: str) -> Any:
         return importlib.import_module(".carrier", __name__).CUDA
     if name == "BFloat16":
         return importlib.import_module("._host", __name__).BFloat16
-    if name in ("kernels", "mx", "ops", "sharding", "carrier", "layout_plan", "nn"):
+    if name in ("kernels", "mx", "ops", "sharding", "carrier", "layout_plan", "nn", "dlpack", "einsum", "move"):
         return importlib.import_module("." + name, __name__)
     raise AttributeError(name)

@@ -40,6 +40,7 @@ SW_OUT_BF16 = 1
 SW_EW_GELU = 0
 SW_EW_GELU_GRAD = 1
 SW_EW_AXPY = 2
+SW_BIN_MUL = 0
 
 
 class DeviceTimeout(RuntimeError):
@@ -115,6 +116,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,
          c_int64, c_void_p],
+    ),
+    "sw_matmul_f32_batched": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
+         c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p],
+    ),
+    "sw_binary_f32": (
+        c_int,
+        [c_int, c_int, POINTER(c_int64), c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p, c_int64,
+         POINTER(c_int64), c_int64, c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p],
     ),
 }
 

@@ -17,10 +17,17 @@ namespace {
 constexpr int kTile = 64;
 constexpr int kKTile = 16;
 
-__global__ void __launch_bounds__(256) matmul_f32_kernel(const float* __restrict__ a, int64_t sam, int64_t sak,
-                                                         const float* __restrict__ b, int64_t sbn, int64_t sbk,
-                                                         float* __restrict__ c, int64_t scm, int64_t scn, int64_t M,
-                                                         int64_t N, int64_t K) {
+// blockIdx.z (+ z0) selects one contraction of a batch: operands advance by
+// their batch strides (0 for a single contraction).
+__global__ void __launch_bounds__(256) matmul_f32_kernel(const float* __restrict__ a, int64_t sab, int64_t sam,
+                                                         int64_t sak, const float* __restrict__ b, int64_t sbb,
+                                                         int64_t sbn, int64_t sbk, float* __restrict__ c,
+                                                         int64_t scb, int64_t scm, int64_t scn, int64_t M,
+                                                         int64_t N, int64_t K, int64_t z0) {
+    const int64_t z = z0 + blockIdx.z;
+    a += z * sab;
+    b += z * sbb;
+    c += z * scb;
     __shared__ float as[kKTile][kTile + 1];
     __shared__ float bs[kKTile][kTile + 1];
     const int tx = threadIdx.x % 16;  // n direction
@@ -67,15 +74,25 @@ __global__ void __launch_bounds__(256) matmul_f32_kernel(const float* __restrict
 }  // namespace
 }  // namespace sw
 
-extern "C" int sw_matmul_f32(const float* a, int64_t sam, int64_t sak, const float* b, int64_t sbn, int64_t sbk,
-                             float* c, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K, void* stream) {
+extern "C" int sw_matmul_f32_batched(const float* a, int64_t sab, int64_t sam, int64_t sak, const float* b,
+                                     int64_t sbb, int64_t sbn, int64_t sbk, float* c, int64_t scb, int64_t scm,
+                                     int64_t scn, int64_t batch, int64_t M, int64_t N, int64_t K, void* stream) {
     using namespace sw;
-    if (M < 0 || N < 0 || K < 0) return fail(SW_ERR_INVALID, "sw_matmul_f32: negative extent");
-    if (M == 0 || N == 0) return ok();
+    if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(SW_ERR_INVALID, "sw_matmul_f32: negative extent");
+    if (batch == 0 || M == 0 || N == 0) return ok();
     if (!a || !b || !c) return fail(SW_ERR_INVALID, "sw_matmul_f32: null pointer");
     if ((M + kTile - 1) / kTile > 65535) return fail(SW_ERR_UNSUPPORTED, "sw_matmul_f32: M too large");
-    dim3 grid((unsigned)((N + kTile - 1) / kTile), (unsigned)((M + kTile - 1) / kTile));
-    matmul_f32_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a, sam, sak, b, sbn, sbk, c, scm, scn, M, N, K);
-    SW_LAUNCH_CHECK("sw_matmul_f32 launch");
+    for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
+        const int64_t nz = batch - z0 < 65535 ? batch - z0 : 65535;
+        dim3 grid((unsigned)((N + kTile - 1) / kTile), (unsigned)((M + kTile - 1) / kTile), (unsigned)nz);
+        matmul_f32_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a, sab, sam, sak, b, sbb, sbn, sbk, c, scb, scm, scn,
+                                                                  M, N, K, z0);
+        SW_LAUNCH_CHECK("sw_matmul_f32 launch");
+    }
     return ok();
+}
+
+extern "C" int sw_matmul_f32(const float* a, int64_t sam, int64_t sak, const float* b, int64_t sbn, int64_t sbk,
+                             float* c, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K, void* stream) {
+    return sw_matmul_f32_batched(a, 0, sam, sak, b, 0, sbn, sbk, c, 0, scm, scn, 1, M, N, K, stream);
 }

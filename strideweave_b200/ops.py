@@ -219,6 +219,76 @@ class CudaMatmul(CudaOperation):
         return (_finish(dl, dls), _finish(dr, drs))
 
 
+# ---- elementwise product (the union step of batched einsum) ------------------------
+
+
+def _binary_mul(a: Tensor, b: Tensor, out: Tensor) -> None:
+    """out = a * b elementwise over three views sharing one shape tree."""
+    import ctypes
+
+    from . import _native as N
+    from .layout_plan import all_leaves
+
+    for t, name in ((a, "lhs"), (b, "rhs"), (out, "output")):
+        if t.carrier.swizzle is not None:
+            raise NotImplementedError(f"{name}: swizzled carriers are not supported by elementwise_mul")
+    la, lb, lo = all_leaves(a.layout), all_leaves(b.layout), all_leaves(out.layout)
+    if not (len(la) == len(lb) == len(lo)) or any(x[0] != y[0] or x[0] != z[0] for x, y, z in zip(la, lb, lo)):
+        raise ValueError("elementwise_mul operands must share one shape tree")
+    keep = [i for i, (e, _) in enumerate(lo) if e != 1]
+    rank = len(keep)
+    arr = ctypes.c_int64 * max(rank, 1)
+    shape = arr(*[lo[i][0] for i in keep])
+    sa, sb, so = (arr(*[leaves[i][1] for i in keep]) for leaves in (la, lb, lo))
+    N.check(N.lib.sw_binary_f32(
+        N.SW_BIN_MUL, rank, shape,
+        N.c_void_p(a.carrier.data_ptr), a.offset, sa, a.carrier.size(),
+        N.c_void_p(b.carrier.data_ptr), b.offset, sb, b.carrier.size(),
+        N.c_void_p(out.carrier.data_ptr), out.offset, so, out.carrier.size(), None))
+
+
+class CudaElementwiseMul(CudaOperation):
+    """Float32 elementwise product of two broadcast-compatible tensors.
+
+    Replaces CpuElementwiseMulOperation (src/strideweave/carriers/cpu/native/
+    ops/elementwise_mul.cpp:8-48): the operands are aligned by the reference's
+    own ``_align_binary_operands`` (differentiable broadcast views,
+    src/strideweave/carriers/operation_helpers.py:129-185), the result takes
+    the canonical layout of the common shape and each product is rounded to
+    binary32; the gradients are g * rhs and g * lhs in the injective canonical
+    layout of each aligned operand.  With this the reference's batched
+    ``einsum`` (union product, then reduce_sum) runs on the device unchanged.
+    """
+
+    def _forward(self, lhs: Any, rhs: Any) -> Tensor:
+        from strideweave.carriers.operation_helpers import _align_binary_operands
+
+        lhs = _cuda_tensor(lhs, "lhs")
+        rhs = _cuda_tensor(rhs, "rhs")
+        if type(lhs.carrier) is not type(rhs.carrier):
+            raise TypeError("Tensor backing carriers must match")
+        lhs, rhs, result_layout = _align_binary_operands(lhs, rhs)
+        if len(self.inputs()) != 0:
+            self.store_inputs(lhs, rhs)  # the gradient flows through the broadcast views
+        plan = resolve_operation_plan("elementwise_mul", lhs.carrier.dtype(), rhs.carrier.dtype(),
+                                      options=self._execution_options)
+        require_capability(self._carrier_class(), plan)
+        result = _new_result(lhs, result_layout, DType.Float32)
+        _binary_mul(lhs, rhs, result)
+        return result
+
+    def backward(self, gradient: Any) -> tuple[Any, Any]:
+        lhs, rhs = self.inputs()
+        gradient = _cuda_tensor(gradient, "gradient")
+        if gradient.layout.shape != lhs.layout.shape:
+            raise ValueError("Tensor shapes must match")
+        dl = _new_result(lhs, injective_layout_for(lhs.layout), DType.Float32)
+        dr = _new_result(rhs, injective_layout_for(rhs.layout), DType.Float32)
+        _binary_mul(gradient, rhs, dl)
+        _binary_mul(gradient, lhs, dr)
+        return (dl, dr)
+
+
 # ---- dispatch table ----------------------------------------------------------------
 
 
@@ -244,6 +314,7 @@ _OPS = {
     "reduce_max": CudaReduceMax,
     "argmax": CudaArgmax,
     "matmul": CudaMatmul,
+    "elementwise_mul": CudaElementwiseMul,
 }
 
 
@@ -273,8 +344,9 @@ def declared_plans() -> list[Any]:
         resolve_operation_plan("argmax", f32),
         resolve_operation_plan("matmul", f32, f32),
         resolve_operation_plan("gelu", f32),
+        resolve_operation_plan("elementwise_mul", f32, f32),
     ]
 
 
-__all__ = ["CudaArgmax", "CudaMatmul", "CudaReduceMax", "CudaReduceSum", "UnsupportedOperationPlan",
+__all__ = ["CudaArgmax", "CudaElementwiseMul", "CudaMatmul", "CudaReduceMax", "CudaReduceSum", "UnsupportedOperationPlan",
            "declared_plans", "make_operation"]
