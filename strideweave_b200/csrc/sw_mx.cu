@@ -250,65 +250,18 @@ __global__ void __launch_bounds__(256) quantize_strided(const float* __restrict_
     }
 }
 
-// Scale, payload and store of one block of `len` (<= 32) values of row r.
-template <int FMT>
-__device__ __forceinline__ void quantize_block32(float (&v)[32], int len, int64_t r, int64_t kb, int64_t kblocks,
-                                                 uint8_t* __restrict__ payload, int64_t ldp,
-                                                 uint8_t* __restrict__ scales, int layout, int64_t lds) {
-    float m = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) m = max_nan_abs(m, v[i]);
-    uint8_t sc;
-    float inv;
-    bool special;
-    block_scale<FMT>(__float_as_uint(m), sc, inv, special);
-    scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
-    if (special) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.0f;  // a NaN/Inf block: payload codes 0
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], inv);
-    }
-    const int64_t c0 = kb * 32;
-    if (FMT == SW_MX_E4M3) {
-        uint8_t* dst = payload + r * ldp + c0;
-        uint32_t w[8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) w[g] = e4m3x4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-        if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {
-            for (int c = 0; c < len; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
-        }
-    } else {
-        uint8_t* dst = payload + r * ldp + c0 / 2;
-        uint32_t w[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) w[g] = e2m1x8(v + 8 * g);
-        if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-        } else {
-            for (int c = 0; c < len; c += 2) {
-                const uint8_t byte = uint8_t((w[c / 8] >> (4 * (c % 8))) & 0xFF);
-                if (c + 1 < len) dst[c / 2] = byte;
-                else dst[c / 2] = uint8_t((dst[c / 2] & 0xF0) | (byte & 0x0F));
-            }
-        }
-    }
-}
-
 // ---- quantise: blocks along a strided axis with unit row stride ---------------
 // (a K x N operand quantised along K, i.e. the blocks of each of N rows run down
 // a column).  A CTA stages a 32 (block) x 128 (row) tile through shared memory
 // with 16-byte loads along the contiguous rows, then each of its 128 threads
-// quantises one row's block from the tile.  Needs rows % 4 == 0, a 16-byte
+// quantises one row's block from the tile in two passes over shared memory
+// (the amax, then scale-and-pack), so only the packed words live in
+// registers and eight CTAs fit on an SM.  Needs rows % 4 == 0, a 16-byte
 // aligned source and a column pitch that is a multiple of 4 elements.
 constexpr int kTileRows = 128;
 
 template <int FMT>
-__global__ void __launch_bounds__(kTileRows) quantize_cols_tiled(const float* __restrict__ x, int64_t rows,
+__global__ void __launch_bounds__(kTileRows, 8) quantize_cols_tiled(const float* __restrict__ x, int64_t rows,
                                                                  int64_t cols, int64_t ldc,
                                                                  uint8_t* __restrict__ payload, int64_t ldp,
                                                                  uint8_t* __restrict__ scales, int layout,
@@ -335,10 +288,50 @@ __global__ void __launch_bounds__(kTileRows) quantize_cols_tiled(const float* __
         __syncthreads();
         const int64_t r = r0 + t;
         if (r < rows) {
-            float v[32];
+            // pass 1: the block's amax from the tile; pass 2: re-read, scale and pack
+            float m = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = tile[i][t];
-            quantize_block32<FMT>(v, len, r, kb, kblocks, payload, ldp, scales, layout, lds);
+            for (int i = 0; i < 32; ++i) m = max_nan_abs(m, tile[i][t]);
+            uint8_t sc;
+            float inv;
+            bool special;
+            block_scale<FMT>(__float_as_uint(m), sc, inv, special);
+            scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+            if (special) inv = 0.0f;  // payload codes 0 below
+            if (FMT == SW_MX_E4M3) {
+                uint32_t w[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    w[g] = special ? 0u
+                                   : e4m3x4(__fmul_rn(tile[4 * g][t], inv), __fmul_rn(tile[4 * g + 1][t], inv),
+                                            __fmul_rn(tile[4 * g + 2][t], inv), __fmul_rn(tile[4 * g + 3][t], inv));
+                uint8_t* dst = payload + r * ldp + kb * 32;
+                if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+                    for (int c = 0; c < len; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+                }
+            } else {
+                uint32_t w[4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    float q[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) q[e] = __fmul_rn(tile[8 * g + e][t], inv);
+                    w[g] = special ? 0u : e2m1x8(q);
+                }
+                uint8_t* dst = payload + r * ldp + kb * 16;
+                if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                } else {
+                    for (int c = 0; c < len; c += 2) {
+                        const uint8_t byte = uint8_t((w[c / 8] >> (4 * (c % 8))) & 0xFF);
+                        if (c + 1 < len) dst[c / 2] = byte;
+                        else dst[c / 2] = uint8_t((dst[c / 2] & 0xF0) | (byte & 0x0F));
+                    }
+                }
+            }
         }
         __syncthreads();  // the next tile overwrites the staging
     }
