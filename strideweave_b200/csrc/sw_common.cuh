@@ -38,6 +38,32 @@ __device__ __forceinline__ void report_device_error(int code) {
 // (microseconds) and far below a watchdog timeout.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
+// Programmatic dependent launch: a grid launched with launch_pdl may be
+// scheduled while the previous grid on its stream drains.  It calls
+// pdl_enter() before touching global memory: that waits for the previous grid
+// (and its memory) to complete, then lets the next grid begin launching.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launches `kernel` with programmatic stream serialization.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace sw
 
 #define SW_CUDA_TRY(expr, what)                         \

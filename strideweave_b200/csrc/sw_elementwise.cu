@@ -29,6 +29,7 @@ __device__ __forceinline__ float apply(float a, float b, float alpha) {
 template <int OP>
 __global__ void __launch_bounds__(256) ew_kernel(int64_t n, const float* __restrict__ a, const float* __restrict__ b,
                                                  float* out, float alpha, bool vec) {
+    pdl_enter();
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
     const int64_t t0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (vec) {
@@ -71,6 +72,7 @@ __global__ void __launch_bounds__(256) mse_loss_kernel(int64_t n, const float* _
 __global__ void __launch_bounds__(256) mse_grad_kernel(int64_t n, const float* __restrict__ p,
                                                        const float* __restrict__ t, const float* __restrict__ up,
                                                        float* __restrict__ g, float two_over_n) {
+    pdl_enter();
     const float s = (up ? up[0] : 1.0f) * two_over_n;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
         g[i] = s * (p[i] - t[i]);
@@ -97,9 +99,10 @@ extern "C" int sw_elementwise_f32(int op, int64_t n, const float* a, const float
                        (op != SW_EW_GELU ? reinterpret_cast<uintptr_t>(b) : 0)) & 15) == 0;
     cudaStream_t s = (cudaStream_t)stream;
     const int grid = grid_of(vec ? n / 4 + 1 : n);
-    if (op == SW_EW_GELU) ew_kernel<SW_EW_GELU><<<grid, 256, 0, s>>>(n, a, b, out, alpha, vec);
-    else if (op == SW_EW_GELU_GRAD) ew_kernel<SW_EW_GELU_GRAD><<<grid, 256, 0, s>>>(n, a, b, out, alpha, vec);
-    else ew_kernel<SW_EW_AXPY><<<grid, 256, 0, s>>>(n, a, b, out, alpha, vec);
+    auto kernel = op == SW_EW_GELU        ? ew_kernel<SW_EW_GELU>
+                  : op == SW_EW_GELU_GRAD ? ew_kernel<SW_EW_GELU_GRAD>
+                                          : ew_kernel<SW_EW_AXPY>;
+    SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, n, a, b, out, alpha, vec), "sw_elementwise_f32 launch");
     SW_LAUNCH_CHECK("sw_elementwise_f32 launch");
     return ok();
 }
@@ -117,7 +120,8 @@ extern "C" int sw_mse_f32(int64_t n, const float* pred, const float* target, flo
         SW_LAUNCH_CHECK("sw_mse_f32 loss launch");
     }
     if (grad) {
-        mse_grad_kernel<<<grid, 256, 0, s>>>(n, pred, target, upstream, grad, 2.0f / float(n));
+        SW_CUDA_TRY(launch_pdl(mse_grad_kernel, grid, 256, 0, s, n, pred, target, upstream, grad, 2.0f / float(n)),
+                    "mse grad launch");
         SW_LAUNCH_CHECK("sw_mse_f32 grad launch");
     }
     return ok();

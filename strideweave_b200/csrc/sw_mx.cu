@@ -107,6 +107,7 @@ template <int FMT>
 __global__ void __launch_bounds__(256) quantize_rows(const float* __restrict__ x, int64_t rows, int64_t cols,
                                                      int64_t ldx, uint8_t* __restrict__ payload, int64_t ldp,
                                                      uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    pdl_enter();
     const int64_t kblocks = (cols + 31) / 32;
     const int64_t segs = (cols + kQuantSegment - 1) / kQuantSegment;
     const int64_t units = rows * segs;
@@ -199,6 +200,7 @@ __global__ void __launch_bounds__(256) quantize_strided(const float* __restrict_
                                                         int64_t ldr, int64_t ldc, uint8_t* __restrict__ payload,
                                                         int64_t ldp, uint8_t* __restrict__ scales, int layout,
                                                         int64_t lds) {
+    pdl_enter();
     const int64_t kblocks = (cols + 31) / 32;
     const int64_t total = rows * kblocks;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
@@ -267,6 +269,7 @@ __global__ void __launch_bounds__(kTileRows, 8) quantize_cols_tiled(const float*
                                                                  uint8_t* __restrict__ scales, int layout,
                                                                  int64_t lds) {
     __shared__ __align__(16) float tile[32][kTileRows + 4];
+    pdl_enter();
     const int64_t kblocks = (cols + 31) / 32;
     const int64_t rtiles = (rows + kTileRows - 1) / kTileRows;
     const int64_t ntiles = rtiles * kblocks;
@@ -365,6 +368,7 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
                                                          const uint8_t* __restrict__ scales, int layout,
                                                          int64_t lds, int64_t rows, int64_t cols,
                                                          float* __restrict__ out, int64_t ldo) {
+    pdl_enter();
     const int64_t kblocks = (cols + 31) / 32;
     const int64_t groups = (cols + 7) / 8;  // 8 elements per thread
     const int64_t total = rows * groups;
@@ -444,32 +448,27 @@ extern "C" int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t col
         SW_CUDA_TRY(cudaMemsetAsync(scales, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s),
                     "scale padding fill");
     }
+    const bool e4 = fmt == SW_MX_E4M3;
     if (ld_x_col == 1) {
         const int64_t items = rows * ((cols + kQuantSegment - 1) / kQuantSegment) * 32;  // a warp per segment
         const int grid = grid_for(items, 256);
-        if (fmt == SW_MX_E4M3)
-            quantize_rows<SW_MX_E4M3><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, payload, ld_payload, scales,
-                                                           scale_layout, ld_scales);
-        else
-            quantize_rows<SW_MX_E2M1><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, payload, ld_payload, scales,
-                                                           scale_layout, ld_scales);
+        auto kernel = e4 ? quantize_rows<SW_MX_E4M3> : quantize_rows<SW_MX_E2M1>;
+        SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, x, rows, cols, ld_x_row, payload, ld_payload, scales,
+                               scale_layout, ld_scales),
+                    "quantize_rows launch");
     } else if (ld_x_row == 1 && rows % 4 == 0 && ld_x_col % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         const int64_t tiles = ((rows + kTileRows - 1) / kTileRows) * kblocks;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sm_count_mx()) * 8));
-        if (fmt == SW_MX_E4M3)
-            quantize_cols_tiled<SW_MX_E4M3><<<grid, kTileRows, 0, s>>>(x, rows, cols, ld_x_col, payload, ld_payload,
-                                                                       scales, scale_layout, ld_scales);
-        else
-            quantize_cols_tiled<SW_MX_E2M1><<<grid, kTileRows, 0, s>>>(x, rows, cols, ld_x_col, payload, ld_payload,
-                                                                       scales, scale_layout, ld_scales);
+        auto kernel = e4 ? quantize_cols_tiled<SW_MX_E4M3> : quantize_cols_tiled<SW_MX_E2M1>;
+        SW_CUDA_TRY(launch_pdl(kernel, grid, kTileRows, 0, s, x, rows, cols, ld_x_col, payload, ld_payload, scales,
+                               scale_layout, ld_scales),
+                    "quantize_cols_tiled launch");
     } else {
         const int grid = grid_for(rows * kblocks, 256);
-        if (fmt == SW_MX_E4M3)
-            quantize_strided<SW_MX_E4M3><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, ld_x_col, payload,
-                                                              ld_payload, scales, scale_layout, ld_scales);
-        else
-            quantize_strided<SW_MX_E2M1><<<grid, 256, 0, s>>>(x, rows, cols, ld_x_row, ld_x_col, payload,
-                                                              ld_payload, scales, scale_layout, ld_scales);
+        auto kernel = e4 ? quantize_strided<SW_MX_E4M3> : quantize_strided<SW_MX_E2M1>;
+        SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, x, rows, cols, ld_x_row, ld_x_col, payload, ld_payload,
+                               scales, scale_layout, ld_scales),
+                    "quantize_strided launch");
     }
     SW_LAUNCH_CHECK("sw_mx_quantize launch");
     return ok();
@@ -488,12 +487,10 @@ extern "C" int sw_mx_dequantize(int fmt, const uint8_t* payload, int64_t ld_payl
     if (ld_out < cols) return fail(SW_ERR_INVALID, "sw_mx_dequantize: output pitch smaller than a row");
     cudaStream_t s = (cudaStream_t)stream;
     const int grid = grid_for(rows * ((cols + 7) / 8), 256);
-    if (fmt == SW_MX_E4M3)
-        dequantize_kernel<SW_MX_E4M3><<<grid, 256, 0, s>>>(payload, ld_payload, scales, scale_layout, ld_scales,
-                                                           rows, cols, out, ld_out);
-    else
-        dequantize_kernel<SW_MX_E2M1><<<grid, 256, 0, s>>>(payload, ld_payload, scales, scale_layout, ld_scales,
-                                                           rows, cols, out, ld_out);
+    auto kernel = fmt == SW_MX_E4M3 ? dequantize_kernel<SW_MX_E4M3> : dequantize_kernel<SW_MX_E2M1>;
+    SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, payload, ld_payload, scales, scale_layout, ld_scales, rows, cols,
+                           out, ld_out),
+                "dequantize launch");
     SW_LAUNCH_CHECK("sw_mx_dequantize launch");
     return ok();
 }

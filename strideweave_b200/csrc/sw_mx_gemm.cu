@@ -134,6 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // barrier set-up, descriptor prefetch and the TMEM allocation overlap the
+    // previous grid's tail; operands are read only after it completes
+    pdl_enter();
 
     const int num_m = args.M / kBM;
     const int num_n = args.N / BN;
@@ -470,7 +473,7 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t tiles = (M / kBM) * (N / BN);
     const int grid = (int)std::min<int64_t>(tiles, sms);
-    kernel<<<grid, kThreads, Cf::kSmemBytes, stream>>>(ma, mb, mc, args);
+    SW_CUDA_TRY(launch_pdl(kernel, grid, kThreads, Cf::kSmemBytes, stream, ma, mb, mc, args), "mx_gemm launch");
     SW_LAUNCH_CHECK("mx_gemm launch");
     return SW_OK;
 }

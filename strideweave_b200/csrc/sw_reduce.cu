@@ -452,15 +452,6 @@ struct FastFold {
     }
 };
 
-// Programmatic dependent launch: a grid launched with the attribute may be
-// scheduled while the previous grid on its stream drains.  It waits for that
-// grid (and its memory) before touching global memory, then lets the next
-// grid begin launching.
-__device__ __forceinline__ void pdl_enter() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 template <bool kSwz>
 __device__ __forceinline__ int64_t phys(const Swz& s, int64_t f) {
     if constexpr (kSwz) return swizzle(s, f);
@@ -811,22 +802,6 @@ int swizzle_top_bit(const Swz& s) {
     return top;
 }
 
-// Launches `kernel` with programmatic stream serialization (see pdl_enter).
-template <class... KArgs, class... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-}
-
 // Where the split column walk takes its scratch from: the library's
 // per-(device, stream) buffer (base == nullptr), or a fixed region the caller
 // of the entry point chose (base, bytes) whose counters are cleared per launch.
@@ -911,7 +886,7 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         const int64_t warps = (p.n_kept + rpw - 1) / rpw;
         const int64_t blocks = (warps + kRowsAffWarps - 1) / kRowsAffWarps;
         const cudaError_t err = launch_pdl(reduce_rows_affine<Op, kSwz, Ord>, dim3((unsigned)blocks),
-                                           dim3(kRowsAffThreads), stream, x, p, L.rw, rpw, out);
+                                           dim3(kRowsAffThreads), 0, stream, x, p, L.rw, rpw, out);
         if (err != cudaSuccess) return cuda_fail(err, "reduce_rows_affine launch");
         return SW_OK;
     }
@@ -940,7 +915,7 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         partials = reinterpret_cast<typename Op::S*>(static_cast<char*>(base) + cbytes);
     }
     const cudaError_t err = launch_pdl(reduce_cols_affine<Op, kSwz, Ord>, dim3((unsigned)col_blocks, (unsigned)L.splits),
-                                       dim3(kColsAffThreads), stream, x, p, L.cstride, L.cweight, out, partials,
+                                       dim3(kColsAffThreads), 0, stream, x, p, L.cstride, L.cweight, out, partials,
                                        counters);
     if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_affine launch");
     return SW_OK;
