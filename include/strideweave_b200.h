@@ -213,6 +213,29 @@ int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t cols,
                    int64_t ld_payload, uint8_t* scales, int scale_layout,
                    int64_t ld_scales, void* stream);
 
+/* What sw_mx_quantize_dual quantises: S = x, gelu(x), or x * gelu'(h). */
+#define SW_XF_NONE 0
+#define SW_XF_GELU 1      /* S = x * Phi(x), as SW_EW_GELU                         */
+#define SW_XF_GELU_GRAD 2 /* S = x * d/dh (h * Phi(h)), as SW_EW_GELU_GRAD (a = h) */
+
+/* Quantises S[rows, cols] (S[i, j] from x[i*ld_x + j], and h likewise) both
+ * ways in one pass: the "row planes" hold S blocked along cols (the operand
+ * [rows, cols]), the "column planes" S blocked along rows (the operand
+ * [cols, rows], i.e. S transposed).  Either plane pair may be NULL.  The
+ * planes are bit-identical to sw_elementwise_f32 followed by two
+ * sw_mx_quantize calls; this is what one activation of an MLP layer needs for
+ * its forward and its weight-gradient contraction.  Requires rows % 32 == 0,
+ * cols % 128 == 0, ld_x % 4 == 0 and 16-byte aligned x and h, else
+ * SW_ERR_UNSUPPORTED (use the separate calls).  No reference counterpart
+ * beyond sw_mx_quantize's: it fuses the GELU of
+ * src/strideweave/carriers/cpu/native/_cpu_operation.hpp:33-40 into it. */
+int sw_mx_quantize_dual(int fmt, int transform, const float* x, const float* h,
+                        int64_t rows, int64_t cols, int64_t ld_x,
+                        uint8_t* payload_r, int64_t ld_payload_r, uint8_t* scales_r,
+                        int scale_layout_r, int64_t ld_scales_r,
+                        uint8_t* payload_c, int64_t ld_payload_c, uint8_t* scales_c,
+                        int scale_layout_c, int64_t ld_scales_c, void* stream);
+
 /* Exact inverse image: out[r*ld_out + c] = element * 2^(scale-127)
  * (NaN where the scale byte is 0xFF). */
 int sw_mx_dequantize(int fmt, const uint8_t* payload, int64_t ld_payload,

@@ -41,6 +41,9 @@ SW_EW_GELU = 0
 SW_EW_GELU_GRAD = 1
 SW_EW_AXPY = 2
 SW_BIN_MUL = 0
+SW_XF_NONE = 0
+SW_XF_GELU = 1
+SW_XF_GELU_GRAD = 2
 
 
 class DeviceTimeout(RuntimeError):
@@ -100,6 +103,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_mx_quantize": (
         c_int,
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p],
+    ),
+    "sw_mx_quantize_dual": (
+        c_int,
+        [c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+         c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p],
     ),
     "sw_mx_dequantize": (
         c_int,

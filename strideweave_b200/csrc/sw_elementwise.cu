@@ -5,19 +5,10 @@
 #include <algorithm>
 
 #include "sw_common.cuh"
+#include "sw_gelu.cuh"
 
 namespace sw {
 namespace {
-
-__device__ __forceinline__ float gelu(float x) {
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
-
-__device__ __forceinline__ float gelu_grad(float x) {
-    const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
-    const float pdf = 0.39894228040143268f * expf(-0.5f * x * x);
-    return cdf + x * pdf;
-}
 
 template <int OP>
 __device__ __forceinline__ float apply(float a, float b, float alpha) {

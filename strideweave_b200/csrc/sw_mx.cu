@@ -18,6 +18,7 @@
 #include <cstring>
 
 #include "sw_common.cuh"
+#include "sw_gelu.cuh"
 
 namespace sw {
 namespace {
@@ -340,6 +341,153 @@ __global__ void __launch_bounds__(kTileRows, 8) quantize_cols_tiled(const float*
     }
 }
 
+// ---- quantise both ways, with the GELU (or its gradient) applied on the way in --
+// One read of S[rows, cols] (unit stride along cols, row pitch ld) gives the
+// MX planes blocked along cols ("row planes", the operand [rows, cols]) and the
+// planes blocked along rows ("column planes", the operand [cols, rows]) - the
+// two operands an MLP layer's forward and weight-gradient contractions take
+// from one activation.  S is x, gelu(x), or x * gelu'(h) with h the
+// pre-activation and x the upstream gradient: the same functions, with the same
+// operand order, as the elementwise kernels, so the planes are bit-identical to
+// those of the unfused sequence.
+// A CTA stages a 32 x 128 tile in which each 32-element row block is padded to
+// 36 floats: float4 reads along a row block (the row planes) and scalar reads
+// down a column (the column planes) are then both free of bank conflicts.
+constexpr int kDualRows = 32;
+constexpr int kDualCols = 128;
+constexpr int kDualPitch = 4 * 36;  // floats per staged row
+
+template <int XF>
+__device__ __forceinline__ float4 dual_transform(float4 x, float4 h) {
+    if (XF == SW_XF_GELU) return make_float4(gelu(x.x), gelu(x.y), gelu(x.z), gelu(x.w));
+    if (XF == SW_XF_GELU_GRAD)
+        return make_float4(x.x * gelu_grad(h.x), x.y * gelu_grad(h.y), x.z * gelu_grad(h.z), x.w * gelu_grad(h.w));
+    return x;
+}
+
+template <int FMT, int XF>
+__global__ void __launch_bounds__(kDualCols, 8)
+    quantize_dual(const float* __restrict__ x, const float* __restrict__ h, int64_t rows, int64_t cols, int64_t ld,
+                  uint8_t* __restrict__ pr, int64_t ldpr, uint8_t* __restrict__ sr, int lr, int64_t ldsr,
+                  uint8_t* __restrict__ pc, int64_t ldpc, uint8_t* __restrict__ sc, int lc, int64_t ldsc) {
+    __shared__ __align__(16) float tile[kDualRows * kDualPitch];
+    pdl_enter();
+    const int t = threadIdx.x;
+    const int64_t ctiles = cols / kDualCols;
+    const int64_t ntiles = (rows / kDualRows) * ctiles;
+    const int c4 = t & 31;
+    for (int64_t tt = blockIdx.x; tt < ntiles; tt += gridDim.x) {
+        const int64_t i0 = (tt / ctiles) * kDualRows;
+        const int64_t j0 = (tt - (tt / ctiles) * ctiles) * kDualCols;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int r = (t >> 5) + 4 * k;
+            const int64_t off = (i0 + r) * ld + j0 + 4 * c4;
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(x + off));
+            const float4 hv = XF == SW_XF_GELU_GRAD ? __ldcs(reinterpret_cast<const float4*>(h + off)) : v;
+            *reinterpret_cast<float4*>(&tile[r * kDualPitch + (c4 >> 3) * 36 + (c4 & 7) * 4]) =
+                dual_transform<XF>(v, hv);
+        }
+        __syncthreads();
+        if (pr) {
+            // thread t: row t / 4 of the tile, 32-block t % 4
+            const int row = t >> 2, blk = t & 3;
+            const float4* src = reinterpret_cast<const float4*>(&tile[row * kDualPitch + blk * 36]);
+            float m = 0.0f;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const float4 v = src[g];
+                m = max_nan_abs(max_nan_abs(max_nan_abs(max_nan_abs(m, v.x), v.y), v.z), v.w);
+            }
+            uint8_t scb;
+            float inv;
+            bool special;
+            block_scale<FMT>(__float_as_uint(m), scb, inv, special);
+            const int64_t r = i0 + row, kb = (j0 >> 5) + blk;
+            sr[scale_offset(lr, r, kb, cols >> 5, ldsr)] = scb;
+            if (FMT == SW_MX_E4M3) {
+                uint32_t w[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                    const float4 v = src[g];
+                    w[g] = special ? 0u
+                                   : e4m3x4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
+                                            __fmul_rn(v.w, inv));
+                }
+                uint8_t* dst = pr + r * ldpr + kb * 32;
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+                    for (int c = 0; c < 32; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+                }
+            } else {
+                uint32_t w[4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const float4 a = src[2 * g], b = src[2 * g + 1];
+                    const float q[8] = {__fmul_rn(a.x, inv), __fmul_rn(a.y, inv), __fmul_rn(a.z, inv),
+                                        __fmul_rn(a.w, inv), __fmul_rn(b.x, inv), __fmul_rn(b.y, inv),
+                                        __fmul_rn(b.z, inv), __fmul_rn(b.w, inv)};
+                    w[g] = special ? 0u : e2m1x8(q);
+                }
+                uint8_t* dst = pr + r * ldpr + kb * 16;
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                } else {
+                    for (int c = 0; c < 16; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+                }
+            }
+        }
+        if (pc) {
+            // thread t: column t of the tile, one 32-block down its rows
+            const float* src = &tile[(t >> 5) * 36 + (t & 31)];
+            float m = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) m = max_nan_abs(m, src[i * kDualPitch]);
+            uint8_t scb;
+            float inv;
+            bool special;
+            block_scale<FMT>(__float_as_uint(m), scb, inv, special);
+            const int64_t r = j0 + t, kb = i0 >> 5;
+            sc[scale_offset(lc, r, kb, rows >> 5, ldsc)] = scb;
+            if (FMT == SW_MX_E4M3) {
+                uint32_t w[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    w[g] = special ? 0u
+                                   : e4m3x4(__fmul_rn(src[(4 * g) * kDualPitch], inv),
+                                            __fmul_rn(src[(4 * g + 1) * kDualPitch], inv),
+                                            __fmul_rn(src[(4 * g + 2) * kDualPitch], inv),
+                                            __fmul_rn(src[(4 * g + 3) * kDualPitch], inv));
+                uint8_t* dst = pc + r * ldpc + kb * 32;
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+                    for (int c = 0; c < 32; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+                }
+            } else {
+                uint32_t w[4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    float q[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) q[e] = __fmul_rn(src[(8 * g + e) * kDualPitch], inv);
+                    w[g] = special ? 0u : e2m1x8(q);
+                }
+                uint8_t* dst = pc + r * ldpc + kb * 16;
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+                } else {
+                    for (int c = 0; c < 16; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+                }
+            }
+        }
+        __syncthreads();  // the next tile overwrites the staging
+    }
+}
+
 // ---- dequantise ----------------------------------------------------------------
 __device__ __forceinline__ float decode_e4m3(uint32_t c) {
     const uint32_t s = (c >> 7) & 1, f = (c >> 3) & 15, m = c & 7;
@@ -471,6 +619,66 @@ extern "C" int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t col
                     "quantize_strided launch");
     }
     SW_LAUNCH_CHECK("sw_mx_quantize launch");
+    return ok();
+}
+
+extern "C" int sw_mx_quantize_dual(int fmt, int transform, const float* x, const float* h, int64_t rows,
+                                   int64_t cols, int64_t ld_x, uint8_t* payload_r, int64_t ld_payload_r,
+                                   uint8_t* scales_r, int scale_layout_r, int64_t ld_scales_r, uint8_t* payload_c,
+                                   int64_t ld_payload_c, uint8_t* scales_c, int scale_layout_c,
+                                   int64_t ld_scales_c, void* stream) {
+    using namespace sw;
+    if (fmt != SW_MX_E4M3 && fmt != SW_MX_E2M1)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: unknown format %d", fmt);
+    if (transform != SW_XF_NONE && transform != SW_XF_GELU && transform != SW_XF_GELU_GRAD)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: unknown transform %d", transform);
+    if (rows < 0 || cols < 0) return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: negative extent");
+    if (rows == 0 || cols == 0) return ok();
+    if (!x || (transform == SW_XF_GELU_GRAD && !h)) return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: null input");
+    if (!payload_r != !scales_r || !payload_c != !scales_c)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: a plane needs both its payload and its scales");
+    if (!payload_r && !payload_c) return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: no output plane");
+    for (int layout : {scale_layout_r, scale_layout_c})
+        if (layout != SW_SCALES_ROWMAJOR && layout != SW_SCALES_TC128)
+            return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: unknown scale layout %d", layout);
+    if (ld_x < cols) return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: row pitch smaller than a row");
+    if (rows % kDualRows != 0 || cols % kDualCols != 0 || ld_x % 4 != 0 ||
+        (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+        (transform == SW_XF_GELU_GRAD && (reinterpret_cast<uintptr_t>(h) & 15) != 0))
+        return fail(SW_ERR_UNSUPPORTED,
+                    "sw_mx_quantize_dual: needs rows %% 32 == 0, cols %% 128 == 0, a pitch of whole 16-byte "
+                    "vectors and 16-byte aligned inputs (rows %lld, cols %lld, pitch %lld)",
+                    (long long)rows, (long long)cols, (long long)ld_x);
+    const bool e4 = fmt == SW_MX_E4M3;
+    cudaStream_t s = (cudaStream_t)stream;
+    // plane geometry: (operand rows, K) = (rows, cols) for the row planes, (cols, rows) for the column planes
+    struct Plane { uint8_t* payload; int64_t ldp; uint8_t* scales; int layout; int64_t lds; int64_t n; int64_t k; };
+    const Plane planes[2] = {{payload_r, ld_payload_r, scales_r, scale_layout_r, ld_scales_r, rows, cols},
+                             {payload_c, ld_payload_c, scales_c, scale_layout_c, ld_scales_c, cols, rows}};
+    for (const Plane& p : planes) {
+        if (!p.payload) continue;
+        const int64_t kblocks = p.k / 32;
+        if (p.ldp < (e4 ? p.k : p.k / 2))
+            return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: payload pitch %lld < row bytes", (long long)p.ldp);
+        if (p.layout == SW_SCALES_ROWMAJOR && p.lds < kblocks)
+            return fail(SW_ERR_INVALID, "sw_mx_quantize_dual: scale pitch smaller than blocks per row");
+        if (p.layout == SW_SCALES_TC128 && (p.n % 128 != 0 || kblocks % 4 != 0))
+            SW_CUDA_TRY(cudaMemsetAsync(p.scales, 127, (size_t)sw_mx_scale_bytes_tc128(p.n, kblocks), s),
+                        "scale padding fill");
+    }
+    const int64_t tiles = (rows / kDualRows) * (cols / kDualCols);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sm_count_mx()) * 8));
+    using Kernel = void (*)(const float*, const float*, int64_t, int64_t, int64_t, uint8_t*, int64_t, uint8_t*, int,
+                            int64_t, uint8_t*, int64_t, uint8_t*, int, int64_t);
+    Kernel kernel;
+    if (transform == SW_XF_NONE) kernel = e4 ? quantize_dual<SW_MX_E4M3, SW_XF_NONE> : quantize_dual<SW_MX_E2M1, SW_XF_NONE>;
+    else if (transform == SW_XF_GELU) kernel = e4 ? quantize_dual<SW_MX_E4M3, SW_XF_GELU> : quantize_dual<SW_MX_E2M1, SW_XF_GELU>;
+    else kernel = e4 ? quantize_dual<SW_MX_E4M3, SW_XF_GELU_GRAD> : quantize_dual<SW_MX_E2M1, SW_XF_GELU_GRAD>;
+    SW_CUDA_TRY(launch_pdl(kernel, grid, kDualCols, 0, s, x, h, rows, cols, ld_x, payload_r, ld_payload_r, scales_r,
+                           scale_layout_r, ld_scales_r, payload_c, ld_payload_c, scales_c, scale_layout_c,
+                           ld_scales_c),
+                "quantize_dual launch");
+    SW_LAUNCH_CHECK("sw_mx_quantize_dual launch");
     return ok();
 }
 

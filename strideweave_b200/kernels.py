@@ -104,6 +104,20 @@ def mx_quantize(fmt: int, x_ptr: int, rows: int, cols: int, ld_row: int, ld_col:
                                  ld_payload, c_void_p(scales_ptr), scale_layout, ld_scales, c_void_p(stream)))
 
 
+def mx_quantize_dual(fmt: int, transform: int, x_ptr: int, h_ptr: int, rows: int, cols: int, ld: int,
+                     row_planes: tuple[int, int] | None, col_planes: tuple[int, int] | None, *,
+                     scale_layout: int = N.SW_SCALES_TC128, stream: int = 0) -> None:
+    """S[rows, cols] (x, gelu(x) or x * gelu'(h); unit stride along cols) quantised
+    along cols into ``row_planes`` (payload, scales) and along rows into
+    ``col_planes``, payload rows packed (see sw_mx_quantize_dual)."""
+    pr, sr = row_planes if row_planes else (0, 0)
+    pc, sc = col_planes if col_planes else (0, 0)
+    N.check(N.lib.sw_mx_quantize_dual(fmt, transform, c_void_p(x_ptr), c_void_p(h_ptr or None), rows, cols, ld,
+                                      c_void_p(pr or None), mx_row_bytes(fmt, cols), c_void_p(sr or None),
+                                      scale_layout, cols // 32, c_void_p(pc or None), mx_row_bytes(fmt, rows),
+                                      c_void_p(sc or None), scale_layout, rows // 32, c_void_p(stream)))
+
+
 def mx_dequantize(fmt: int, payload_ptr: int, ld_payload: int, scales_ptr: int, rows: int, cols: int, out_ptr: int,
                   ld_out: int, *, scale_layout: int = N.SW_SCALES_TC128, ld_scales: int = 0,
                   stream: int = 0) -> None:

@@ -109,6 +109,64 @@ def quantize(t: Tensor, fmt: str = "MXFP8_E4M3") -> Tensor:
     return Tensor._from_representation(rep)
 
 
+def dual_geometry(t: Tensor) -> tuple[int, int, int, int, bool] | None:
+    """(address, rows, cols, pitch, transposed) of the memory matrix behind a
+    Float32 CUDA matrix when ``sw_mx_quantize_dual`` can read it, else None.
+    ``transposed`` means the memory rows are the tensor's columns (a
+    column-major tensor)."""
+    ptr, R, C, sr, sc = _f32_operand(t, "operand")
+    if sc == 1 and R > 1:
+        rows, cols, ld, transposed = R, C, sr, False
+    elif sr == 1:
+        rows, cols, ld, transposed = C, R, sc, True
+    else:
+        return None
+    if rows % 32 or cols % 128 or ld % 4 or ptr % 16 or ld < cols:
+        return None
+    return ptr, rows, cols, ld, transposed
+
+
+Planes = tuple[Any, Any]  # (payload carrier, scale carrier), TC128 scales, packed rows
+
+
+def quantize_both(t: Tensor, code: int, *, transform: int = N.SW_XF_NONE, h: Tensor | None = None,
+                  need_t: bool = True, need_tT: bool = True) -> tuple[Planes | None, Planes | None] | None:
+    """The contraction operands t [R, C] (blocks along C) and t^T [C, R] (blocks
+    along R) of S = t, gelu(t) or t * gelu'(h), from one read of t (and h,
+    which shares t's layout).  The planes equal those of the elementwise
+    kernel followed by two ``quantize`` calls, bit for bit.  Returns None when
+    the fused quantiser cannot read t's layout."""
+    from .carrier import CUDA
+
+    geo = dual_geometry(t)
+    if geo is None:
+        return None
+    ptr, rows, cols, ld, transposed = geo
+    h_ptr = 0
+    if transform == N.SW_XF_GELU_GRAD:
+        if h is None or h.layout != t.layout:
+            return None
+        hgeo = dual_geometry(h)
+        if hgeo is None:
+            return None
+        h_ptr = hgeo[0]
+    R, C = (cols, rows) if transposed else (rows, cols)
+    elem = DType.E4M3 if code == N.SW_MX_E4M3 else DType.E2M1
+    dev = t.carrier.device
+
+    def planes(n: int, k: int) -> Planes:
+        return (CUDA(n * k, dtype=elem, empty=True, device=dev),
+                CUDA(kernels.scale_bytes_tc128(n, k // 32), dtype=DType.E8M0, empty=True, device=dev))
+
+    q_t = planes(R, C) if need_t else None
+    q_tT = planes(C, R) if need_tT else None
+    row_q, col_q = (q_tT, q_t) if transposed else (q_t, q_tT)
+    kernels.mx_quantize_dual(code, transform, ptr, h_ptr, rows, cols, ld,
+                             (row_q[0].data_ptr, row_q[1].data_ptr) if row_q else None,
+                             (col_q[0].data_ptr, col_q[1].data_ptr) if col_q else None)
+    return q_t, q_tT
+
+
 class MXPlanes:
     """The two planes of a validated MX tensor, lowered for the kernels."""
 

@@ -205,47 +205,136 @@ def gelu_grad(x: Tensor, g: Tensor) -> Tensor:
 
 
 def train_step(model: "MLP", x: Tensor, target: Tensor, lr: float) -> Tensor:
-    """One fused training step of an MLP: forward, MSE loss, backward and SGD,
-    with the same kernels and the same MX re-quantisation as the autograd path
+    """One training step of an MLP: forward, MSE loss, backward and SGD, with
+    the same contractions and the same MX re-quantisation as the autograd path
     (MxLinear / CudaGelu / CudaMSELoss), scheduled explicitly.
 
     The reference's leaf-gradient accumulation copies a gradient element by
     element through `Tensor.__getitem__` (src/strideweave/core/native/
     _tensor.cpp:914-990).  That is harmless on a host carrier but would stall
     a device carrier for seconds per weight, so the full-size step runs here.
-    Returns the loss (a one-element CUDA tensor, read it after the step).
+
+    Each activation, weight and gradient is read once by the two-way quantiser
+    (``sw_mx_quantize_dual``): it applies the GELU (forward) or the GELU
+    derivative (backward) on the way in and writes both operands the layer's
+    contractions take from it.  The activations themselves are never stored,
+    and the result is bit-identical to the autograd step.  Shapes that the
+    quantiser cannot tile fall back to the separate kernels.  Returns the loss
+    (a one-element CUDA tensor, read it after the step).
     """
     from strideweave import no_grad
 
+    with no_grad():
+        loss = _train_step_dual(model, x, target, lr)
+        if loss is None:
+            loss = _train_step_separate(model, x, target, lr)
+    return loss
+
+
+def _mse_and_grad(y: Tensor, target: Tensor) -> tuple[Tensor, Tensor]:
+    from .carrier import CUDA
+
+    pp, n = _compact(y, "pred")
+    tp, _ = _compact(target, "target")
+    if y.layout != target.layout:
+        raise ValueError("pred and target layouts must match")
+    loss = Tensor(CUDA(1, dtype=DType.Float32, empty=True, device=y.carrier.device), 0, SCALAR)
+    g = _like(y)
+    # unit upstream gradient: no host-to-device upload inside the step
+    N.check(N.lib.sw_mse_f32(n, N.c_void_p(pp), N.c_void_p(tp), N.c_void_p(_ptr(loss)), None,
+                             N.c_void_p(_ptr(g)), None))
+    return loss, g
+
+
+def _sgd_update(weight: Any, dw: Tensor, lr: float) -> None:
+    wp, wn = _compact(weight, "weight")
+    N.check(N.lib.sw_elementwise_f32(N.SW_EW_AXPY, wn, N.c_void_p(wp), N.c_void_p(_ptr(dw)), N.c_void_p(wp),
+                                     -float(lr), None))
+    weight.carrier._increment_version()
+
+
+def _train_step_dual(model: "MLP", x: Tensor, target: Tensor, lr: float) -> Tensor | None:
+    from . import kernels, mx
+    from .carrier import CUDA
+    from .layout_plan import injective_layout_for, mode_leaves, single_stride
+
+    layers = model.layers
+    codes = {mx.FORMATS[layer.fmt][2] for layer in layers}
+    if len(codes) != 1:
+        return None
+    code = codes.pop()
+    q = 256 if code == N.SW_MX_E2M1 else 128
+    geo = mx.dual_geometry(x)
+    if geo is None or any(mx.dual_geometry(layer.weight) is None for layer in layers):
+        return None
+    B = geo[2] if geo[4] else geo[1]
+    if B % q or any(layer.in_features % q or layer.out_features % q for layer in layers):
+        return None
+    if x.layout.shape.top_level[1] != layers[0].in_features:
+        raise ValueError("Matmul inner dimensions must match")
+    dev = x.carrier.device
+
+    def rb(k: int) -> int:
+        return kernels.mx_row_bytes(code, k)
+
+    def gemm(a: Any, b: Any, out: Tensor, M: int, Nn: int, K: int) -> None:
+        (_, s0), (_, s1) = single_stride(mode_leaves(out.layout, 0)), single_stride(mode_leaves(out.layout, 1))
+        kernels.mx_gemm(code, a[0].data_ptr, rb(K), a[1].data_ptr, b[0].data_ptr, rb(K), b[1].data_ptr,
+                        _ptr(out), M, Nn, K, ldc_m=s0, ldc_n=s1)
+
+    # forward: the operands of each layer's input (x, then gelu(h)) and weights
+    wq = [mx.quantize_both(layer.weight, code, need_tT=i > 0) for i, layer in enumerate(layers)]
+    aq = [mx.quantize_both(x, code)]
+    pres = []
+    for i, layer in enumerate(layers):
+        lay = canonical_layout(x.layout.shape.top_level[0], layer.weight.layout.shape.top_level[0])
+        h = Tensor(CUDA(lay.cosize, dtype=DType.Float32, empty=True, device=dev), 0, lay)
+        gemm(aq[i][0], wq[i][0], h, B, layer.out_features, layer.in_features)
+        pres.append(h)
+        if i + 1 < len(layers):
+            aq.append(mx.quantize_both(h, code, transform=N.SW_XF_GELU))
+            if aq[-1] is None:
+                raise RuntimeError("the two-way quantiser refused a contraction result")
+    loss, g = _mse_and_grad(pres[-1], target)
+    g_h, xf = None, N.SW_XF_NONE
+    for i in reversed(range(len(layers))):
+        layer = layers[i]
+        qg = mx.quantize_both(g, code, transform=xf, h=g_h, need_t=i > 0)
+        if qg is None:
+            raise RuntimeError("the two-way quantiser refused a gradient")
+        dx = None
+        if i > 0:
+            # dx[b, k] = sum_o g[b, o] w[o, k], stored like the layer input
+            lay = injective_layout_for(pres[i - 1].layout)
+            dx = Tensor(CUDA(lay.cosize, dtype=DType.Float32, empty=True, device=dev), 0, lay)
+            gemm(qg[0], wq[i][1], dx, B, layer.in_features, layer.out_features)
+        # dw[o, k] = sum_b g[b, o] a[b, k]
+        lay = injective_layout_for(layer.weight.layout)
+        dw = Tensor(CUDA(lay.cosize, dtype=DType.Float32, empty=True, device=dev), 0, lay)
+        gemm(qg[1], aq[i][1], dw, layer.out_features, layer.in_features, B)
+        _sgd_update(layer.weight, dw, lr)
+        if i > 0:
+            g, g_h, xf = dx, pres[i - 1], N.SW_XF_GELU_GRAD
+    return loss
+
+
+def _train_step_separate(model: "MLP", x: Tensor, target: Tensor, lr: float) -> Tensor:
+    """The same step with one kernel per elementwise operation and one
+    quantisation per contraction operand."""
     from . import mx
 
-    with no_grad():
-        acts, pres = [x], []
-        for i, layer in enumerate(model.layers):
-            h = mx.linear_forward(acts[-1], layer.weight, layer.fmt)
-            pres.append(h)
-            acts.append(gelu(h) if i + 1 < len(model.layers) else h)
-        y = acts[-1]
-        pp, n = _compact(y, "pred")
-        tp, _ = _compact(target, "target")
-        if y.layout != target.layout:
-            raise ValueError("pred and target layouts must match")
-        from .carrier import CUDA
-
-        loss = Tensor(CUDA(1, dtype=DType.Float32, empty=True, device=y.carrier.device), 0, SCALAR)
-        g = _like(y)
-        # unit upstream gradient: no host-to-device upload inside the step
-        N.check(N.lib.sw_mse_f32(n, N.c_void_p(pp), N.c_void_p(tp), N.c_void_p(_ptr(loss)), None,
-                                 N.c_void_p(_ptr(g)), None))
-        for i in reversed(range(len(model.layers))):
-            layer = model.layers[i]
-            dx, dw = mx.linear_backward(acts[i], layer.weight, g, layer.fmt, need_dx=i > 0)
-            wp, wn = _compact(layer.weight, "weight")
-            N.check(N.lib.sw_elementwise_f32(N.SW_EW_AXPY, wn, N.c_void_p(wp), N.c_void_p(_ptr(dw)), N.c_void_p(wp),
-                                             -float(lr), None))
-            layer.weight.carrier._increment_version()
-            if i > 0:
-                g = gelu_grad(pres[i - 1], dx)
+    acts, pres = [x], []
+    for i, layer in enumerate(model.layers):
+        h = mx.linear_forward(acts[-1], layer.weight, layer.fmt)
+        pres.append(h)
+        acts.append(gelu(h) if i + 1 < len(model.layers) else h)
+    loss, g = _mse_and_grad(acts[-1], target)
+    for i in reversed(range(len(model.layers))):
+        layer = model.layers[i]
+        dx, dw = mx.linear_backward(acts[i], layer.weight, g, layer.fmt, need_dx=i > 0)
+        _sgd_update(layer.weight, dw, lr)
+        if i > 0:
+            g = gelu_grad(pres[i - 1], dx)
     return loss
 
 

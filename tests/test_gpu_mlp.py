@@ -123,3 +123,44 @@ def test_fused_train_step_equals_the_autograd_step():
     assert abs(loss_a[0] - loss_b[0]) <= 1e-6 * abs(loss_a[0])
     for la, lb in zip(a.layers, b.layers):
         np.testing.assert_array_equal(la.weight.carrier.to_numpy(), lb.weight.carrier.to_numpy())
+
+
+@pytest.mark.parametrize("fmt", ["MXFP8_E4M3", "MXFP4"])
+def test_two_way_quantiser_step_equals_the_separate_kernels(fmt):
+    """The step that quantises each activation, weight and gradient once, both
+    ways, with the GELU (or its derivative) applied on the way in, leaves the
+    same weights and loss as the step of separate kernels, bit for bit."""
+    from strideweave_b200 import CUDA, nn
+
+    B, dims = 256, [256, 512, 768, 256]
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((B, dims[0])).astype(np.float32)
+    t = rng.standard_normal((B, dims[-1])).astype(np.float32)
+    xt = Tensor(CUDA.from_numpy(x.ravel()), 0, Layout(Shape([B, dims[0]]), Stride([dims[0], 1])))
+    tt = Tensor(CUDA.from_numpy(t.T.ravel().copy()), 0, Layout(Shape([B, dims[-1]]), Stride([1, B])))
+    a, b = nn.MLP(dims, fmt=fmt, seed=4), nn.MLP(dims, fmt=fmt, seed=4)
+    with sw.no_grad():
+        for _ in range(2):
+            la = nn._train_step_dual(a, xt, tt, 0.05)
+            lb = nn._train_step_separate(b, xt, tt, 0.05)
+            assert la is not None
+            assert abs(la[0] - lb[0]) <= 1e-6 * abs(lb[0])
+    for wa, wb in zip(a.layers, b.layers):
+        np.testing.assert_array_equal(wa.weight.carrier.to_numpy(), wb.weight.carrier.to_numpy())
+
+
+def test_untileable_batch_falls_back_to_the_separate_kernels():
+    from strideweave_b200 import CUDA, nn
+
+    B, dims = 128, [128, 256, 128]  # the batch is tileable, a 96-row input is not
+    rng = np.random.default_rng(2)
+    model = nn.MLP(dims, seed=1)
+    x = rng.standard_normal((B, dims[0])).astype(np.float32)
+    xt = Tensor(CUDA.from_numpy(x.T.ravel().copy()), 0, Layout(Shape([B, dims[0]]), Stride([1, B])))
+    tt = Tensor(CUDA.from_numpy(np.zeros(B * dims[-1], np.float32)), 0,
+                Layout(Shape([B, dims[-1]]), Stride([1, B])))
+    assert nn.MLP(dims, seed=1).train_step(xt, tt, lr=0.01)[0] > 0  # column-major input: the dual path reads it
+    odd = Tensor(CUDA.from_numpy(np.zeros(96 * dims[0], np.float32)), 0,
+                 Layout(Shape([96, dims[0]]), Stride([dims[0], 1])))
+    with sw.no_grad():
+        assert nn._train_step_dual(model, odd, tt, 0.01) is None
