@@ -46,10 +46,23 @@ constexpr int kBKBytes = 128;  // payload bytes of K per stage (one 128B swizzle
 constexpr int kThreads = 192;  // 6 warps
 constexpr int kTmemCols = 512;
 
-// kTmaEpi: the accumulator is drained into a 128-byte-swizzled shared-memory
-// tile (bf16, 128 x BN) and written by TMA bulk stores that run while the next
-// tile's MMAs do; the TMEM accumulator is released as soon as it is read.
-template <int FMT, int BN, int kStages, bool kTmaEpi>
+// Epilogues.  kEpiDirect stores from registers (any pitches, accumulation into
+// C).  The staged ones drain the accumulator into shared memory and write it
+// with TMA bulk stores that run while the next tile's MMAs do; the TMEM
+// accumulator is released as soon as it is read:
+//   kEpiBf16Rows - bf16, row-major C, the whole 128 x BN tile staged with the
+//                  128-byte swizzle;
+//   kEpiF32Rows  - fp32, row-major C, 128 x 32 chunks (128-byte swizzle)
+//                  rotating through kOutBufs buffers;
+//   kEpiF32Cols  - fp32, column-major C, the same chunks stored [32 n][128 m].
+constexpr int kEpiDirect = 0;
+constexpr int kEpiBf16Rows = 1;
+constexpr int kEpiF32Rows = 2;
+constexpr int kEpiF32Cols = 3;
+constexpr int kOutBufs = 4;
+constexpr int kChunkBytes = kBM * 32 * 4;  // one 128 x 32 fp32 chunk
+
+template <int FMT, int BN, int kStages, int kEpi>
 struct Cfg {
     static constexpr int kAtoms = FMT == SW_MX_E4M3 ? 1 : 2;      // scale atoms (4 blocks) per stage
     static constexpr int kABytes = kBM * kBKBytes;                 // 16 KiB
@@ -70,7 +83,8 @@ struct Cfg {
     static constexpr int kOffBar = kOffSfb + kStages * kSfbBytes;
     static constexpr int kNumBars = 2 * kStages + 3;
     static constexpr int kOffSlot = kOffBar + kNumBars * 8;
-    static constexpr int kStageOutBytes = kTmaEpi ? kBM * BN * 2 : 0;   // bf16 staging tile
+    static constexpr int kStageOutBytes =
+        kEpi == kEpiBf16Rows ? kBM * BN * 2 : (kEpi == kEpiDirect ? 0 : kOutBufs * kChunkBytes);
     static constexpr int kOffOut = (kOffSlot + 16 + 1023) / 1024 * 1024;
     static constexpr int kSmemBytes = kOffOut + kStageOutBytes + 1024;  // + alignment slack
     static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -95,11 +109,11 @@ struct GemmArgs {
     int out_bf16;
 };
 
-template <int FMT, int BN, int kStages, bool kTmaEpi>
+template <int FMT, int BN, int kStages, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
-    using C = Cfg<FMT, BN, kStages, kTmaEpi>;
+    using C = Cfg<FMT, BN, kStages, kEpi>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = ptx::smem_addr(smem);
@@ -124,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::fence_barrier_init();
         ptx::prefetch_tmap(&tmap_a);
         ptx::prefetch_tmap(&tmap_b);
-        if (kTmaEpi) ptx::prefetch_tmap(&tmap_c);
+        if (kEpi != kEpiDirect) ptx::prefetch_tmap(&tmap_c);
     }
     if (warp == 1) {
         ptx::tmem_alloc(ptx::smem_addr(tmem_slot), kTmemCols);
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_commit(bar_drain);
             ptx::mbar_wait(bar_drain, 0);
         }
-    } else if (kTmaEpi) {
+    } else if (kEpi == kEpiBf16Rows) {
         // ---------------- epilogue, staged through shared memory ----------------
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;   // row of the tile this thread drains
@@ -301,6 +315,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int g = 0; g < BN / 64; ++g)
                     ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, mb * kBM, stage_addr + g * (kBM * 128));
                 ptx::bulk_commit_group();
+            }
+        }
+        if (leader) ptx::bulk_wait_group0();
+    } else if (kEpi == kEpiF32Rows || kEpi == kEpiF32Cols) {
+        // ---------------- epilogue, fp32 chunks staged through shared memory ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;   // row of the tile this thread drains
+        const bool leader = threadIdx.x == 64;  // first epilogue thread issues the stores
+        float* stage_out = reinterpret_cast<float*>(smem + C::kOffOut);
+        const uint32_t stage_addr = sbase + C::kOffOut;
+        // As in the bf16 epilogue, every thread meets the same named barriers for
+        // every chunk even after a bounded wait has given up.
+        uint32_t tile_iter = 0, seq = 0;
+        bool alive = true;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
+            int mb, nb;
+            tile_coords(t, mb, nb);
+            if (alive && !ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) alive = false;
+            if (alive) ptx::tc_fence_after();
+#pragma unroll 1
+            for (int chunk = 0; chunk < BN / 32; ++chunk, ++seq) {
+                const int buf = int(seq % kOutBufs);
+                uint32_t r[32];
+                if (alive) {
+                    ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + chunk * 32, r);
+                    ptx::tmem_ld_wait();
+                    if (chunk == BN / 32 - 1) {
+                        // the accumulator is in registers: the next tile may start
+                        ptx::tc_fence_before();
+                        ptx::mbar_arrive(bar_tmem_empty);
+                    }
+                    // the store that last read this buffer must be done with it
+                    if (leader) ptx::bulk_wait_group_read<kOutBufs - 1>();
+                }
+                ptx::named_barrier(1, 128);
+                if (alive) {
+                    float* b = stage_out + buf * (kChunkBytes / 4);
+                    if (kEpi == kEpiF32Cols) {
+                        // [32 n][128 m]: the lanes of a warp write consecutive m
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) b[e * kBM + row] = __uint_as_float(r[e]);
+                    } else {
+                        // [128 m][32 n], 16-byte units swizzled by m % 8 (the map's 128-byte swizzle)
+                        float4* rowp = reinterpret_cast<float4*>(b + row * 32);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            rowp[u ^ (row & 7)] = make_float4(__uint_as_float(r[4 * u]), __uint_as_float(r[4 * u + 1]),
+                                                              __uint_as_float(r[4 * u + 2]),
+                                                              __uint_as_float(r[4 * u + 3]));
+                    }
+                    ptx::fence_proxy_async_smem();
+                }
+                ptx::named_barrier(1, 128);
+                if (leader && alive) {
+                    const uint32_t src = stage_addr + buf * kChunkBytes;
+                    if (kEpi == kEpiF32Cols)
+                        ptx::tma_store_2d(&tmap_c, mb * kBM, nb * BN + chunk * 32, src);
+                    else
+                        ptx::tma_store_2d(&tmap_c, nb * BN + chunk * 32, mb * kBM, src);
+                    ptx::bulk_commit_group();
+                }
             }
         }
         if (leader) ptx::bulk_wait_group0();
@@ -418,6 +493,23 @@ int make_output_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, in
     return SW_OK;
 }
 
+// 2-D fp32 map over an outer x inner matrix (row pitch ld_bytes), box
+// box_inner x box_outer, 128-byte swizzle when `swizzle` (a 32-float inner box).
+int make_output_map_f32(CUtensorMap* map, void* base, int64_t outer, int64_t inner, int64_t ld_bytes,
+                        uint32_t box_inner, uint32_t box_outer, bool swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return fail(SW_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SW_ERR_INVALID, "cuTensorMapEncodeTiled (fp32 output) failed (%d)", (int)r);
+    return SW_OK;
+}
+
 // 2-D uint8 map over rows x row_bytes (pitch ld), box 128 bytes x box_rows,
 // 128-byte swizzle (the canonical K-major layout of the UMMA descriptors).
 int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int64_t ld,
@@ -435,11 +527,11 @@ int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
     return SW_OK;
 }
 
-template <int FMT, int BN, int kStages, bool kTmaEpi>
+template <int FMT, int BN, int kStages, int kEpi>
 int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t* b, int64_t ldb,
                 const uint8_t* sfb, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N,
                 int64_t K, int beta_one, cudaStream_t stream) {
-    using Cf = Cfg<FMT, BN, kStages, kTmaEpi>;
+    using Cf = Cfg<FMT, BN, kStages, kEpi>;
     const int64_t row_bytes = FMT == SW_MX_E4M3 ? K : K / 2;
     CUtensorMap ma, mb;
     int rc = make_operand_map(&ma, a, M, row_bytes, lda, kBM);
@@ -448,10 +540,10 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     if (rc != SW_OK) return rc;
     CUtensorMap mc;
     memset(&mc, 0, sizeof(mc));
-    if (kTmaEpi) {
-        rc = make_output_map(&mc, c, M, N, ldc_m * 2);
-        if (rc != SW_OK) return rc;
-    }
+    if (kEpi == kEpiBf16Rows) rc = make_output_map(&mc, c, M, N, ldc_m * 2);
+    if (kEpi == kEpiF32Rows) rc = make_output_map_f32(&mc, c, M, N, ldc_m * 4, 32, kBM, true);
+    if (kEpi == kEpiF32Cols) rc = make_output_map_f32(&mc, c, N, M, ldc_n * 4, kBM, 32, false);
+    if (rc != SW_OK) return rc;
     GemmArgs args;
     args.sfa = sfa;
     args.sfb = sfb;
@@ -465,7 +557,7 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.katoms = (int)((K / 32 + 3) / 4);
     args.beta_one = beta_one;
     args.out_bf16 = out_dtype == SW_OUT_BF16;
-    auto kernel = mx_gemm_kernel<FMT, BN, kStages, kTmaEpi>;
+    auto kernel = mx_gemm_kernel<FMT, BN, kStages, kEpi>;
     SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
                 "set gemm smem");
     int dev = 0, sms = 148;
@@ -507,21 +599,29 @@ extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, c
         return fail(SW_ERR_INVALID, "sw_mx_gemm: payload and scale planes must be 16-byte aligned");
     if (ldc_m < 1 || ldc_n < 1) return fail(SW_ERR_INVALID, "sw_mx_gemm: output pitches must be positive");
     cudaStream_t s = (cudaStream_t)stream;
-    // bf16 row-major results without accumulation take the staged TMA epilogue
-    // (3 mainloop stages + the 64 KiB staging tile); everything else stores
-    // straight from registers (4 stages).
-    const bool tma_epi = out_dtype == SW_OUT_BF16 && ldc_n == 1 && !beta_one && N % 256 == 0 &&
-                         (ldc_m * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+    // Results without accumulation, with a unit pitch on either side, take a
+    // staged TMA epilogue (3 mainloop stages + the staging buffers); anything
+    // else stores straight from registers (4 stages).
+    const bool aligned_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+    const int esize = out_dtype == SW_OUT_BF16 ? 2 : 4;
+    int epi = kEpiDirect;
+    if (!beta_one && N % 256 == 0 && aligned_c) {
+        if (ldc_n == 1 && (ldc_m * esize) % 16 == 0 && ldc_m >= N)
+            epi = out_dtype == SW_OUT_BF16 ? kEpiBf16Rows : kEpiF32Rows;
+        else if (out_dtype == SW_OUT_F32 && ldc_m == 1 && (ldc_n * 4) % 16 == 0 && ldc_n >= M)
+            epi = kEpiF32Cols;
+    }
     int rc;
 #define SW_GEMM(F, BNV, ST, EPI) \
     launch_gemm<F, BNV, ST, EPI>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K, beta_one, s)
-    if (fmt_a == SW_MX_E4M3) {
-        rc = tma_epi ? SW_GEMM(SW_MX_E4M3, 256, 3, true)
-                     : (N % 256 == 0 ? SW_GEMM(SW_MX_E4M3, 256, 4, false) : SW_GEMM(SW_MX_E4M3, 128, 4, false));
-    } else {
-        rc = tma_epi ? SW_GEMM(SW_MX_E2M1, 256, 3, true)
-                     : (N % 256 == 0 ? SW_GEMM(SW_MX_E2M1, 256, 4, false) : SW_GEMM(SW_MX_E2M1, 128, 4, false));
-    }
+#define SW_GEMM_FMT(F)                                                                  \
+    (epi == kEpiBf16Rows  ? SW_GEMM(F, 256, 3, kEpiBf16Rows)                             \
+     : epi == kEpiF32Rows ? SW_GEMM(F, 256, 3, kEpiF32Rows)                              \
+     : epi == kEpiF32Cols ? SW_GEMM(F, 256, 3, kEpiF32Cols)                              \
+     : N % 256 == 0       ? SW_GEMM(F, 256, 4, kEpiDirect)                               \
+                          : SW_GEMM(F, 128, 4, kEpiDirect))
+    rc = fmt_a == SW_MX_E4M3 ? SW_GEMM_FMT(SW_MX_E4M3) : SW_GEMM_FMT(SW_MX_E2M1);
+#undef SW_GEMM_FMT
 #undef SW_GEMM
     if (rc != SW_OK) return rc;
     return ok();

@@ -101,14 +101,41 @@ def test_narrow_tile_path_and_layouts(fmt):
 
 
 @pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
-def test_many_tiles_persistent_schedule(fmt):
+@pytest.mark.parametrize("col_major", [False, True])
+def test_many_tiles_persistent_schedule(fmt, col_major):
     # more tiles than SMs, several K stages per tile, activations N(0,1) and
-    # weights N(0, 0.02) as in the large contraction configs
+    # weights N(0, 0.02) as in the large contraction configs; fp32 C in either
+    # order goes through the staged epilogue's rotating chunk buffers
     M, N_, K = 2048, 2560, 1024
     A, B, da, db = operands(fmt, M, N_, K, seed=5, b_sigma=0.02)
-    got = run_gemm(fmt, A, B, M, N_, K)
+    got = run_gemm(fmt, A, B, M, N_, K, col_major=col_major)
     want = da.astype(np.float64) @ db.astype(np.float64).T
     assert rel_frobenius(got, want) <= 1e-5
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
+@pytest.mark.parametrize("col_major", [False, True])
+def test_staged_fp32_epilogue_equals_the_direct_stores(fmt, col_major):
+    # pitched fp32 C: the staged TMA-store epilogue (no accumulation) against
+    # the register-store epilogue (accumulation onto zeros), bit for bit
+    from strideweave_b200 import kernels
+
+    M, N_, K = 384, 512, 512
+    (pa, sa, ra), (pb, sb, rb), _, _ = operands(fmt, M, N_, K, seed=12)
+    ldc_m, ldc_n = (1, M + 32) if col_major else (N_ + 64, 1)
+    span = (N_ - 1) * ldc_n + (M - 1) * ldc_m + 1
+    outs = []
+    for beta_one in (False, True):
+        c = empty(4 * span, fill=0)
+        kernels.mx_gemm(fmt, pa.ptr, ra, sa.ptr, pb.ptr, rb, sb.ptr, c.ptr, M, N_, K, ldc_m=ldc_m, ldc_n=ldc_n,
+                        beta_one=beta_one)
+        N.raise_device_status()
+        outs.append(to_host(c, span, np.float32) + np.float32(0.0))  # +0 folds a -0 sum into +0
+    np.testing.assert_array_equal(outs[0], outs[1])
+    idx = np.arange(M)[:, None] * ldc_m + np.arange(N_)[None, :] * ldc_n
+    untouched = np.ones(span, bool)
+    untouched[idx.ravel()] = False
+    assert not outs[0][untouched].any()  # the pitch gaps are not written
 
 
 @pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
