@@ -253,7 +253,7 @@ def main() -> None:
     ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed busy time under the clock sampler before the timed region")
-    ap.add_argument("--profile-case", choices=["reduce", "quantize", "mxfp8", "mxfp4", "mlp"],
+    ap.add_argument("--profile-case", choices=["reduce", "quantize", "dual", "mxfp8", "mxfp4", "mlp"],
                     help="run a short, fixed sequence of launches for ncu and exit (no timing)")
     ap.add_argument("--reps", type=int, default=2, help="rounds of launches of --profile-case")
     args = ap.parse_args()
@@ -543,6 +543,35 @@ def bench_quantize(torch, N, kernels, s, stream) -> dict:
                                       "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
                                       "bytes": moved}
         del pay, sc
+    # the MLP's two-way quantiser: S = x * gelu'(h) over a [4096 x 8192] hidden
+    # gradient (two 128 MiB reads), both MXFP8 operands written
+    r2, c2 = 4096, 8192
+    xs = [srcs[i].view(-1)[: r2 * c2] for i in range(2)]
+    hs = [srcs[1 - i].view(-1)[r2 * c2:] for i in range(2)]
+    planes = [(N.DeviceBuffer(r2 * c2), N.DeviceBuffer(kernels.scale_bytes_tc128(r2, c2 // 32))),
+              (N.DeviceBuffer(r2 * c2), N.DeviceBuffer(kernels.scale_bytes_tc128(c2, r2 // 32)))]
+    moved = 2 * r2 * c2 * 4 + 2 * r2 * c2 + kernels.scale_bytes_tc128(r2, c2 // 32) + \
+        kernels.scale_bytes_tc128(c2, r2 // 32)
+
+    def qd(i):
+        kernels.mx_quantize_dual(N.SW_MX_E4M3, N.SW_XF_GELU_GRAD, xs[i % 2].data_ptr(), hs[i % 2].data_ptr(), r2, c2,
+                                 c2, (planes[0][0].ptr, planes[0][1].ptr), (planes[1][0].ptr, planes[1][1].ptr),
+                                 stream=s)
+    for i in range(4):
+        qd(i)
+    torch.cuda.synchronize()
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        qd(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    gbs = moved / (us * 1e3)
+    out["mxfp8_dual_gelu_grad_4096x8192"] = {"us": round(us, 2), "gbs": round(gbs, 1),
+                                             "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                                             "bytes": moved}
     N.raise_device_status()
     return out
 
@@ -653,8 +682,11 @@ def profile_case(case: str, reps: int) -> None:
     reduce: the three layouts of X[8192 x 4096] x (sum, max, argmax), `reps`
     rounds (9 launches per round).  quantize: MXFP8 then MXFP4 of a Float32
     [8192 x 8192] along rows and along strided columns, `reps` rounds (4
-    launches per round).  mxfp8 / mxfp4: quantise two 8192 x 8192
-    operands, then `reps` contractions at M = N = K = 8192 (bf16 C).
+    launches per round).  dual: the two-way MXFP8 quantiser over a
+    [4096 x 8192] hidden activation, with GELU then with GELU', `reps` rounds
+    (2 launches per round).  mxfp8 / mxfp4: quantise two 8192 x 8192
+    operands, then `reps` contractions at M = N = K = 8192 (bf16 C).  mlp: the
+    MLP training step, `reps` steps after one warm-up step.
     """
     from strideweave_b200 import _native as N
     from strideweave_b200 import kernels
@@ -679,6 +711,23 @@ def profile_case(case: str, reps: int) -> None:
                 N.synchronize()
         N.raise_device_status()
         print("profile case quantize: ok")
+        return
+    if case == "dual":
+        rows, cols = 4096, 8192
+        rng = np.random.default_rng(8)
+        x, h = N.DeviceBuffer(rows * cols * 4), N.DeviceBuffer(rows * cols * 4)
+        x.upload(rng.standard_normal((rows, cols)).astype(np.float32))
+        h.upload((rng.standard_normal((rows, cols)) * 2).astype(np.float32))
+        pr, pc = N.DeviceBuffer(rows * cols), N.DeviceBuffer(rows * cols)
+        sr = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, cols // 32))
+        sc = N.DeviceBuffer(kernels.scale_bytes_tc128(cols, rows // 32))
+        for _ in range(reps):
+            for xf in (N.SW_XF_GELU, N.SW_XF_GELU_GRAD):
+                kernels.mx_quantize_dual(N.SW_MX_E4M3, xf, x.ptr, h.ptr, rows, cols, cols, (pr.ptr, sr.ptr),
+                                         (pc.ptr, sc.ptr))
+            N.synchronize()
+        N.raise_device_status()
+        print("profile case dual: ok")
         return
     if case == "reduce":
         x = np.random.default_rng(0).uniform(-1, 1, size=(R, C)).astype(np.float32)

@@ -253,6 +253,14 @@ __global__ void __launch_bounds__(256) quantize_strided(const float* __restrict_
     }
 }
 
+// 16-byte global -> shared copies that complete asynchronously (cp.async).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // ---- quantise: blocks along a strided axis with unit row stride ---------------
 // (a K x N operand quantised along K, i.e. the blocks of each of N rows run down
 // a column).  A CTA stages a 32 (block) x 128 (row) tile through shared memory
@@ -314,7 +322,9 @@ __global__ void __launch_bounds__(kTileRows, 8) quantize_cols_tiled(const float*
                     reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
                     reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
                 } else {
-                    for (int c = 0; c < len; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+#pragma unroll
+                    for (int c = 0; c < 32; ++c)
+                        if (c < len) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
                 }
             } else {
                 uint32_t w[4];
@@ -329,7 +339,9 @@ __global__ void __launch_bounds__(kTileRows, 8) quantize_cols_tiled(const float*
                 if (len == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
                     *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
                 } else {
-                    for (int c = 0; c < len; c += 2) {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 2) {
+                        if (c >= len) continue;
                         const uint8_t byte = uint8_t((w[c / 8] >> (4 * (c % 8))) & 0xFF);
                         if (c + 1 < len) dst[c / 2] = byte;
                         else dst[c / 2] = uint8_t((dst[c / 2] & 0xF0) | (byte & 0x0F));
@@ -350,9 +362,11 @@ __global__ void __launch_bounds__(kTileRows, 8) quantize_cols_tiled(const float*
 // pre-activation and x the upstream gradient: the same functions, with the same
 // operand order, as the elementwise kernels, so the planes are bit-identical to
 // those of the unfused sequence.
-// A CTA stages a 32 x 128 tile in which each 32-element row block is padded to
+// A CTA stages 32 x 128 tiles in which each 32-element row block is padded to
 // 36 floats: float4 reads along a row block (the row planes) and scalar reads
-// down a column (the column planes) are then both free of bank conflicts.
+// down a column (the column planes) are then both free of bank conflicts.  Two
+// stages: cp.async brings the CTA's next tile (and its h tile) while the
+// current one is transformed in place and quantised.
 constexpr int kDualRows = 32;
 constexpr int kDualCols = 128;
 constexpr int kDualPitch = 4 * 36;  // floats per staged row
@@ -365,32 +379,78 @@ __device__ __forceinline__ float4 dual_transform(float4 x, float4 h) {
     return x;
 }
 
+
+constexpr int kDualTileFloats = kDualRows * kDualPitch;
+
+// One block's packed payload: 16-byte stores where the destination allows.
+__device__ __forceinline__ void dual_store32(uint8_t* dst, const uint32_t (&w)[8]) {
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+        for (int c = 0; c < 32; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+    }
+}
+__device__ __forceinline__ void dual_store16(uint8_t* dst, const uint32_t (&w)[4]) {
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        for (int c = 0; c < 16; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
+    }
+}
+
+template <int XF>
+constexpr int dual_min_blocks() { return XF == SW_XF_GELU_GRAD ? 3 : 6; }
+
 template <int FMT, int XF>
-__global__ void __launch_bounds__(kDualCols, 8)
+__global__ void __launch_bounds__(kDualCols, dual_min_blocks<XF>())
     quantize_dual(const float* __restrict__ x, const float* __restrict__ h, int64_t rows, int64_t cols, int64_t ld,
                   uint8_t* __restrict__ pr, int64_t ldpr, uint8_t* __restrict__ sr, int lr, int64_t ldsr,
                   uint8_t* __restrict__ pc, int64_t ldpc, uint8_t* __restrict__ sc, int lc, int64_t ldsc) {
-    __shared__ __align__(16) float tile[kDualRows * kDualPitch];
+    extern __shared__ __align__(16) float dsm[];
+    // stage s: x tile at dsm + s * kDualTileFloats, h tile (GELU') after both x tiles
     pdl_enter();
     const int t = threadIdx.x;
     const int64_t ctiles = cols / kDualCols;
     const int64_t ntiles = (rows / kDualRows) * ctiles;
     const int c4 = t & 31;
-    for (int64_t tt = blockIdx.x; tt < ntiles; tt += gridDim.x) {
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(dsm));
+    auto issue = [&](int64_t tt, int stage) {
         const int64_t i0 = (tt / ctiles) * kDualRows;
         const int64_t j0 = (tt - (tt / ctiles) * ctiles) * kDualCols;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int r = (t >> 5) + 4 * k;
             const int64_t off = (i0 + r) * ld + j0 + 4 * c4;
-            const float4 v = __ldcs(reinterpret_cast<const float4*>(x + off));
-            const float4 hv = XF == SW_XF_GELU_GRAD ? __ldcs(reinterpret_cast<const float4*>(h + off)) : v;
-            *reinterpret_cast<float4*>(&tile[r * kDualPitch + (c4 >> 3) * 36 + (c4 & 7) * 4]) =
-                dual_transform<XF>(v, hv);
+            const int so = stage * kDualTileFloats + r * kDualPitch + (c4 >> 3) * 36 + (c4 & 7) * 4;
+            cp_async16(sbase + 4u * so, x + off);
+            if (XF == SW_XF_GELU_GRAD) cp_async16(sbase + 4u * (2 * kDualTileFloats + so), h + off);
+        }
+    };
+    int stage = 0;
+    if (int64_t(blockIdx.x) < ntiles) issue(blockIdx.x, 0);
+    cp_async_commit();
+    for (int64_t tt = blockIdx.x; tt < ntiles; tt += gridDim.x, stage ^= 1) {
+        const int64_t i0 = (tt / ctiles) * kDualRows;
+        const int64_t j0 = (tt - (tt / ctiles) * ctiles) * kDualCols;
+        if (tt + gridDim.x < ntiles) issue(tt + gridDim.x, stage ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();  // this thread's copies of tile tt have landed
+        float* tile = dsm + stage * kDualTileFloats;
+        if (XF != SW_XF_NONE) {
+            const float* htile = dsm + (2 + stage) * kDualTileFloats;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int r = (t >> 5) + 4 * k;
+                const int so = r * kDualPitch + (c4 >> 3) * 36 + (c4 & 7) * 4;
+                float4* q = reinterpret_cast<float4*>(tile + so);
+                const float4 v = *q;
+                const float4 hv = XF == SW_XF_GELU_GRAD ? *reinterpret_cast<const float4*>(htile + so) : v;
+                *q = dual_transform<XF>(v, hv);
+            }
         }
         __syncthreads();
         if (pr) {
-            // thread t: row t / 4 of the tile, 32-block t % 4
             const int row = t >> 2, blk = t & 3;
             const float4* src = reinterpret_cast<const float4*>(&tile[row * kDualPitch + blk * 36]);
             float m = 0.0f;
@@ -414,13 +474,7 @@ __global__ void __launch_bounds__(kDualCols, 8)
                                    : e4m3x4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
                                             __fmul_rn(v.w, inv));
                 }
-                uint8_t* dst = pr + r * ldpr + kb * 32;
-                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                } else {
-                    for (int c = 0; c < 32; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
-                }
+                dual_store32(pr + r * ldpr + kb * 32, w);
             } else {
                 uint32_t w[4];
 #pragma unroll
@@ -431,16 +485,10 @@ __global__ void __launch_bounds__(kDualCols, 8)
                                         __fmul_rn(b.z, inv), __fmul_rn(b.w, inv)};
                     w[g] = special ? 0u : e2m1x8(q);
                 }
-                uint8_t* dst = pr + r * ldpr + kb * 16;
-                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-                } else {
-                    for (int c = 0; c < 16; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
-                }
+                dual_store16(pr + r * ldpr + kb * 16, w);
             }
         }
         if (pc) {
-            // thread t: column t of the tile, one 32-block down its rows
             const float* src = &tile[(t >> 5) * 36 + (t & 31)];
             float m = 0.0f;
 #pragma unroll
@@ -460,13 +508,7 @@ __global__ void __launch_bounds__(kDualCols, 8)
                                             __fmul_rn(src[(4 * g + 1) * kDualPitch], inv),
                                             __fmul_rn(src[(4 * g + 2) * kDualPitch], inv),
                                             __fmul_rn(src[(4 * g + 3) * kDualPitch], inv));
-                uint8_t* dst = pc + r * ldpc + kb * 32;
-                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                } else {
-                    for (int c = 0; c < 32; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
-                }
+                dual_store32(pc + r * ldpc + kb * 32, w);
             } else {
                 uint32_t w[4];
 #pragma unroll
@@ -476,16 +518,12 @@ __global__ void __launch_bounds__(kDualCols, 8)
                     for (int e = 0; e < 8; ++e) q[e] = __fmul_rn(src[(8 * g + e) * kDualPitch], inv);
                     w[g] = special ? 0u : e2m1x8(q);
                 }
-                uint8_t* dst = pc + r * ldpc + kb * 16;
-                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-                } else {
-                    for (int c = 0; c < 16; ++c) dst[c] = uint8_t((w[c / 4] >> (8 * (c % 4))) & 0xFF);
-                }
+                dual_store16(pc + r * ldpc + kb * 16, w);
             }
         }
-        __syncthreads();  // the next tile overwrites the staging
+        __syncthreads();  // the next iteration's copies overwrite this stage
     }
+    cp_async_wait<0>();
 }
 
 // ---- dequantise ----------------------------------------------------------------
@@ -667,14 +705,17 @@ extern "C" int sw_mx_quantize_dual(int fmt, int transform, const float* x, const
                         "scale padding fill");
     }
     const int64_t tiles = (rows / kDualRows) * (cols / kDualCols);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sm_count_mx()) * 8));
+    const int per_sm = transform == SW_XF_GELU_GRAD ? 3 : 6;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sm_count_mx()) * per_sm));
     using Kernel = void (*)(const float*, const float*, int64_t, int64_t, int64_t, uint8_t*, int64_t, uint8_t*, int,
                             int64_t, uint8_t*, int64_t, uint8_t*, int, int64_t);
     Kernel kernel;
     if (transform == SW_XF_NONE) kernel = e4 ? quantize_dual<SW_MX_E4M3, SW_XF_NONE> : quantize_dual<SW_MX_E2M1, SW_XF_NONE>;
     else if (transform == SW_XF_GELU) kernel = e4 ? quantize_dual<SW_MX_E4M3, SW_XF_GELU> : quantize_dual<SW_MX_E2M1, SW_XF_GELU>;
     else kernel = e4 ? quantize_dual<SW_MX_E4M3, SW_XF_GELU_GRAD> : quantize_dual<SW_MX_E2M1, SW_XF_GELU_GRAD>;
-    SW_CUDA_TRY(launch_pdl(kernel, grid, kDualCols, 0, s, x, h, rows, cols, ld_x, payload_r, ld_payload_r, scales_r,
+    const size_t smem = size_t(transform == SW_XF_GELU_GRAD ? 4 : 2) * kDualTileFloats * sizeof(float);
+    SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "dual smem");
+    SW_CUDA_TRY(launch_pdl(kernel, grid, kDualCols, smem, s, x, h, rows, cols, ld_x, payload_r, ld_payload_r, scales_r,
                            scale_layout_r, ld_scales_r, payload_c, ld_payload_c, scales_c, scale_layout_c,
                            ld_scales_c),
                 "quantize_dual launch");
