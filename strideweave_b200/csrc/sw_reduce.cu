@@ -28,7 +28,7 @@
 //               per kept ordinal, pointer increments only, no index math.
 //   cols_affine - the kept mode is unit-stride and the reduced mode is one
 //               leaf: CTAs own 128 kept ordinals and a slice of the fibre;
-//               slices meet in a small scratch buffer (at most SMs x 4 x 128
+//               slices meet in a small scratch buffer (at most SMs x 3 x 128
 //               partials), folded by the last CTA of each column block.
 //   gather    - anything else: one warp per kept ordinal, scalar loads.
 #include <cooperative_groups.h>
@@ -562,6 +562,7 @@ __global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const f
 constexpr int kColsAffThreads = 256;
 constexpr int kColsAffWarps = kColsAffThreads / 32;
 constexpr int64_t kMaxColSlices = 256;  // slices of a split column walk
+constexpr int kColsAffPerSm = 3;        // resident CTAs per SM (80 registers a thread)
 
 // Column walk: kept leaf 0 is unit-stride; the reduced mode is one leaf
 // (extent n_red, stride `stride`, ordinal weight `weight`).  CTA (bx, by)
@@ -588,7 +589,7 @@ __device__ __forceinline__ ArgmaxOp::S load_partial<ArgmaxOp>(const ArgmaxOp::S*
 }
 
 template <class Op, bool kSwz, class Ord>
-__global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const float* __restrict__ x, DevPlan p,
+__global__ void __launch_bounds__(kColsAffThreads, kColsAffPerSm) reduce_cols_affine(const float* __restrict__ x, DevPlan p,
                                                                          int64_t stride, int64_t weight, void* out,
                                                                          typename Op::S* partials,
                                                                          unsigned* counters) {
@@ -616,9 +617,9 @@ __global__ void __launch_bounds__(kColsAffThreads, 4) reduce_cols_affine(const f
         w.iters = int((j1 - j0 + kColsAffWarps - 1) / kColsAffWarps);
         FastFold<Op, Ord> f;
         const float* ptr = x + phys<kSwz>(p.swz, col + w.off0);
-        // argmax carries an ordinal per component: a shallower unroll keeps
-        // it inside the register budget
-        constexpr int kU = Op::kKind == Kind::kArgmax ? 4 : 8;
+        // eight 16-byte loads in flight per lane (argmax included: the
+        // 80-register budget of three CTAs per SM holds its ordinals)
+        constexpr int kU = 8;
         if (fast_walk<Op, Ord, kU>(ptr, w.doff, w.iters, f)) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[e] = f.component(e, w.ord0, w.dord, Ord(0));
@@ -1000,16 +1001,15 @@ Launch choose(DevPlan& p, int kind, bool aligned) {
     }
     if (aligned && ku == 0 && p.n_kept % 4 == 0 && strides_mult4(p.kept, 0) && strides_mult4(p.red, -1)) {
         const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
-        // every CTA resident at once (4 per SM): no second, partial wave
-        const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * 4 / col_blocks);
+        // every CTA resident at once (kColsAffPerSm per SM): no second, partial wave
+        const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * kColsAffPerSm / col_blocks);
         if (p.red.rank == 1 && swizzle_commutes(p.swz, int64_t(kColsAffWarps) * p.red.stride[0])) {
             // slices meet in scratch memory: no cap from the cluster size.  The
             // number of CTAs per SM that streams fastest differs by operation
             // (measured on the 8192 x 4096 transposed walk, 64 column blocks:
-            // sum 6 slices, max 4, argmax 9; argmax keeps fewer loads in flight
-            // per warp and needs more warps, max loses more than sum to each
+            // sum 6 slices, max 5, argmax 6; max loses more than sum to each
             // additional slice of partials)
-            const double per_sm = kind == SW_REDUCE_SUM ? 2.5 : kind == SW_REDUCE_MAX ? 1.75 : 4.0;
+            const double per_sm = kind == SW_REDUCE_SUM ? 2.5 : kind == SW_REDUCE_MAX ? 2.0 : 2.6;
             const int64_t target = std::max<int64_t>(1, std::llround(double(sm_count()) * per_sm / double(col_blocks)));
             L.kernel = 4;
             L.splits = (int)std::max<int64_t>(1, std::min<int64_t>({std::min(target, std::max<int64_t>(want, 1)),
