@@ -74,6 +74,18 @@ int sw_stream_create(void** stream);
 int sw_stream_destroy(void* stream);
 int sw_stream_synchronize(void* stream);
 
+/* CUDA graphs of a stream's work, for a step that repeats with the same
+ * buffers (an MLP training step): capture starts on a stream from
+ * sw_stream_create and ends in an executable graph; the graph can then be
+ * launched on any stream, the legacy default stream (NULL) included, where it
+ * is ordered with every other carrier operation.  Between begin and end the
+ * calling thread may only enqueue work on that stream.  No reference
+ * counterpart: the reference executes eagerly on the host. */
+int sw_graph_capture_begin(void* stream);
+int sw_graph_capture_end(void* stream, void** graph_exec);
+int sw_graph_launch(void* graph_exec, void* stream);
+int sw_graph_destroy(void* graph_exec);
+
 /* Reads and clears the device-side error word that bounded waits and device
  * bound checks write (SW_OK if none fired).  Synchronises the device. */
 int sw_device_status(int* status);

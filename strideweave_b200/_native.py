@@ -87,6 +87,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_stream_create": (c_int, [POINTER(c_void_p)]),
     "sw_stream_destroy": (c_int, [c_void_p]),
     "sw_stream_synchronize": (c_int, [c_void_p]),
+    "sw_graph_capture_begin": (c_int, [c_void_p]),
+    "sw_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "sw_graph_launch": (c_int, [c_void_p, c_void_p]),
+    "sw_graph_destroy": (c_int, [c_void_p]),
     "sw_device_status": (c_int, [POINTER(c_int)]),
     "sw_reduce_f32": (c_int, [POINTER(ReducePlan), c_void_p, c_int64, c_void_p, c_void_p]),
     "sw_reduce_f32_noalloc": (c_int, [POINTER(ReducePlan), c_void_p, c_int64, c_void_p, c_void_p]),

@@ -166,6 +166,38 @@ int sw_stream_synchronize(void* stream) {
     return ok();
 }
 
+int sw_graph_capture_begin(void* stream) {
+    if (!stream) return fail(SW_ERR_INVALID, "sw_graph_capture_begin: capture needs a stream from sw_stream_create");
+    SW_CUDA_TRY(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal),
+                "cudaStreamBeginCapture");
+    return ok();
+}
+
+int sw_graph_capture_end(void* stream, void** graph_exec) {
+    if (!stream || !graph_exec) return fail(SW_ERR_INVALID, "sw_graph_capture_end: null argument");
+    *graph_exec = nullptr;
+    cudaGraph_t graph = nullptr;
+    SW_CUDA_TRY(cudaStreamEndCapture((cudaStream_t)stream, &graph), "cudaStreamEndCapture");
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t err = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    SW_CUDA_TRY(err, "cudaGraphInstantiate");
+    *graph_exec = (void*)exec;
+    return ok();
+}
+
+int sw_graph_launch(void* graph_exec, void* stream) {
+    if (!graph_exec) return fail(SW_ERR_INVALID, "sw_graph_launch: null graph");
+    SW_CUDA_TRY(cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream), "cudaGraphLaunch");
+    return ok();
+}
+
+int sw_graph_destroy(void* graph_exec) {
+    if (!graph_exec) return ok();
+    SW_CUDA_TRY(cudaGraphExecDestroy((cudaGraphExec_t)graph_exec), "cudaGraphExecDestroy");
+    return ok();
+}
+
 int sw_device_status(int* status) {
     if (!status) return fail(SW_ERR_INVALID, "sw_device_status: null output");
     SW_CUDA_TRY(cudaDeviceSynchronize(), "cudaDeviceSynchronize");

@@ -191,6 +191,10 @@ class MLP:
     def train_step(self, x: Tensor, target: Tensor, lr: float) -> Tensor:
         return train_step(self, x, target, lr)
 
+    def capture_step(self, x: Tensor, target: Tensor, lr: float) -> "CapturedTrainStep":
+        """``train_step(x, target, lr)`` captured in a CUDA graph (see CapturedTrainStep)."""
+        return CapturedTrainStep(self, x, target, lr)
+
 
 def gelu_grad(x: Tensor, g: Tensor) -> Tensor:
     """g * gelu'(x) (same layout as x)."""
@@ -253,69 +257,227 @@ def _sgd_update(weight: Any, dw: Tensor, lr: float) -> None:
     weight.carrier._increment_version()
 
 
+class _DualStep:
+    """The buffers and kernel arguments of one MLP training step through the
+    two-way quantiser, built once for a model and an input / target placement
+    and reused by every step, eager or captured in a CUDA graph.
+
+    Per step: each weight, the input, each hidden pre-activation (with the
+    GELU) and each gradient (with the GELU derivative) is quantised once into
+    the operands both of its contractions take; eight contractions; the MSE
+    loss and gradient; an in-place SGD update per weight.  Nothing is
+    allocated after construction except the caller's loss."""
+
+    @classmethod
+    def build(cls, model: "MLP", x: Tensor, target: Tensor) -> "_DualStep | None":
+        from . import mx
+
+        layers = model.layers
+        codes = {mx.FORMATS[layer.fmt][2] for layer in layers}
+        if len(codes) != 1:
+            return None
+        code = next(iter(codes))
+        q = 256 if code == N.SW_MX_E2M1 else 128
+        geo = mx.dual_geometry(x)
+        if geo is None or any(mx.dual_geometry(layer.weight) is None for layer in layers):
+            return None
+        B = geo[2] if geo[4] else geo[1]
+        if B % q or any(layer.in_features % q or layer.out_features % q for layer in layers):
+            return None
+        if x.layout.shape.top_level[1] != layers[0].in_features:
+            raise ValueError("Matmul inner dimensions must match")
+        return cls(model, x, target, code, B)
+
+    def __init__(self, model: "MLP", x: Tensor, target: Tensor, code: int, B: int) -> None:
+        from . import kernels, mx
+        from .carrier import CUDA
+        from .layout_plan import injective_layout_for, mode_leaves, single_stride
+
+        self.layers = model.layers
+        self.code, self.B = code, B
+        self.x, self.target = x, target
+        dev = x.carrier.device
+        elem = DType.E4M3 if code == N.SW_MX_E4M3 else DType.E2M1
+
+        def planes(n: int, k: int) -> tuple[Any, Any]:
+            return (CUDA(n * k, dtype=elem, empty=True, device=dev),
+                    CUDA(kernels.scale_bytes_tc128(n, k // 32), dtype=DType.E8M0, empty=True, device=dev))
+
+        def f32(layout: Layout) -> Tensor:
+            return Tensor(CUDA(layout.cosize, dtype=DType.Float32, empty=True, device=dev), 0, layout)
+
+        def strides(t: Tensor) -> tuple[int, int]:
+            return single_stride(mode_leaves(t.layout, 0))[1], single_stride(mode_leaves(t.layout, 1))[1]
+
+        L = len(self.layers)
+        self.wq = [(planes(l.out_features, l.in_features), planes(l.in_features, l.out_features) if i > 0 else None)
+                   for i, l in enumerate(self.layers)]
+        self.aq = [(planes(B, l.in_features), planes(l.in_features, B)) for l in self.layers]
+        self.h = [f32(canonical_layout(x.layout.shape.top_level[0], l.weight.layout.shape.top_level[0]))
+                  for l in self.layers]
+        if self.h[-1].layout != target.layout:
+            raise ValueError("pred and target layouts must match")
+        self.g = f32(self.h[-1].layout)
+        self.qg = [(planes(B, l.out_features) if i > 0 else None, planes(l.out_features, B))
+                   for i, l in enumerate(self.layers)]
+        self.dx = [None] + [f32(injective_layout_for(self.h[i - 1].layout)) for i in range(1, L)]
+        self.dw = [f32(injective_layout_for(l.weight.layout)) for l in self.layers]
+        self.n_out = self.h[-1].size()
+        # every call of a step, with its arguments resolved to integers
+        self.calls: list[tuple[str, tuple]] = []
+        for i, layer in enumerate(self.layers):
+            self._dual(layer.weight, N.SW_XF_NONE, None, self.wq[i][0], self.wq[i][1])
+        self._dual(x, N.SW_XF_NONE, None, self.aq[0][0], self.aq[0][1])
+        for i, layer in enumerate(self.layers):
+            self._gemm(self.aq[i][0], self.wq[i][0], self.h[i], B, layer.out_features, layer.in_features, strides)
+            if i + 1 < L:
+                self._dual(self.h[i], N.SW_XF_GELU, None, self.aq[i + 1][0], self.aq[i + 1][1])
+        self.calls.append(("mse", (self.n_out, _ptr(self.h[-1]), _ptr(target), _ptr(self.g))))
+        g, g_h, xf = self.g, None, N.SW_XF_NONE
+        for i in reversed(range(L)):
+            layer = self.layers[i]
+            self._dual(g, xf, g_h, self.qg[i][0], self.qg[i][1])
+            if i > 0:
+                # dx[b, k] = sum_o g[b, o] w[o, k], stored like the layer input
+                self._gemm(self.qg[i][0], self.wq[i][1], self.dx[i], B, layer.in_features, layer.out_features,
+                           strides)
+            # dw[o, k] = sum_b g[b, o] a[b, k]
+            self._gemm(self.qg[i][1], self.aq[i][1], self.dw[i], layer.out_features, layer.in_features, B, strides)
+            wp, wn = _compact(layer.weight, "weight")
+            self.calls.append(("axpy", (wn, wp, _ptr(self.dw[i]))))
+            if i > 0:
+                g, g_h, xf = self.dx[i], self.h[i - 1], N.SW_XF_GELU_GRAD
+
+    def _dual(self, t: Tensor, xf: int, h: Tensor | None, q_t: Any, q_tT: Any) -> None:
+        from . import mx
+
+        geo = mx.dual_geometry(t)
+        if geo is None or (h is not None and (h.layout != t.layout or mx.dual_geometry(h) is None)):
+            raise RuntimeError("the two-way quantiser cannot read a tensor of the step")
+        ptr, rows, cols, ld, transposed = geo
+        row_q, col_q = (q_tT, q_t) if transposed else (q_t, q_tT)
+        self.calls.append(("dual", (xf, ptr, _ptr(h) if h is not None else 0, rows, cols, ld,
+                                    (row_q[0].data_ptr, row_q[1].data_ptr) if row_q else None,
+                                    (col_q[0].data_ptr, col_q[1].data_ptr) if col_q else None)))
+
+    def _gemm(self, a: Any, b: Any, out: Tensor, M: int, Nn: int, K: int, strides: Any) -> None:
+        s0, s1 = strides(out)
+        self.calls.append(("gemm", (a[0].data_ptr, a[1].data_ptr, b[0].data_ptr, b[1].data_ptr, _ptr(out), M, Nn,
+                                    K, s0, s1)))
+
+    def run(self, loss_ptr: int, lr: float, stream: int = 0) -> None:
+        """Enqueues one step on `stream`; the loss lands at loss_ptr."""
+        from . import kernels
+
+        code = self.code
+        sp = N.c_void_p(stream or None)
+        for kind, a in self.calls:
+            if kind == "dual":
+                xf, ptr, hp, rows, cols, ld, rq, cq = a
+                kernels.mx_quantize_dual(code, xf, ptr, hp, rows, cols, ld, rq, cq, stream=stream)
+            elif kind == "gemm":
+                ap, asc, bp, bsc, cp, M, Nn, K, s0, s1 = a
+                rb = kernels.mx_row_bytes(code, K)
+                kernels.mx_gemm(code, ap, rb, asc, bp, rb, bsc, cp, M, Nn, K, ldc_m=s0, ldc_n=s1, stream=stream)
+            elif kind == "mse":
+                n, pp, tp, gp = a
+                N.check(N.lib.sw_mse_f32(n, N.c_void_p(pp), N.c_void_p(tp), N.c_void_p(loss_ptr), None,
+                                         N.c_void_p(gp), sp))
+            else:
+                wn, wp, dwp = a
+                N.check(N.lib.sw_elementwise_f32(N.SW_EW_AXPY, wn, N.c_void_p(wp), N.c_void_p(dwp),
+                                                 N.c_void_p(wp), -float(lr), sp))
+
+    def bump_weight_versions(self) -> None:
+        for layer in self.layers:
+            layer.weight.carrier._increment_version()
+
+
+def _dual_step_for(model: "MLP", x: Tensor, target: Tensor) -> _DualStep | None:
+    """The model's cached step for this input / target placement (rebuilt when
+    the placement or a weight's storage changes)."""
+    key = (x.carrier.data_ptr + 4 * x.offset, str(x.layout), target.carrier.data_ptr + 4 * target.offset,
+           str(target.layout), tuple(layer.weight.carrier.data_ptr for layer in model.layers))
+    cached = getattr(model, "_dual_step", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    model._dual_step = None  # release the previous buffers first
+    plan = _DualStep.build(model, x, target)
+    if plan is not None:
+        model._dual_step = (key, plan)
+    return plan
+
+
 def _train_step_dual(model: "MLP", x: Tensor, target: Tensor, lr: float) -> Tensor | None:
-    from . import kernels, mx
     from .carrier import CUDA
-    from .layout_plan import injective_layout_for, mode_leaves, single_stride
 
-    layers = model.layers
-    codes = {mx.FORMATS[layer.fmt][2] for layer in layers}
-    if len(codes) != 1:
+    plan = _dual_step_for(model, x, target)
+    if plan is None:
         return None
-    code = codes.pop()
-    q = 256 if code == N.SW_MX_E2M1 else 128
-    geo = mx.dual_geometry(x)
-    if geo is None or any(mx.dual_geometry(layer.weight) is None for layer in layers):
-        return None
-    B = geo[2] if geo[4] else geo[1]
-    if B % q or any(layer.in_features % q or layer.out_features % q for layer in layers):
-        return None
-    if x.layout.shape.top_level[1] != layers[0].in_features:
-        raise ValueError("Matmul inner dimensions must match")
-    dev = x.carrier.device
-
-    def rb(k: int) -> int:
-        return kernels.mx_row_bytes(code, k)
-
-    def gemm(a: Any, b: Any, out: Tensor, M: int, Nn: int, K: int) -> None:
-        (_, s0), (_, s1) = single_stride(mode_leaves(out.layout, 0)), single_stride(mode_leaves(out.layout, 1))
-        kernels.mx_gemm(code, a[0].data_ptr, rb(K), a[1].data_ptr, b[0].data_ptr, rb(K), b[1].data_ptr,
-                        _ptr(out), M, Nn, K, ldc_m=s0, ldc_n=s1)
-
-    # forward: the operands of each layer's input (x, then gelu(h)) and weights
-    wq = [mx.quantize_both(layer.weight, code, need_tT=i > 0) for i, layer in enumerate(layers)]
-    aq = [mx.quantize_both(x, code)]
-    pres = []
-    for i, layer in enumerate(layers):
-        lay = canonical_layout(x.layout.shape.top_level[0], layer.weight.layout.shape.top_level[0])
-        h = Tensor(CUDA(lay.cosize, dtype=DType.Float32, empty=True, device=dev), 0, lay)
-        gemm(aq[i][0], wq[i][0], h, B, layer.out_features, layer.in_features)
-        pres.append(h)
-        if i + 1 < len(layers):
-            aq.append(mx.quantize_both(h, code, transform=N.SW_XF_GELU))
-            if aq[-1] is None:
-                raise RuntimeError("the two-way quantiser refused a contraction result")
-    loss, g = _mse_and_grad(pres[-1], target)
-    g_h, xf = None, N.SW_XF_NONE
-    for i in reversed(range(len(layers))):
-        layer = layers[i]
-        qg = mx.quantize_both(g, code, transform=xf, h=g_h, need_t=i > 0)
-        if qg is None:
-            raise RuntimeError("the two-way quantiser refused a gradient")
-        dx = None
-        if i > 0:
-            # dx[b, k] = sum_o g[b, o] w[o, k], stored like the layer input
-            lay = injective_layout_for(pres[i - 1].layout)
-            dx = Tensor(CUDA(lay.cosize, dtype=DType.Float32, empty=True, device=dev), 0, lay)
-            gemm(qg[0], wq[i][1], dx, B, layer.in_features, layer.out_features)
-        # dw[o, k] = sum_b g[b, o] a[b, k]
-        lay = injective_layout_for(layer.weight.layout)
-        dw = Tensor(CUDA(lay.cosize, dtype=DType.Float32, empty=True, device=dev), 0, lay)
-        gemm(qg[1], aq[i][1], dw, layer.out_features, layer.in_features, B)
-        _sgd_update(layer.weight, dw, lr)
-        if i > 0:
-            g, g_h, xf = dx, pres[i - 1], N.SW_XF_GELU_GRAD
+    loss = Tensor(CUDA(1, dtype=DType.Float32, empty=True, device=x.carrier.device), 0, SCALAR)
+    plan.run(_ptr(loss), lr)
+    plan.bump_weight_versions()
     return loss
+
+
+class CapturedTrainStep:
+    """An MLP training step captured once in a CUDA graph and replayed.
+
+    ``step()`` launches the graph on the legacy default stream, where it is
+    ordered with every other carrier operation, and returns that step's loss.
+    The graph holds the addresses of ``x``, ``target`` and the weights: to
+    train on other data write it into ``x`` and ``target`` (the replay reads
+    their current contents).  ``lr`` is fixed at capture.  The step is the one
+    ``MLP.train_step`` runs (the two-way quantiser path), bit for bit.
+    """
+
+    def __init__(self, model: "MLP", x: Tensor, target: Tensor, lr: float) -> None:
+        from .carrier import CUDA
+
+        self._exec = None
+        self._stream = None
+        plan = _DualStep.build(model, x, target)
+        if plan is None:
+            raise NotImplementedError("CapturedTrainStep needs shapes the two-way quantiser tiles "
+                                      "(batch and features multiples of 128, 256 for MXFP4)")
+        self.plan = plan
+        self.loss = Tensor(CUDA(1, dtype=DType.Float32, empty=True, device=x.carrier.device), 0, SCALAR)
+        stream = N.c_void_p()
+        N.check(N.lib.sw_stream_create(N.ctypes.byref(stream)))
+        self._stream = stream.value
+        N.check(N.lib.sw_graph_capture_begin(N.c_void_p(self._stream)))
+        exec_ = N.c_void_p()
+        try:
+            plan.run(_ptr(self.loss), lr, self._stream)
+        finally:
+            rc = N.lib.sw_graph_capture_end(N.c_void_p(self._stream), N.ctypes.byref(exec_))
+        N.check(rc)
+        self._exec = exec_.value
+
+    def step(self) -> Tensor:
+        from .carrier import CUDA
+
+        if self._exec is None:
+            raise RuntimeError("the captured step was released")
+        N.check(N.lib.sw_graph_launch(N.c_void_p(self._exec), None))
+        self.plan.bump_weight_versions()
+        out = Tensor(CUDA(1, dtype=DType.Float32, empty=True, device=self.loss.carrier.device), 0, SCALAR)
+        N.check(N.lib.sw_memcpy_d2d(N.c_void_p(_ptr(out)), N.c_void_p(_ptr(self.loss)), 4, None))
+        return out
+
+    def close(self) -> None:
+        if self._exec is not None:
+            N.lib.sw_graph_destroy(N.c_void_p(self._exec))
+            self._exec = None
+        if self._stream is not None:
+            N.lib.sw_stream_destroy(N.c_void_p(self._stream))
+            self._stream = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _train_step_separate(model: "MLP", x: Tensor, target: Tensor, lr: float) -> Tensor:
@@ -368,4 +530,5 @@ class SGD:
 
 NN_OPERATIONS = {"gelu": CudaGelu, "mse_loss": CudaMSELoss}
 
-__all__ = ["GELU", "MLP", "MSELoss", "MXLinear", "SGD", "gelu", "gelu_grad", "mse_loss", "train_step"]
+__all__ = ["CapturedTrainStep", "GELU", "MLP", "MSELoss", "MXLinear", "SGD", "gelu", "gelu_grad", "mse_loss",
+           "train_step"]

@@ -164,3 +164,34 @@ def test_untileable_batch_falls_back_to_the_separate_kernels():
                  Layout(Shape([96, dims[0]]), Stride([dims[0], 1])))
     with sw.no_grad():
         assert nn._train_step_dual(model, odd, tt, 0.01) is None
+
+
+@pytest.mark.parametrize("fmt", ["MXFP8_E4M3", "MXFP4"])
+def test_captured_step_replays_the_eager_step(fmt):
+    """Three replays of the CUDA-graph step leave the weights and losses of
+    three eager steps, bit for bit; new data written into x is read by the
+    next replay."""
+    from strideweave_b200 import CUDA, nn
+
+    B, dims = 256, [256, 512, 256]
+    rng = np.random.default_rng(13)
+    x = rng.standard_normal((B, dims[0])).astype(np.float32)
+    t = rng.standard_normal((B, dims[-1])).astype(np.float32)
+    lay_x = Layout(Shape([B, dims[0]]), Stride([dims[0], 1]))
+    lay_t = Layout(Shape([B, dims[-1]]), Stride([1, B]))
+    a, b = nn.MLP(dims, fmt=fmt, seed=2), nn.MLP(dims, fmt=fmt, seed=2)
+    xa, ta = Tensor(CUDA.from_numpy(x.ravel()), 0, lay_x), Tensor(CUDA.from_numpy(t.T.ravel().copy()), 0, lay_t)
+    xb, tb = Tensor(CUDA.from_numpy(x.ravel()), 0, lay_x), Tensor(CUDA.from_numpy(t.T.ravel().copy()), 0, lay_t)
+    graph = b.capture_step(xb, tb, lr=0.05)
+    x2 = rng.standard_normal((B, dims[0])).astype(np.float32)
+    for k in range(3):
+        if k == 2:  # new data: eager gets a new tensor, the graph gets it written into its input
+            xa = Tensor(CUDA.from_numpy(x2.ravel()), 0, lay_x)
+            xb.carrier.upload_raw(x2.ravel())
+        la = a.train_step(xa, ta, lr=0.05)
+        lb = graph.step()
+        assert abs(la[0] - lb[0]) <= 1e-6 * abs(la[0])  # an atomic sum over blocks
+    for wa, wb in zip(a.layers, b.layers):
+        np.testing.assert_array_equal(wa.weight.carrier.to_numpy(), wb.weight.carrier.to_numpy())
+    graph.close()
+
