@@ -95,6 +95,10 @@ int sw_device_status(int* status);
 #define SW_REDUCE_SUM 0
 #define SW_REDUCE_MAX 1
 #define SW_REDUCE_ARGMAX 2
+/* reduce_sum with accumulator_dtype=Float64: the Float32 elements are summed
+ * in binary64 and the sum is rounded once to binary32
+ * (src/strideweave/carriers/cpu/native/_cpu_accumulation.hpp:38-41). */
+#define SW_REDUCE_SUM_F64 3
 
 /* A two-mode (kept, reduced) Float32 view lowered to flat leaf arrays.
  * Leaves are listed first-leaf-fastest (StrideWeave's colexicographic order,
@@ -299,6 +303,19 @@ int sw_matmul_f32_batched(const float* a, int64_t sab, int64_t sam, int64_t sak,
                           float* c, int64_t scb, int64_t scm, int64_t scn,
                           int64_t batch, int64_t M, int64_t N, int64_t K,
                           void* stream);
+
+#define SW_ACC_F32 0 /* the default FLOATING / Float32 accumulator              */
+#define SW_ACC_F64 1 /* accumulator_dtype=Float64: binary32 products summed in
+                      * binary64, rounded once (operation_policy.py:784-815) */
+
+/* sw_matmul_f32_batched with a chosen accumulator (SW_ACC_*): the widened
+ * plan of CpuMatmulOperation (_cpu_accumulation.hpp:38-41), forward and
+ * backward alike. */
+int sw_matmul_f32_batched_ex(const float* a, int64_t sab, int64_t sam, int64_t sak,
+                             const float* b, int64_t sbb, int64_t sbn, int64_t sbk,
+                             float* c, int64_t scb, int64_t scm, int64_t scn,
+                             int64_t batch, int64_t M, int64_t N, int64_t K,
+                             int accumulator, void* stream);
 
 /* ---- binary elementwise -------------------------------------------------- */
 

@@ -30,6 +30,9 @@ SW_MAX_SWIZZLE = 4
 SW_REDUCE_SUM = 0
 SW_REDUCE_MAX = 1
 SW_REDUCE_ARGMAX = 2
+SW_REDUCE_SUM_F64 = 3
+SW_ACC_F32 = 0
+SW_ACC_F64 = 1
 
 SW_MX_E4M3 = 1
 SW_MX_E2M1 = 2
@@ -128,6 +131,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,
          c_int64, c_void_p],
+    ),
+    "sw_matmul_f32_batched_ex": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
+         c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p],
     ),
     "sw_matmul_f32_batched": (
         c_int,

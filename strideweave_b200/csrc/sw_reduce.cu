@@ -112,6 +112,20 @@ struct SumOp {
     }
 };
 
+// reduce_sum with accumulator_dtype=Float64: Float32 elements summed in
+// binary64, the result rounded once (_cpu_accumulation.hpp:38-41).  Only the
+// general gather walk instantiates it.
+struct SumOp64 {
+    static constexpr Kind kKind = Kind::kSum;
+    struct S { double v; };
+    static __device__ __forceinline__ S identity() { return {0.0}; }
+    static __device__ __forceinline__ void add(S& s, float v, int64_t) { s.v = __dadd_rn(s.v, double(v)); }
+    static __device__ __forceinline__ void merge(S& a, const S& b) { a.v = __dadd_rn(a.v, b.v); }
+    static __device__ __forceinline__ S shfl(const S& s, int lane_mask) {
+        return {__shfl_xor_sync(0xffffffffu, s.v, lane_mask)};
+    }
+};
+
 struct MaxOp {
     static constexpr Kind kKind = Kind::kMax;
     struct S { float v; int64_t j; };  // j only orders NaNs
@@ -160,6 +174,10 @@ __device__ __forceinline__ void store_result(void* out, int64_t i, const typenam
 template <>
 __device__ __forceinline__ void store_result<SumOp>(void* out, int64_t i, const SumOp::S& s) {
     static_cast<float*>(out)[i] = s.v;
+}
+template <>
+__device__ __forceinline__ void store_result<SumOp64>(void* out, int64_t i, const SumOp64::S& s) {
+    static_cast<float*>(out)[i] = __double2float_rn(s.v);
 }
 template <>
 __device__ __forceinline__ void store_result<MaxOp>(void* out, int64_t i, const MaxOp::S& s) {
@@ -1037,7 +1055,7 @@ namespace {
 int reduce_entry(const sw_reduce_plan* plan, const float* x, int64_t x_size, void* out, void* stream,
                  const ScratchSource& src) {
     if (!plan || !out) return fail(SW_ERR_INVALID, "sw_reduce_f32: null plan or output");
-    if (plan->kind < SW_REDUCE_SUM || plan->kind > SW_REDUCE_ARGMAX)
+    if (plan->kind < SW_REDUCE_SUM || plan->kind > SW_REDUCE_SUM_F64)
         return fail(SW_ERR_INVALID, "sw_reduce_f32: unknown reduction kind %d", plan->kind);
     if (plan->kept_rank < 0 || plan->kept_rank > SW_MAX_LEAVES || plan->reduced_rank < 0 ||
         plan->reduced_rank > SW_MAX_LEAVES || plan->swizzle_rank < 0 || plan->swizzle_rank > SW_MAX_SWIZZLE)
@@ -1064,7 +1082,8 @@ int reduce_entry(const sw_reduce_plan* plan, const float* x, int64_t x_size, voi
     }
     if (p.n_kept == 0) return ok();
     if (p.n_red == 0) {
-        if (plan->kind != SW_REDUCE_SUM) return fail(SW_ERR_INVALID, "reduction fibers must be non-empty");
+        if (plan->kind != SW_REDUCE_SUM && plan->kind != SW_REDUCE_SUM_F64)
+            return fail(SW_ERR_INVALID, "reduction fibers must be non-empty");
         SW_CUDA_TRY(cudaMemsetAsync(out, 0, size_t(p.n_kept) * 4, (cudaStream_t)stream), "zero sum");
         return ok();
     }
@@ -1091,10 +1110,17 @@ int reduce_entry(const sw_reduce_plan* plan, const float* x, int64_t x_size, voi
         if (hi_window >= x_size)
             return fail(SW_ERR_INVALID, "sw_reduce_f32: swizzle may address past the carrier end");
     }
+    cudaStream_t s = (cudaStream_t)stream;
+    if (plan->kind == SW_REDUCE_SUM_F64) {
+        // the widened sum walks any layout with the general gather kernel
+        const int64_t blocks = std::min<int64_t>((p.n_kept + 7) / 8, int64_t(sm_count()) * 8);
+        reduce_gather<SumOp64><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(x, p, out);
+        SW_LAUNCH_CHECK("reduction launch");
+        return ok();
+    }
     const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (p.offset % 4 == 0) &&
                          swizzle_keeps_vec4(p.swz);
     const Launch L = choose(p, plan->kind, aligned);
-    cudaStream_t s = (cudaStream_t)stream;
     int rc;
     switch (plan->kind) {
         case SW_REDUCE_SUM: rc = launch_for<SumOp>(x, p, L, out, s, src); break;

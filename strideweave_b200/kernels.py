@@ -17,7 +17,8 @@ from . import _native as N
 Leaf = tuple[int, int]  # (extent, stride)
 SwizzleStage = tuple[int, int, int]  # (bits, base, shift)
 
-REDUCE_KINDS = {"reduce_sum": N.SW_REDUCE_SUM, "reduce_max": N.SW_REDUCE_MAX, "argmax": N.SW_REDUCE_ARGMAX}
+REDUCE_KINDS = {"reduce_sum": N.SW_REDUCE_SUM, "reduce_max": N.SW_REDUCE_MAX, "argmax": N.SW_REDUCE_ARGMAX,
+                "reduce_sum_f64": N.SW_REDUCE_SUM_F64}
 
 
 def make_reduce_plan(kind: str, offset: int, kept: Sequence[Leaf], reduced: Sequence[Leaf],
@@ -137,6 +138,9 @@ def mx_gemm(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, 
 
 
 def matmul_f32(a_ptr: int, sam: int, sak: int, b_ptr: int, sbn: int, sbk: int, c_ptr: int, scm: int, scn: int,
-               M: int, N_: int, K: int, *, stream: int = 0) -> None:
-    N.check(N.lib.sw_matmul_f32(c_void_p(a_ptr), sam, sak, c_void_p(b_ptr), sbn, sbk, c_void_p(c_ptr), scm, scn,
-                                M, N_, K, c_void_p(stream)))
+               M: int, N_: int, K: int, *, acc64: bool = False, stream: int = 0) -> None:
+    """C[m, n] = sum_k A[m, k] B[n, k] with binary32 products, summed in binary32
+    (or in binary64 and rounded once when ``acc64``)."""
+    N.check(N.lib.sw_matmul_f32_batched_ex(c_void_p(a_ptr), 0, sam, sak, c_void_p(b_ptr), 0, sbn, sbk,
+                                           c_void_p(c_ptr), 0, scm, scn, 1, M, N_, K,
+                                           N.SW_ACC_F64 if acc64 else N.SW_ACC_F32, c_void_p(stream)))

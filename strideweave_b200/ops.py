@@ -90,8 +90,10 @@ class CudaReduction(CudaOperation):
         plan = resolve_operation_plan(self.kind, tensor.carrier.dtype(), options=self._execution_options)
         require_capability(self._carrier_class(), plan)
         result = _new_result(tensor, output_layout, plan.output)
+        # the widened plan (accumulator_dtype=Float64) sums in binary64
+        kind = "reduce_sum_f64" if self.kind == "reduce_sum" and plan.accumulator_dtype is DType.Float64 else self.kind
         if n:
-            kernels.reduce_f32(self.kind, tensor.carrier.data_ptr, tensor.carrier.size(), tensor.offset,
+            kernels.reduce_f32(kind, tensor.carrier.data_ptr, tensor.carrier.size(), tensor.offset,
                                mode_leaves(layout, 0), mode_leaves(layout, 1), result.carrier.data_ptr,
                                swizzle=swizzle_stages(tensor.carrier))
         return result
@@ -194,10 +196,14 @@ class CudaMatmul(CudaOperation):
         plan = resolve_operation_plan("matmul", lhs.carrier.dtype(), rhs.carrier.dtype(),
                                       options=self._execution_options)
         require_capability(self._carrier_class(), plan)
+        # the widened plan sums the binary32 products in binary64; the backward
+        # contracts the same terms and keeps the forward's accumulator
+        # (tests/test_cpu_plan.py:193 pins this for the CPU carrier)
+        self.ctx["acc64"] = plan.accumulator_dtype is DType.Float64
         a, sam, sak, _ka = _strided(lhs)
         b, sbn, sbk, _kb = _strided(rhs)
         result = _new_result(lhs, output_layout, DType.Float32)
-        kernels.matmul_f32(a, sam, sak, b, sbn, sbk, result.carrier.data_ptr, 1, M, M, Nn, K)
+        kernels.matmul_f32(a, sam, sak, b, sbn, sbk, result.carrier.data_ptr, 1, M, M, Nn, K, acc64=self.ctx["acc64"])
         return result
 
     def backward(self, gradient: Any) -> tuple[Any, Any]:
@@ -212,10 +218,11 @@ class CudaMatmul(CudaOperation):
         g, sgm, sgn, _kg = _strided(gradient)
         dl, dlp, dlm, dlk, dls = _output(injective_layout_for(lhs.layout), lhs)
         dr, drp, drn, drk, drs = _output(injective_layout_for(rhs.layout), rhs)
+        acc64 = bool(self.ctx.get("acc64", False))
         # dlhs[m, k] = sum_n g[m, n] rhs[n, k]  (rhs viewed as [k, n])
-        kernels.matmul_f32(g, sgm, sgn, b, sbk, sbn, dlp, dlm, dlk, M, K, Nn)
+        kernels.matmul_f32(g, sgm, sgn, b, sbk, sbn, dlp, dlm, dlk, M, K, Nn, acc64=acc64)
         # drhs[n, k] = sum_m g[m, n] lhs[m, k]  (g viewed as [n, m], lhs as [k, m])
-        kernels.matmul_f32(g, sgn, sgm, a, sak, sam, drp, drn, drk, Nn, K, M)
+        kernels.matmul_f32(g, sgn, sgm, a, sak, sam, drp, drn, drk, Nn, K, M, acc64=acc64)
         return (_finish(dl, dls), _finish(dr, drs))
 
 
@@ -340,9 +347,11 @@ def declared_plans() -> list[Any]:
     f32 = DType.Float32
     return [
         resolve_operation_plan("reduce_sum", f32),
+        resolve_operation_plan("reduce_sum", f32, accumulator_dtype=DType.Float64),
         resolve_operation_plan("reduce_max", f32),
         resolve_operation_plan("argmax", f32),
         resolve_operation_plan("matmul", f32, f32),
+        resolve_operation_plan("matmul", f32, f32, accumulator_dtype=DType.Float64),
         resolve_operation_plan("gelu", f32),
         resolve_operation_plan("elementwise_mul", f32, f32),
     ]
