@@ -37,6 +37,7 @@
 
 #include "sw_common.cuh"
 #include "sw_ptx.cuh"
+#include "sw_tma.cuh"
 
 namespace sw {
 namespace {
@@ -462,20 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---- host side -------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void* p = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 // 2-D bf16 map over C (rows x cols, row pitch ld_bytes), box 64 x 128 with the
 // 128-byte swizzle of the epilogue's staging tile.

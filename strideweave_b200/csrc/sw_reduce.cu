@@ -116,7 +116,6 @@ struct SumOp {
 // binary64, the result rounded once (_cpu_accumulation.hpp:38-41).  Only the
 // general gather walk instantiates it.
 struct SumOp64 {
-    static constexpr Kind kKind = Kind::kSum;
     struct S { double v; };
     static __device__ __forceinline__ S identity() { return {0.0}; }
     static __device__ __forceinline__ void add(S& s, float v, int64_t) { s.v = __dadd_rn(s.v, double(v)); }
