@@ -36,6 +36,10 @@ R, C = 8192, 4096
 X_BYTES = R * C * 4
 RED_BYTES = X_BYTES + R * 4  # algorithmic bytes of one reduction launch
 LAYOUTS = ("rowmajor", "transposed", "tiled_swizzled")
+# DRAM bytes (read + write) per launch that ncu measured for each layout's
+# three reductions (mean), against 134,250,496 algorithmic bytes: the
+# committed `--profile-case reduce` capture of the kernels this file times.
+NCU_TRAFFIC = {"rowmajor": 139.70e6, "transposed": 138.00e6, "tiled_swizzled": 139.04e6}
 OPS = ("reduce_sum", "reduce_max", "argmax")
 SWZ = [(3, 2, 3)]
 
@@ -441,7 +445,9 @@ def main() -> None:
                        "parallelism": f"replicas x{world} (each rank its own X)"},
             "roofline": {"bound": "hbm", "kernel": f"sw_reduce_f32[{dominant}]", "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "peak_source": peaks["source"], "traffic": None,
+                         "peak_source": peaks["source"], "traffic": NCU_TRAFFIC.get(dominant),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, mean of the "
+                                           "layout's three kernels, from the committed --set full capture",
                          "per_layout_gbs": {lay: round(3 * RED_BYTES / (by_layout[lay] / 1e3) / 1e9, 1)
                                             for lay in LAYOUTS},
                          "per_kernel_gbs": {f"{op}/{lay}": round(RED_BYTES / (per_kernel[(op, lay)] / 1e3) / 1e9, 1)
