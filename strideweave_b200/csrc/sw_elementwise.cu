@@ -69,6 +69,50 @@ __global__ void __launch_bounds__(256) mse_grad_kernel(int64_t n, const float* _
         g[i] = s * (p[i] - t[i]);
 }
 
+// Loss and gradient in one pass (no upstream gradient: the loss is the root):
+// d = p - t once per element, grad = two_over_n * d, loss += sum d^2 / n.
+// The gradient is the same expression as mse_grad_kernel's; the loss sums in
+// another order (an atomic sum over blocks either way).  16-byte vectors when
+// `vec`.
+__global__ void __launch_bounds__(256) mse_fused_kernel(int64_t n, const float* __restrict__ p,
+                                                        const float* __restrict__ t, float* loss,
+                                                        float* __restrict__ g, float inv_n, float two_over_n,
+                                                        bool vec) {
+    float acc = 0.0f;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    const int64_t t0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    int64_t tail = 0;
+    if (vec) {
+        const int64_t nv = n / 4;
+        for (int64_t i = t0; i < nv; i += stride) {
+            const float4 a = reinterpret_cast<const float4*>(p)[i];
+            const float4 b = reinterpret_cast<const float4*>(t)[i];
+            const float d0 = a.x - b.x, d1 = a.y - b.y, d2 = a.z - b.z, d3 = a.w - b.w;
+            acc = fmaf(d0, d0, acc);
+            acc = fmaf(d1, d1, acc);
+            acc = fmaf(d2, d2, acc);
+            acc = fmaf(d3, d3, acc);
+            reinterpret_cast<float4*>(g)[i] = make_float4(two_over_n * d0, two_over_n * d1, two_over_n * d2,
+                                                          two_over_n * d3);
+        }
+        tail = nv * 4;
+    }
+    for (int64_t i = tail + t0; i < n; i += stride) {
+        const float d = p[i] - t[i];
+        acc = fmaf(d, d, acc);
+        g[i] = two_over_n * d;
+    }
+    for (int sh = 16; sh > 0; sh >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, sh);
+    __shared__ float part[8];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = 0.0f;
+        for (int w = 0; w < 8; ++w) b += part[w];
+        atomicAdd(loss, b * inv_n);
+    }
+}
+
 int grid_of(int64_t n) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -105,6 +149,16 @@ extern "C" int sw_mse_f32(int64_t n, const float* pred, const float* target, flo
     if (!pred || !target || (!loss && !grad)) return fail(SW_ERR_INVALID, "sw_mse_f32: null pointer");
     cudaStream_t s = (cudaStream_t)stream;
     const int grid = grid_of(n);
+    if (loss && grad && !upstream) {
+        // the training step's case: one pass writes the gradient and sums the loss
+        const bool vec = ((reinterpret_cast<uintptr_t>(pred) | reinterpret_cast<uintptr_t>(target) |
+                           reinterpret_cast<uintptr_t>(grad)) & 15) == 0;
+        SW_CUDA_TRY(cudaMemsetAsync(loss, 0, sizeof(float), s), "mse loss reset");
+        mse_fused_kernel<<<vec ? grid_of(n / 4 + 1) : grid, 256, 0, s>>>(n, pred, target, loss, grad,
+                                                                        1.0f / float(n), 2.0f / float(n), vec);
+        SW_LAUNCH_CHECK("sw_mse_f32 launch");
+        return ok();
+    }
     if (loss) {
         SW_CUDA_TRY(cudaMemsetAsync(loss, 0, sizeof(float), s), "mse loss reset");
         mse_loss_kernel<<<grid, 256, 0, s>>>(n, pred, target, loss, 1.0f / float(n));

@@ -195,3 +195,27 @@ def test_captured_step_replays_the_eager_step(fmt):
         np.testing.assert_array_equal(wa.weight.carrier.to_numpy(), wb.weight.carrier.to_numpy())
     graph.close()
 
+
+
+@pytest.mark.parametrize("n", [1 << 20, 1000003])
+def test_mse_loss_and_gradient_in_one_pass(n):
+    """sw_mse_f32 with loss and gradient and no upstream runs one fused pass:
+    the gradient equals the gradient-only call bit for bit, the loss the
+    loss-only call up to the order of its atomic sum."""
+    from strideweave_b200 import _native as N
+    from tests.gpu_util import empty, to_device, to_host
+
+    rng = np.random.default_rng(n)
+    p = rng.standard_normal(n).astype(np.float32)
+    t = rng.standard_normal(n).astype(np.float32)
+    dp, dt = to_device(p), to_device(t)
+    loss_a, grad_a = empty(4), empty(4 * n)
+    loss_b, grad_b = empty(4), empty(4 * n)
+    N.check(N.lib.sw_mse_f32(n, N.c_void_p(dp.ptr), N.c_void_p(dt.ptr), N.c_void_p(loss_a.ptr), None,
+                             N.c_void_p(grad_a.ptr), None))
+    N.check(N.lib.sw_mse_f32(n, N.c_void_p(dp.ptr), N.c_void_p(dt.ptr), N.c_void_p(loss_b.ptr), None, None, None))
+    N.check(N.lib.sw_mse_f32(n, N.c_void_p(dp.ptr), N.c_void_p(dt.ptr), None, None, N.c_void_p(grad_b.ptr), None))
+    np.testing.assert_array_equal(to_host(grad_a, n, np.float32), to_host(grad_b, n, np.float32))
+    la, lb = to_host(loss_a, 1, np.float32)[0], to_host(loss_b, 1, np.float32)[0]
+    want = float(np.mean((p.astype(np.float64) - t) ** 2))
+    assert abs(la - lb) <= 1e-5 * lb and abs(la - want) <= 1e-5 * want
