@@ -90,6 +90,13 @@ int sw_graph_destroy(void* graph_exec);
  * bound checks write (SW_OK if none fired).  Synchronises the device. */
 int sw_device_status(int* status);
 
+/* Exercises the device-side failure path without a fault: one thread waits,
+ * with the contraction pipeline's bounded wait and a limit of limit_ns
+ * (at most 1 s), on an mbarrier that nothing arrives on; the wait gives up,
+ * sw_device_status then reports SW_ERR_TIMEOUT and the context stays usable.
+ * No reference counterpart (the reference has no device waits). */
+int sw_probe_bounded_wait(int64_t limit_ns, void* stream);
+
 /* ---- layout-aware reductions -------------------------------------------- */
 
 #define SW_REDUCE_SUM 0

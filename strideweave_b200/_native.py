@@ -90,6 +90,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_stream_create": (c_int, [POINTER(c_void_p)]),
     "sw_stream_destroy": (c_int, [c_void_p]),
     "sw_stream_synchronize": (c_int, [c_void_p]),
+    "sw_probe_bounded_wait": (c_int, [c_int64, c_void_p]),
     "sw_graph_capture_begin": (c_int, [c_void_p]),
     "sw_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "sw_graph_launch": (c_int, [c_void_p, c_void_p]),

@@ -51,18 +51,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Waits for the phase of parity `parity` to complete.  Gives up after
-// kWaitLimitNs of wall time, records SW_ERR_TIMEOUT in the device error word
-// and returns false; the caller then unwinds.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// `limit_ns` of wall time (kWaitLimitNs by default), or after 2^30 polls
+// should the timer stall, records SW_ERR_TIMEOUT in the device error word and
+// returns false; the caller then unwinds.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
+    for (uint32_t i = 1; i < (1u << 30); ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-            report_device_error(SW_ERR_TIMEOUT);
-            return false;
-        }
+        if ((i & 255) == 0 && globaltimer_ns() - t0 > limit_ns) break;
     }
+    report_device_error(SW_ERR_TIMEOUT);
+    return false;
 }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

@@ -3,12 +3,26 @@
 #include <cstring>
 
 #include "sw_common.cuh"
+#include "sw_ptx.cuh"
 
 namespace sw {
 
 namespace {
 thread_local std::string t_last_error;
+
+// An mbarrier that nothing arrives on, waited for with the same bounded wait
+// the contraction's pipeline uses: the wait gives up after `limit_ns`, records
+// SW_ERR_TIMEOUT and the kernel returns.
+__global__ void bounded_wait_probe(unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t addr = ptx::smem_addr(&bar);
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(addr, 1);
+        ptx::fence_barrier_init();
+        ptx::mbar_wait(addr, 0, limit_ns);
+    }
 }
+}  // namespace
 
 __device__ int g_device_error = 0;
 
@@ -195,6 +209,14 @@ int sw_graph_launch(void* graph_exec, void* stream) {
 int sw_graph_destroy(void* graph_exec) {
     if (!graph_exec) return ok();
     SW_CUDA_TRY(cudaGraphExecDestroy((cudaGraphExec_t)graph_exec), "cudaGraphExecDestroy");
+    return ok();
+}
+
+int sw_probe_bounded_wait(int64_t limit_ns, void* stream) {
+    if (limit_ns < 0 || limit_ns > 1000000000)
+        return fail(SW_ERR_INVALID, "sw_probe_bounded_wait: the limit must lie in [0, 1 s]");
+    sw::bounded_wait_probe<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned long long)limit_ns);
+    SW_LAUNCH_CHECK("bounded wait probe launch");
     return ok();
 }
 
