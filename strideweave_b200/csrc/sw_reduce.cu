@@ -605,12 +605,48 @@ __device__ __forceinline__ ArgmaxOp::S load_partial<ArgmaxOp>(const ArgmaxOp::S*
     return {__ldcg(&p->v), (int64_t)__ldcg(reinterpret_cast<const long long*>(&p->j))};
 }
 
+// The column walk's partials, in shared memory and in scratch, in the
+// narrowest form that holds them: on a 32-bit-ordinal walk, max and argmax
+// keep their ordinal in 32 bits (8 bytes a partial instead of 16).  The
+// identity's "no ordinal" INT64_MAX maps to INT32_MAX, which no 32-bit walk
+// reaches (its ordinals stay below 2^30).
+template <class Op, class Ord>
+struct Packed {
+    using T = typename Op::S;
+    static __device__ __forceinline__ T pack(const typename Op::S& s) { return s; }
+    static __device__ __forceinline__ typename Op::S unpack(const T& t) { return t; }
+    static __device__ __forceinline__ T load(const T* p) { return load_partial<Op>(p); }
+};
+struct Packed8 {
+    float v;
+    int32_t j;
+};
+template <class Op>
+struct PackedOrd32 {
+    using T = Packed8;
+    static __device__ __forceinline__ T pack(const typename Op::S& s) {
+        return {s.v, s.j >= int64_t(INT32_MAX) ? INT32_MAX : int32_t(s.j)};
+    }
+    static __device__ __forceinline__ typename Op::S unpack(const T& t) {
+        return {t.v, t.j == INT32_MAX ? INT64_MAX : int64_t(t.j)};
+    }
+    static __device__ __forceinline__ T load(const T* p) {
+        const unsigned long long bits = __ldcg(reinterpret_cast<const unsigned long long*>(p));
+        return T{__uint_as_float(uint32_t(bits)), int32_t(uint32_t(bits >> 32))};
+    }
+};
+template <>
+struct Packed<MaxOp, int32_t> : PackedOrd32<MaxOp> {};
+template <>
+struct Packed<ArgmaxOp, int32_t> : PackedOrd32<ArgmaxOp> {};
+
 template <class Op, bool kSwz, class Ord>
 __global__ void __launch_bounds__(kColsAffThreads, kColsAffPerSm) reduce_cols_affine(const float* __restrict__ x, DevPlan p,
                                                                          int64_t stride, int64_t weight, void* out,
-                                                                         typename Op::S* partials,
+                                                                         typename Packed<Op, Ord>::T* partials,
                                                                          unsigned* counters) {
-    __shared__ typename Op::S part[kColsAffWarps][32][4];
+    using P = Packed<Op, Ord>;
+    __shared__ typename P::T part[kColsAffWarps][32][4];
     __shared__ unsigned s_last;
     pdl_enter();
     const int lane = threadIdx.x & 31;
@@ -645,21 +681,21 @@ __global__ void __launch_bounds__(kColsAffThreads, kColsAffPerSm) reduce_cols_af
         }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) part[warp][lane][e] = acc[e];
+    for (int e = 0; e < 4; ++e) part[warp][lane][e] = P::pack(acc[e]);
     __syncthreads();
     // warps 0..3 fold component `warp` (kept ordinal kv*4 + warp) of the 8 warps' partials
     typename Op::S v = Op::identity();
     const int64_t kept_i = kv * 4 + warp;
     if (warp < 4) {
-        v = part[0][lane][warp];
+        v = P::unpack(part[0][lane][warp]);
 #pragma unroll
-        for (int w = 1; w < kColsAffWarps; ++w) Op::merge(v, part[w][lane][warp]);
+        for (int w = 1; w < kColsAffWarps; ++w) Op::merge(v, P::unpack(part[w][lane][warp]));
     }
     if (splits == 1) {
         if (warp < 4 && live_col) store_result<Op>(out, kept_i, v);
         return;
     }
-    if (warp < 4 && live_col) partials[int64_t(split) * p.n_kept + kept_i] = v;
+    if (warp < 4 && live_col) partials[int64_t(split) * p.n_kept + kept_i] = P::pack(v);
     __threadfence();  // this CTA's partials are visible before its ticket is
     __syncthreads();
     if (threadIdx.x == 0) s_last = atomicAdd(&counters[blockIdx.x], 1u) == unsigned(splits - 1) ? 1u : 0u;
@@ -669,16 +705,16 @@ __global__ void __launch_bounds__(kColsAffThreads, kColsAffPerSm) reduce_cols_af
     if (warp < 4 && live_col) {
         // a batch of independent loads in flight before each round of merges:
         // the usual slice counts (about SMs x 4 / column blocks) take one round trip
-        constexpr int kB = sizeof(typename Op::S) > 4 ? 10 : 16;
+        constexpr int kB = sizeof(typename P::T) > 4 ? 10 : 16;
         typename Op::S r = Op::identity();
         for (int s0 = 0; s0 < splits; s0 += kB) {
-            typename Op::S q[kB];
+            typename P::T q[kB];
 #pragma unroll
             for (int u = 0; u < kB; ++u)
-                if (s0 + u < splits) q[u] = load_partial<Op>(partials + int64_t(s0 + u) * p.n_kept + kept_i);
+                if (s0 + u < splits) q[u] = P::load(partials + int64_t(s0 + u) * p.n_kept + kept_i);
 #pragma unroll
             for (int u = 0; u < kB; ++u)
-                if (s0 + u < splits) Op::merge(r, q[u]);
+                if (s0 + u < splits) Op::merge(r, P::unpack(q[u]));
         }
         store_result<Op>(out, kept_i, r);
     }
@@ -910,11 +946,12 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
     }
     // split column walk: more than one slice needs scratch for the partials
     const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
-    typename Op::S* partials = nullptr;
+    using PT = typename Packed<Op, Ord>::T;
+    PT* partials = nullptr;
     unsigned* counters = nullptr;
     if (L.splits > 1) {
         const size_t cbytes = (size_t(col_blocks) * sizeof(unsigned) + 255) & ~size_t(255);
-        const size_t need = cbytes + size_t(L.splits) * size_t(p.n_kept) * sizeof(typename Op::S);
+        const size_t need = cbytes + size_t(L.splits) * size_t(p.n_kept) * sizeof(PT);
         void* base = nullptr;
         if (src.base) {
             if (need > src.bytes)
@@ -930,7 +967,7 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
             if (rc != SW_OK) return rc;
         }
         counters = static_cast<unsigned*>(base);
-        partials = reinterpret_cast<typename Op::S*>(static_cast<char*>(base) + cbytes);
+        partials = reinterpret_cast<PT*>(static_cast<char*>(base) + cbytes);
     }
     const cudaError_t err = launch_pdl(reduce_cols_affine<Op, kSwz, Ord>, dim3((unsigned)col_blocks, (unsigned)L.splits),
                                        dim3(kColsAffThreads), 0, stream, x, p, L.cstride, L.cweight, out, partials,
