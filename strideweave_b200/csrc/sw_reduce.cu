@@ -1058,12 +1058,11 @@ Launch choose(DevPlan& p, int kind, bool aligned) {
         // every CTA resident at once (kColsAffPerSm per SM): no second, partial wave
         const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * kColsAffPerSm / col_blocks);
         if (p.red.rank == 1 && swizzle_commutes(p.swz, int64_t(kColsAffWarps) * p.red.stride[0])) {
-            // slices meet in scratch memory: no cap from the cluster size.  The
-            // number of CTAs per SM that streams fastest differs by operation
-            // (measured on the 8192 x 4096 transposed walk, 64 column blocks:
-            // sum 6 slices, max 5, argmax 6; max loses more than sum to each
-            // additional slice of partials)
-            const double per_sm = kind == SW_REDUCE_SUM ? 2.5 : kind == SW_REDUCE_MAX ? 2.0 : 2.6;
+            // slices meet in scratch memory: no cap from the cluster size.  About
+            // 2.6 CTAs per SM streams fastest for every operation (measured on
+            // the 8192 x 4096 transposed walk, 64 column blocks: 6 slices; with
+            // 16-byte max / argmax partials max preferred 5)
+            const double per_sm = 2.6;
             const int64_t target = std::max<int64_t>(1, std::llround(double(sm_count()) * per_sm / double(col_blocks)));
             L.kernel = 4;
             L.splits = (int)std::max<int64_t>(1, std::min<int64_t>({std::min(target, std::max<int64_t>(want, 1)),
