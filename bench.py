@@ -604,12 +604,13 @@ def quantize_generated(torch, N, kernels, fmt, rows, cols, seed, sigma=1.0, bloc
 def bench_sharded(torch, dist, N, kernels, mode, world, rank, steps=5, warmup=2) -> dict:
     """Config 5: sharded MXFP8 contraction M=65536, N=16384, K=16384, inputs
     N(0,1), at `world` GPUs; M-split (B replicated, no collective) or K-split
-    (NCCL reduce-scatter of Float32 partials, overlapped over 4 N-chunks)."""
+    (NCCL reduce-scatter of Float32 partials, overlapped over 8 N-chunks; the
+    contractions leave 32 SMs to the collective so the two run side by side)."""
     from strideweave_b200.sharding import MXShardedContraction, ShardPlan
 
     M, Nn, K = 65536, 16384, 16384
     fmt = N.SW_MX_E4M3
-    plan = ShardPlan(mode, world, rank, M, Nn, K, k_quantum=128, chunks=4 if mode == "k" else 1)
+    plan = ShardPlan(mode, world, rank, M, Nn, K, k_quantum=128, chunks=8 if mode == "k" else 1)
     rows = plan.rows_local if mode == "m" else M
     a = quantize_generated(torch, N, kernels, fmt, rows, plan.k_local, seed=7000 + rank)
     b = quantize_generated(torch, N, kernels, fmt, Nn, plan.k_local, seed=9000 + (rank if mode == "k" else 0))
@@ -635,7 +636,7 @@ def bench_sharded(torch, dist, N, kernels, mode, world, rank, steps=5, warmup=2)
     del op, a, b
     torch.cuda.empty_cache()
     return {"tflops": round(tflops, 1), "ms": round(ms, 3), "n_gpus": world, "scaling": "strong",
-            "config": f"MXFP8 M=65536 N=16384 K=16384, {'M-split' if mode == 'm' else 'K-split + NCCL reduce-scatter, 4 N-chunks'}"}
+            "config": f"MXFP8 M=65536 N=16384 K=16384, {'M-split' if mode == 'm' else 'K-split + NCCL reduce-scatter, 8 N-chunks, 32 SMs left to the collective'}"}
 
 
 def bench_mlp(torch, N, steps=5, warmup=2) -> dict:

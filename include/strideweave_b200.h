@@ -288,6 +288,17 @@ int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
                int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
                void* stream);
 
+/* sw_mx_gemm on at most max_ctas SMs (0 = every SM).  The persistent kernel
+ * otherwise holds one CTA with ~220 KB of shared memory on every SM, so a
+ * kernel launched beside it on another stream (an NCCL collective) cannot
+ * start until it ends; leaving a few SMs free lets a K-split's
+ * reduce-scatter overlap the next chunk's contraction. */
+int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
+                  const uint8_t* scales_a, const uint8_t* b, int64_t ldb,
+                  const uint8_t* scales_b, void* c, int out_dtype, int64_t ldc_m,
+                  int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
+                  int max_ctas, void* stream);
+
 /* ---- Float32 contraction (the reference's own plan) ---------------------- */
 
 /* C[m, n] = sum_k A[m, k] * B[n, k], Float32 products accumulated in Float32,

@@ -518,7 +518,7 @@ int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
 template <int FMT, int BN, int kStages, int kEpi>
 int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t* b, int64_t ldb,
                 const uint8_t* sfb, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N,
-                int64_t K, int beta_one, cudaStream_t stream) {
+                int64_t K, int beta_one, int max_ctas, cudaStream_t stream) {
     using Cf = Cfg<FMT, BN, kStages, kEpi>;
     const int64_t row_bytes = FMT == SW_MX_E4M3 ? K : K / 2;
     CUtensorMap ma, mb;
@@ -552,7 +552,8 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t tiles = (M / kBM) * (N / BN);
-    const int grid = (int)std::min<int64_t>(tiles, sms);
+    int grid = (int)std::min<int64_t>(tiles, sms);
+    if (max_ctas > 0) grid = std::min(grid, max_ctas);  // leave SMs to concurrent work (a collective)
     SW_CUDA_TRY(launch_pdl(kernel, grid, kThreads, Cf::kSmemBytes, stream, ma, mb, mc, args), "mx_gemm launch");
     SW_LAUNCH_CHECK("mx_gemm launch");
     return SW_OK;
@@ -561,10 +562,10 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
 }  // namespace
 }  // namespace sw
 
-extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
-                          const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
-                          int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
-                          void* stream) {
+extern "C" int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
+                             const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
+                             int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
+                             int max_ctas, void* stream) {
     using namespace sw;
     if (fmt_a != fmt_b) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: mixed operand formats are not supported");
     if (fmt_a != SW_MX_E4M3 && fmt_a != SW_MX_E2M1) return fail(SW_ERR_INVALID, "sw_mx_gemm: unknown format %d", fmt_a);
@@ -586,6 +587,7 @@ extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, c
          reinterpret_cast<uintptr_t>(scales_b)) & 15)
         return fail(SW_ERR_INVALID, "sw_mx_gemm: payload and scale planes must be 16-byte aligned");
     if (ldc_m < 1 || ldc_n < 1) return fail(SW_ERR_INVALID, "sw_mx_gemm: output pitches must be positive");
+    if (max_ctas < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: max_ctas must be >= 0 (0 = every SM)");
     cudaStream_t s = (cudaStream_t)stream;
     // Results without accumulation, with a unit pitch on either side, take a
     // staged TMA epilogue (3 mainloop stages + the staging buffers); anything
@@ -601,7 +603,8 @@ extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, c
     }
     int rc;
 #define SW_GEMM(F, BNV, ST, EPI) \
-    launch_gemm<F, BNV, ST, EPI>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K, beta_one, s)
+    launch_gemm<F, BNV, ST, EPI>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K, beta_one, \
+                                 max_ctas, s)
 #define SW_GEMM_FMT(F)                                                                  \
     (epi == kEpiBf16Rows  ? SW_GEMM(F, 256, 3, kEpiBf16Rows)                             \
      : epi == kEpiF32Rows ? SW_GEMM(F, 256, 3, kEpiF32Rows)                              \
@@ -613,4 +616,12 @@ extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, c
 #undef SW_GEMM
     if (rc != SW_OK) return rc;
     return ok();
+}
+
+extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
+                          const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
+                          int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
+                          void* stream) {
+    return sw_mx_gemm_ex(fmt_a, fmt_b, a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K,
+                         beta_one, 0, stream);
 }

@@ -128,13 +128,14 @@ def mx_dequantize(fmt: int, payload_ptr: int, ld_payload: int, scales_ptr: int, 
 
 def mx_gemm(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int, c_ptr: int,
             M: int, N_: int, K: int, *, out_bf16: bool = False, ldc_m: int | None = None, ldc_n: int = 1,
-            beta_one: bool = False, stream: int = 0) -> None:
-    """C[m, n] = sum_k A[m, k] B[n, k] over MX operands (see sw_mx_gemm)."""
+            beta_one: bool = False, max_ctas: int = 0, stream: int = 0) -> None:
+    """C[m, n] = sum_k A[m, k] B[n, k] over MX operands (see sw_mx_gemm); at
+    most ``max_ctas`` SMs when it is positive (sw_mx_gemm_ex)."""
     if ldc_m is None:
         ldc_m = N_
-    N.check(N.lib.sw_mx_gemm(fmt, fmt, c_void_p(a_ptr), lda, c_void_p(sfa_ptr), c_void_p(b_ptr), ldb,
-                             c_void_p(sfb_ptr), c_void_p(c_ptr), N.SW_OUT_BF16 if out_bf16 else N.SW_OUT_F32,
-                             ldc_m, ldc_n, M, N_, K, int(beta_one), c_void_p(stream)))
+    N.check(N.lib.sw_mx_gemm_ex(fmt, fmt, c_void_p(a_ptr), lda, c_void_p(sfa_ptr), c_void_p(b_ptr), ldb,
+                                c_void_p(sfb_ptr), c_void_p(c_ptr), N.SW_OUT_BF16 if out_bf16 else N.SW_OUT_F32,
+                                ldc_m, ldc_n, M, N_, K, int(beta_one), int(max_ctas), c_void_p(stream)))
 
 
 def matmul_f32(a_ptr: int, sam: int, sak: int, b_ptr: int, sbn: int, sbk: int, c_ptr: int, scm: int, scn: int,
