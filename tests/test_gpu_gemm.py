@@ -159,3 +159,22 @@ def test_staged_bf16_epilogue_rounds_the_fp32_result(fmt):
     b16 = run_gemm(fmt, A, B, M, N_, K, out_bf16=True)
     want = torch.from_numpy(f32).to(torch.bfloat16).to(torch.float32).numpy()
     np.testing.assert_array_equal(b16, want)
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
+def test_cta_cap_changes_the_schedule_not_the_result(fmt):
+    # sw_mx_gemm_ex on 7 and on 1 SMs: every tile still computed, bit-identical
+    from strideweave_b200 import kernels
+
+    M, N_, K = 512, 768, 512
+    (pa, sa, ra), (pb, sb, rb), _, _ = operands(fmt, M, N_, K, seed=21)
+    outs = []
+    for cap in (0, 7, 1):
+        c = empty(4 * M * N_, fill=0)
+        kernels.mx_gemm(fmt, pa.ptr, ra, sa.ptr, pb.ptr, rb, sb.ptr, c.ptr, M, N_, K, max_ctas=cap)
+        N.raise_device_status()
+        outs.append(to_host(c, M * N_, np.float32))
+    np.testing.assert_array_equal(outs[0], outs[1])
+    np.testing.assert_array_equal(outs[0], outs[2])
+    with pytest.raises(ValueError):
+        kernels.mx_gemm(fmt, pa.ptr, ra, sa.ptr, pb.ptr, rb, sb.ptr, pa.ptr, M, N_, K, max_ctas=-1)
