@@ -97,6 +97,24 @@ int sw_device_status(int* status);
  * No reference counterpart (the reference has no device waits). */
 int sw_probe_bounded_wait(int64_t limit_ns, void* stream);
 
+/* ---- collectives of a sharded contraction ------------------------------- */
+
+/* NCCL behind the C ABI, for hosts that shard a contraction without
+ * torch.distributed (the survey's sw_nccl_* wrappers).  Rank 0 creates the
+ * id; the host hands the same SW_NCCL_ID_BYTES to every rank, and each rank,
+ * with its device current, creates its communicator.  Float32 sums only: the
+ * K-split reduce-scatter and an all-gather of C row blocks.  NCCL is loaded
+ * at first use; without it every call returns SW_ERR_UNSUPPORTED.
+ * Replaces nothing in the reference, which has no multi-device path. */
+#define SW_NCCL_ID_BYTES 128
+int sw_nccl_get_unique_id(uint8_t* id);
+int sw_nccl_comm_init(void** comm, int world, int rank, const uint8_t* id);
+/* recv[i] = sum over ranks of send[rank * recv_count + i] (recv_count per rank). */
+int sw_nccl_reduce_scatter_f32(const float* send, float* recv, int64_t recv_count, void* comm, void* stream);
+/* recv[r * send_count + i] = send of rank r, element i. */
+int sw_nccl_all_gather_f32(const float* send, float* recv, int64_t send_count, void* comm, void* stream);
+int sw_nccl_comm_destroy(void* comm);
+
 /* ---- layout-aware reductions -------------------------------------------- */
 
 #define SW_REDUCE_SUM 0

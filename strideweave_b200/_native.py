@@ -47,6 +47,7 @@ SW_BIN_MUL = 0
 SW_XF_NONE = 0
 SW_XF_GELU = 1
 SW_XF_GELU_GRAD = 2
+SW_NCCL_ID_BYTES = 128
 
 
 class DeviceTimeout(RuntimeError):
@@ -91,6 +92,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_stream_destroy": (c_int, [c_void_p]),
     "sw_stream_synchronize": (c_int, [c_void_p]),
     "sw_probe_bounded_wait": (c_int, [c_int64, c_void_p]),
+    "sw_nccl_get_unique_id": (c_int, [c_void_p]),
+    "sw_nccl_comm_init": (c_int, [POINTER(c_void_p), c_int, c_int, c_void_p]),
+    "sw_nccl_reduce_scatter_f32": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "sw_nccl_all_gather_f32": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "sw_nccl_comm_destroy": (c_int, [c_void_p]),
     "sw_graph_capture_begin": (c_int, [c_void_p]),
     "sw_graph_capture_end": (c_int, [c_void_p, POINTER(c_void_p)]),
     "sw_graph_launch": (c_int, [c_void_p, c_void_p]),

@@ -133,6 +133,54 @@ def run_ksplit(plan: ShardPlan, contract: ChunkContract, reduce_scatter: ReduceS
     return outs
 
 
+# ---- NCCL through the C ABI ---------------------------------------------------------
+
+
+class NcclCommunicator:
+    """One rank's NCCL communicator created through the C ABI (``sw_nccl_*``),
+    for a sharded contraction driven without torch.distributed.  Rank 0
+    creates the id with ``new_id()``; the host hands the same bytes to every
+    rank (any channel the ranks share), and each rank builds its communicator
+    with its device current."""
+
+    def __init__(self, world: int, rank: int, nccl_id: bytes) -> None:
+        from . import _native as N
+
+        if len(nccl_id) != N.SW_NCCL_ID_BYTES:
+            raise ValueError(f"an NCCL id is {N.SW_NCCL_ID_BYTES} bytes")
+        self._N = N
+        self.world, self.rank = world, rank
+        buf = (N.ctypes.c_uint8 * N.SW_NCCL_ID_BYTES).from_buffer_copy(nccl_id)
+        comm = N.c_void_p()
+        N.check(N.lib.sw_nccl_comm_init(N.ctypes.byref(comm), world, rank, buf))
+        self._comm = comm.value
+
+    @staticmethod
+    def new_id() -> bytes:
+        from . import _native as N
+
+        buf = (N.ctypes.c_uint8 * N.SW_NCCL_ID_BYTES)()
+        N.check(N.lib.sw_nccl_get_unique_id(buf))
+        return bytes(buf)
+
+    def reduce_scatter_f32(self, out_ptr: int, in_ptr: int, recv_count: int, stream: int = 0) -> None:
+        """out[i] = sum over ranks of in[rank * recv_count + i]."""
+        N = self._N
+        N.check(N.lib.sw_nccl_reduce_scatter_f32(N.c_void_p(in_ptr), N.c_void_p(out_ptr), int(recv_count),
+                                                 N.c_void_p(self._comm), N.c_void_p(stream or None)))
+
+    def all_gather_f32(self, out_ptr: int, in_ptr: int, send_count: int, stream: int = 0) -> None:
+        """out[r * send_count + i] = in of rank r, element i."""
+        N = self._N
+        N.check(N.lib.sw_nccl_all_gather_f32(N.c_void_p(in_ptr), N.c_void_p(out_ptr), int(send_count),
+                                             N.c_void_p(self._comm), N.c_void_p(stream or None)))
+
+    def close(self) -> None:
+        if self._comm is not None:
+            self._N.check(self._N.lib.sw_nccl_comm_destroy(self._N.c_void_p(self._comm)))
+            self._comm = None
+
+
 # ---- the GPU implementation ---------------------------------------------------------
 
 
@@ -146,7 +194,7 @@ class MXShardedContraction:
     """
 
     def __init__(self, plan: ShardPlan, fmt: int, a_planes: tuple[Any, Any], b_planes: tuple[Any, Any],
-                 group: Any = None) -> None:
+                 group: Any = None, comm: NcclCommunicator | None = None) -> None:
         import torch
 
         from . import _native as N
@@ -158,6 +206,7 @@ class MXShardedContraction:
         self.kernels = kernels
         self.torch = torch
         self.group = group
+        self.comm = comm  # reduce-scatter through the C ABI instead of torch.distributed
         self.a_pay, self.a_sc = a_planes
         self.b_pay, self.b_sc = b_planes
         self.row_bytes = kernels.mx_row_bytes(fmt, plan.k_local)
@@ -211,7 +260,10 @@ class MXShardedContraction:
 
         def reduce_scatter(out: Any, part: Any, c: int) -> None:
             with torch.cuda.stream(self.comm_stream):
-                if plan.world == 1:
+                if self.comm is not None:
+                    self.comm.reduce_scatter_f32(out.data_ptr(), part.data_ptr(), out.numel(),
+                                                 self.comm_stream.cuda_stream)
+                elif plan.world == 1:
                     out.copy_(part)
                 else:
                     dist.reduce_scatter_tensor(out, part, op=dist.ReduceOp.SUM, group=self.group)
