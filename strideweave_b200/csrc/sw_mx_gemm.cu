@@ -11,11 +11,13 @@
 //            shared memory into TMEM (tcgen05.cp .32x128b.warpx4) and issues
 //            the tcgen05.mma block_scale instructions, committing each stage
 //            back to the producer and each finished tile to the epilogue;
-//   warps 2..5 - epilogue: tcgen05.ld of the accumulator.  bf16 row-major
-//            results are staged in a 128-byte-swizzled shared-memory tile and
-//            written by TMA bulk stores; the accumulator is released as soon as
-//            it is in registers, so the stores overlap the next tile's MMAs
-//            (3-stage ring).  Other results are stored from registers.
+//   warps 2.. - epilogue: tcgen05.ld of the accumulator.  Results with a unit
+//            pitch are staged in shared memory and written by TMA bulk stores
+//            by eight warps, two per TMEM sub-partition, each holding half of
+//            the tile's columns in registers: the accumulator is released as
+//            soon as it is read, so the stores overlap the next tile's MMAs
+//            (3-stage ring).  Other results are stored from registers by four
+//            warps.
 // The scale atoms are read exactly as the carrier stores them (the
 // SW_SCALES_TC128 placement): a 512-byte atom holds 128 rows x 4 blocks in the
 // order the tcgen05.cp replication expects, so no shuffle is needed.
@@ -44,7 +46,6 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // payload bytes of K per stage (one 128B swizzle row)
-constexpr int kThreads = 192;  // 6 warps
 constexpr int kTmemCols = 512;
 
 // Epilogues.  kEpiDirect stores from registers (any pitches, accumulation into
@@ -56,6 +57,9 @@ constexpr int kTmemCols = 512;
 //   kEpiF32Rows  - fp32, row-major C, 128 x 32 chunks (128-byte swizzle)
 //                  rotating through kOutBufs buffers;
 //   kEpiF32Cols  - fp32, column-major C, the same chunks stored [32 n][128 m].
+// In the staged epilogues warp w drains TMEM sub-partition w % 4 (rows
+// 32 (w % 4) ..) and column half (w - 2) / 4; each half has its own share of
+// the staging memory, named barrier and store-issuing thread.
 constexpr int kEpiDirect = 0;
 constexpr int kEpiBf16Rows = 1;
 constexpr int kEpiF32Rows = 2;
@@ -65,6 +69,9 @@ constexpr int kChunkBytes = kBM * 32 * 4;  // one 128 x 32 fp32 chunk
 
 template <int FMT, int BN, int kStages, int kEpi>
 struct Cfg {
+    static constexpr int kEpiWarps = kEpi == kEpiDirect ? 4 : 8;
+    static constexpr int kEpiThreads = 32 * kEpiWarps;
+    static constexpr int kThreads = 64 + kEpiThreads;             // producer + MMA warps + epilogue
     static constexpr int kAtoms = FMT == SW_MX_E4M3 ? 1 : 2;      // scale atoms (4 blocks) per stage
     static constexpr int kABytes = kBM * kBKBytes;                 // 16 KiB
     static constexpr int kBBytes = BN * kBKBytes;
@@ -77,6 +84,7 @@ struct Cfg {
     static constexpr int kAccCol = 0;
     static constexpr int kSfCol0 = BN;                             // scale columns follow the accumulator
     static_assert(BN + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
+    static_assert(kEpi == kEpiDirect || BN == 256, "the staged epilogues split a 256-column tile in two halves");
     static constexpr int kOffA = 0;
     static constexpr int kOffB = kOffA + kStages * kABytes;
     static constexpr int kOffSfa = kOffB + kStages * kBBytes;
@@ -111,10 +119,11 @@ struct GemmArgs {
 };
 
 template <int FMT, int BN, int kStages, int kEpi>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
     using C = Cfg<FMT, BN, kStages, kEpi>;
+    static_assert(C::kThreads == (kEpi == kEpiDirect ? 192 : 320), "launch bounds");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = ptx::smem_addr(smem);
@@ -134,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_init(bar_empty + 8 * s, 1);
         }
         ptx::mbar_init(bar_tmem_full, 1);
-        ptx::mbar_init(bar_tmem_empty, 128);
+        ptx::mbar_init(bar_tmem_empty, C::kEpiThreads);
         ptx::mbar_init(bar_drain, 1);
         ptx::fence_barrier_init();
         ptx::prefetch_tmap(&tmap_a);
@@ -264,8 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (kEpi == kEpiBf16Rows) {
         // ---------------- epilogue, staged through shared memory ----------------
         const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;   // row of the tile this thread drains
-        const bool leader = threadIdx.x == 64;  // first epilogue thread issues the stores
+        const int half = (warp - 2) >> 2;        // columns [128 half, 128 half + 128) of the tile
+        const int row = quarter * 32 + lane;     // row of the tile this thread drains
+        const bool leader = threadIdx.x == 64 + 128 * half;  // issues this half's stores
         uint8_t* stage_out = smem + C::kOffOut;
         const uint32_t stage_addr = sbase + C::kOffOut;
         // Every epilogue thread runs the same barrier sequence for every tile:
@@ -276,44 +286,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
             int mb, nb;
             tile_coords(t, mb, nb);
+            uint32_t w[4][16];  // the half's 128 columns as bf16 pairs
             if (alive && !ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) alive = false;
-            if (alive) ptx::tc_fence_after();
-            // the previous tile's stores must have left the staging tile
-            if (leader && alive) ptx::bulk_wait_group_read0();
-            ptx::named_barrier(1, 128);
             if (alive) {
-#pragma unroll 1
-                for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                ptx::tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
                     uint32_t r[32];
-                    ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + chunk * 32, r);
+                    ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + half * 128 + c * 32,
+                                            r);
                     ptx::tmem_ld_wait();
-                    if (chunk == BN / 32 - 1) {
-                        // the accumulator is in registers: the next tile may start
-                        ptx::tc_fence_before();
-                        ptx::mbar_arrive(bar_tmem_empty);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                        w[c][e] = *reinterpret_cast<uint32_t*>(&h);
                     }
+                }
+                // the accumulator is in registers: the next tile may start
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(bar_tmem_empty);
+            }
+            // the previous tile's stores of this half must have left its staging
+            if (leader && alive) ptx::bulk_wait_group_read0();
+            ptx::named_barrier(1 + half, 128);
+            if (alive) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
                     // 32 columns = 64 bytes = four 16-byte units of a 128-byte
                     // row of column group chunk/2, swizzled by row % 8
+                    const int chunk = half * 4 + c;
                     uint8_t* grp = stage_out + (chunk >> 1) * (kBM * 128) + row * 128;
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[8 * u + 2 * e]),
-                                                                     __uint_as_float(r[8 * u + 2 * e + 1]));
-                            w[e] = *reinterpret_cast<uint32_t*>(&h);
-                        }
                         const int unit = ((chunk & 1) * 4 + u) ^ (row & 7);
-                        *reinterpret_cast<uint4*>(grp + unit * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+                        *reinterpret_cast<uint4*>(grp + unit * 16) =
+                            make_uint4(w[c][4 * u], w[c][4 * u + 1], w[c][4 * u + 2], w[c][4 * u + 3]);
                     }
                 }
                 ptx::fence_proxy_async_smem();
             }
-            ptx::named_barrier(1, 128);
+            ptx::named_barrier(1 + half, 128);
             if (leader && alive) {
 #pragma unroll
-                for (int g = 0; g < BN / 64; ++g)
+                for (int g = 2 * half; g < 2 * half + 2; ++g)
                     ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, mb * kBM, stage_addr + g * (kBM * 128));
                 ptx::bulk_commit_group();
             }
@@ -322,53 +337,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (kEpi == kEpiF32Rows || kEpi == kEpiF32Cols) {
         // ---------------- epilogue, fp32 chunks staged through shared memory ----------------
         const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;   // row of the tile this thread drains
-        const bool leader = threadIdx.x == 64;  // first epilogue thread issues the stores
+        const int half = (warp - 2) >> 2;        // chunks 4 half .. 4 half + 3 of the tile
+        const int row = quarter * 32 + lane;     // row of the tile this thread drains
+        const bool leader = threadIdx.x == 64 + 128 * half;  // issues this half's stores
         float* stage_out = reinterpret_cast<float*>(smem + C::kOffOut);
         const uint32_t stage_addr = sbase + C::kOffOut;
         // As in the bf16 epilogue, every thread meets the same named barriers for
-        // every chunk even after a bounded wait has given up.
-        uint32_t tile_iter = 0, seq = 0;
+        // every chunk even after a bounded wait has given up.  Each half rotates
+        // through its own two of the kOutBufs chunk buffers.
+        uint32_t tile_iter = 0;
         bool alive = true;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
             int mb, nb;
             tile_coords(t, mb, nb);
+            uint32_t r[4][32];
             if (alive && !ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) alive = false;
-            if (alive) ptx::tc_fence_after();
-#pragma unroll 1
-            for (int chunk = 0; chunk < BN / 32; ++chunk, ++seq) {
-                const int buf = int(seq % kOutBufs);
-                uint32_t r[32];
-                if (alive) {
-                    ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + chunk * 32, r);
-                    ptx::tmem_ld_wait();
-                    if (chunk == BN / 32 - 1) {
-                        // the accumulator is in registers: the next tile may start
-                        ptx::tc_fence_before();
-                        ptx::mbar_arrive(bar_tmem_empty);
-                    }
-                    // the store that last read this buffer must be done with it
-                    if (leader) ptx::bulk_wait_group_read<kOutBufs - 1>();
-                }
-                ptx::named_barrier(1, 128);
+            if (alive) {
+                ptx::tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + half * 128 + c * 32,
+                                            r[c]);
+                ptx::tmem_ld_wait();
+                // the accumulator is in registers: the next tile may start
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(bar_tmem_empty);
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int chunk = half * 4 + c;
+                const int buf = 2 * half + (c & 1);
+                // the store that last read this buffer (two chunks ago) must be done with it
+                if (leader && alive) ptx::bulk_wait_group_read<1>();
+                ptx::named_barrier(1 + half, 128);
                 if (alive) {
                     float* b = stage_out + buf * (kChunkBytes / 4);
                     if (kEpi == kEpiF32Cols) {
                         // [32 n][128 m]: the lanes of a warp write consecutive m
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) b[e * kBM + row] = __uint_as_float(r[e]);
+                        for (int e = 0; e < 32; ++e) b[e * kBM + row] = __uint_as_float(r[c][e]);
                     } else {
                         // [128 m][32 n], 16-byte units swizzled by m % 8 (the map's 128-byte swizzle)
                         float4* rowp = reinterpret_cast<float4*>(b + row * 32);
 #pragma unroll
                         for (int u = 0; u < 8; ++u)
-                            rowp[u ^ (row & 7)] = make_float4(__uint_as_float(r[4 * u]), __uint_as_float(r[4 * u + 1]),
-                                                              __uint_as_float(r[4 * u + 2]),
-                                                              __uint_as_float(r[4 * u + 3]));
+                            rowp[u ^ (row & 7)] =
+                                make_float4(__uint_as_float(r[c][4 * u]), __uint_as_float(r[c][4 * u + 1]),
+                                            __uint_as_float(r[c][4 * u + 2]), __uint_as_float(r[c][4 * u + 3]));
                     }
                     ptx::fence_proxy_async_smem();
                 }
-                ptx::named_barrier(1, 128);
+                ptx::named_barrier(1 + half, 128);
                 if (leader && alive) {
                     const uint32_t src = stage_addr + buf * kChunkBytes;
                     if (kEpi == kEpiF32Cols)
@@ -554,7 +573,7 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     const int64_t tiles = (M / kBM) * (N / BN);
     int grid = (int)std::min<int64_t>(tiles, sms);
     if (max_ctas > 0) grid = std::min(grid, max_ctas);  // leave SMs to concurrent work (a collective)
-    SW_CUDA_TRY(launch_pdl(kernel, grid, kThreads, Cf::kSmemBytes, stream, ma, mb, mc, args), "mx_gemm launch");
+    SW_CUDA_TRY(launch_pdl(kernel, grid, Cf::kThreads, Cf::kSmemBytes, stream, ma, mb, mc, args), "mx_gemm launch");
     SW_LAUNCH_CHECK("mx_gemm launch");
     return SW_OK;
 }
