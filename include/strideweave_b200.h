@@ -317,6 +317,23 @@ int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
                   int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
                   int max_ctas, void* stream);
 
+/* `batch` independent contractions C_p = A_p B_p^T (p < batch) in one
+ * persistent launch: the batched block-scaled GEMM that a batched einsum over
+ * MX operands lowers to, in place of the union product the reference
+ * materialises (einops/__init__.py:459-475).  The operands are stacks:
+ * A_p is rows [p M, (p + 1) M) of one [batch M, K] MX operand (payload pitch
+ * lda, SW_SCALES_TC128 scales of the whole stack), B_p rows [p N, (p + 1) N)
+ * of one [batch N, K] operand.  C_p starts batch_stride_c elements after
+ * C_(p-1) and has the pitches ldc_m / ldc_n; row-major results with
+ * batch_stride_c = M ldc_m and column-major ones with N ldc_n are written
+ * by the staged epilogues.  Other arguments and errors as sw_mx_gemm. */
+int sw_mx_gemm_batched(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
+                       const uint8_t* scales_a, const uint8_t* b, int64_t ldb,
+                       const uint8_t* scales_b, void* c, int out_dtype,
+                       int64_t ldc_m, int64_t ldc_n, int64_t batch_stride_c,
+                       int64_t batch, int64_t M, int64_t N, int64_t K,
+                       int beta_one, void* stream);
+
 /* ---- Float32 contraction (the reference's own plan) ---------------------- */
 
 /* C[m, n] = sum_k A[m, k] * B[n, k], Float32 products accumulated in Float32,

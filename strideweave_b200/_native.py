@@ -141,6 +141,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_void_p,
         ],
     ),
+    "sw_mx_gemm_batched": (
+        c_int,
+        [
+            c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int,
+            c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p,
+        ],
+    ),
     "sw_matmul_f32": (
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,

@@ -116,6 +116,8 @@ struct GemmArgs {
     int katoms;           // scale atoms per row group (ceil(K/128))
     int beta_one;
     int out_bf16;
+    int batch;            // stacked problems (block-diagonal), 1 for one contraction
+    int64_t c_batch;      // elements between consecutive problems' C (direct epilogue)
 };
 
 template <int FMT, int BN, int kStages, int kEpi>
@@ -164,10 +166,17 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
 
     const int num_m = args.M / kBM;
     const int num_n = args.N / BN;
-    const int num_tiles = num_m * num_n;
+    const int per_batch = num_m * num_n;
+    const int num_tiles = args.batch * per_batch;
     constexpr int kGroup = 8;  // M blocks per raster group (L2 reuse of B)
 
-    auto tile_coords = [&](int t, int& mb, int& nb) {
+    // Tile t of a batched launch is tile t % per_batch of problem
+    // t / per_batch.  (mb, nb) are the problem's own blocks; problem p's A
+    // and B are row blocks p * num_m + mb and p * num_n + nb of the stacked
+    // operands (and of their scale planes).
+    auto tile_coords = [&](int t, int& p, int& mb, int& nb) {
+        p = t / per_batch;
+        t -= p * per_batch;
         const int per_group = kGroup * num_n;
         const int g = t / per_group;
         const int first = g * kGroup;
@@ -185,21 +194,22 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             uint32_t issued[kStages] = {0};
             bool alive = true;
             for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-                int mb, nb;
-                tile_coords(t, mb, nb);
+                int p, mb, nb;
+                tile_coords(t, p, mb, nb);
+                const int ga = p * num_m + mb, gb = p * num_n + nb;  // stacked row blocks
                 for (int ks = 0; ks < args.k_stages; ++ks) {
                     if (!ptx::mbar_wait(bar_empty + 8 * stage, phase ^ 1)) { alive = false; break; }
                     const uint32_t full = bar_full + 8 * stage;
                     ptx::mbar_arrive_expect_tx(full, C::kStageTx);
-                    ptx::tma_load_2d(sbase + C::kOffA + stage * C::kABytes, &tmap_a, ks * kBKBytes, mb * kBM, full);
-                    ptx::tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tmap_b, ks * kBKBytes, nb * BN, full);
+                    ptx::tma_load_2d(sbase + C::kOffA + stage * C::kABytes, &tmap_a, ks * kBKBytes, ga * kBM, full);
+                    ptx::tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tmap_b, ks * kBKBytes, gb * BN, full);
                     const int64_t atom0 = int64_t(ks) * C::kAtoms;
                     ptx::bulk_load(sbase + C::kOffSfa + stage * C::kSfaBytes,
-                                   args.sfa + (int64_t(mb) * args.katoms + atom0) * 512, C::kSfaBytes, full);
+                                   args.sfa + (int64_t(ga) * args.katoms + atom0) * 512, C::kSfaBytes, full);
 #pragma unroll
                     for (int g = 0; g < BN / 128; ++g) {
                         ptx::bulk_load(sbase + C::kOffSfb + stage * C::kSfbBytes + g * C::kAtoms * 512,
-                                       args.sfb + ((int64_t(nb) * (BN / 128) + g) * args.katoms + atom0) * 512,
+                                       args.sfb + ((int64_t(gb) * (BN / 128) + g) * args.katoms + atom0) * 512,
                                        C::kAtoms * 512, full);
                     }
                     issued[stage] += 1;
@@ -284,8 +294,8 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
         uint32_t tile_iter = 0;
         bool alive = true;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
-            int mb, nb;
-            tile_coords(t, mb, nb);
+            int p, mb, nb;
+            tile_coords(t, p, mb, nb);
             uint32_t w[4][16];  // the half's 128 columns as bf16 pairs
             if (alive && !ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) alive = false;
             if (alive) {
@@ -329,7 +339,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             if (leader && alive) {
 #pragma unroll
                 for (int g = 2 * half; g < 2 * half + 2; ++g)
-                    ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, mb * kBM, stage_addr + g * (kBM * 128));
+                    ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, (p * num_m + mb) * kBM, stage_addr + g * (kBM * 128));
                 ptx::bulk_commit_group();
             }
         }
@@ -348,8 +358,8 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
         uint32_t tile_iter = 0;
         bool alive = true;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
-            int mb, nb;
-            tile_coords(t, mb, nb);
+            int p, mb, nb;
+            tile_coords(t, p, mb, nb);
             uint32_t r[4][32];
             if (alive && !ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) alive = false;
             if (alive) {
@@ -391,9 +401,9 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                 if (leader && alive) {
                     const uint32_t src = stage_addr + buf * kChunkBytes;
                     if (kEpi == kEpiF32Cols)
-                        ptx::tma_store_2d(&tmap_c, mb * kBM, nb * BN + chunk * 32, src);
+                        ptx::tma_store_2d(&tmap_c, mb * kBM, (p * num_n + nb) * BN + chunk * 32, src);
                     else
-                        ptx::tma_store_2d(&tmap_c, nb * BN + chunk * 32, mb * kBM, src);
+                        ptx::tma_store_2d(&tmap_c, nb * BN + chunk * 32, (p * num_m + mb) * kBM, src);
                     ptx::bulk_commit_group();
                 }
             }
@@ -405,8 +415,8 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
         const int row_in_tile = quarter * 32 + lane;
         uint32_t tile_iter = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_iter) {
-            int mb, nb;
-            tile_coords(t, mb, nb);
+            int p, mb, nb;
+            tile_coords(t, p, mb, nb);
             if (!ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) break;
             ptx::tc_fence_after();
             const int64_t m = int64_t(mb) * kBM + row_in_tile;
@@ -417,7 +427,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                 ptx::tmem_ld_wait();
                 const int64_t n0 = int64_t(nb) * BN + chunk * 32;
                 if (args.out_bf16) {
-                    __nv_bfloat16* cptr = static_cast<__nv_bfloat16*>(args.c);
+                    __nv_bfloat16* cptr = static_cast<__nv_bfloat16*>(args.c) + p * args.c_batch;
                     if (args.ldc_n == 1 && (((m * args.ldc_m + n0) & 7) == 0) &&
                         ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
                         uint4* dst = reinterpret_cast<uint4*>(cptr + m * args.ldc_m + n0);
@@ -444,7 +454,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                         }
                     }
                 } else {
-                    float* cptr = static_cast<float*>(args.c);
+                    float* cptr = static_cast<float*>(args.c) + p * args.c_batch;
                     if (args.ldc_n == 1 && (((m * args.ldc_m + n0) & 3) == 0) &&
                         ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
                         float4* dst = reinterpret_cast<float4*>(cptr + m * args.ldc_m + n0);
@@ -537,19 +547,21 @@ int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
 template <int FMT, int BN, int kStages, int kEpi>
 int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t* b, int64_t ldb,
                 const uint8_t* sfb, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N,
-                int64_t K, int beta_one, int max_ctas, cudaStream_t stream) {
+                int64_t K, int beta_one, int64_t batch, int64_t c_batch, int max_ctas, cudaStream_t stream) {
     using Cf = Cfg<FMT, BN, kStages, kEpi>;
     const int64_t row_bytes = FMT == SW_MX_E4M3 ? K : K / 2;
+    // the maps cover the stacked operands (batch * M rows of A, batch * N of B)
+    // and, for the staged epilogues, the stacked results
     CUtensorMap ma, mb;
-    int rc = make_operand_map(&ma, a, M, row_bytes, lda, kBM);
+    int rc = make_operand_map(&ma, a, batch * M, row_bytes, lda, kBM);
     if (rc != SW_OK) return rc;
-    rc = make_operand_map(&mb, b, N, row_bytes, ldb, BN);
+    rc = make_operand_map(&mb, b, batch * N, row_bytes, ldb, BN);
     if (rc != SW_OK) return rc;
     CUtensorMap mc;
     memset(&mc, 0, sizeof(mc));
-    if (kEpi == kEpiBf16Rows) rc = make_output_map(&mc, c, M, N, ldc_m * 2);
-    if (kEpi == kEpiF32Rows) rc = make_output_map_f32(&mc, c, M, N, ldc_m * 4, 32, kBM, true);
-    if (kEpi == kEpiF32Cols) rc = make_output_map_f32(&mc, c, N, M, ldc_n * 4, kBM, 32, false);
+    if (kEpi == kEpiBf16Rows) rc = make_output_map(&mc, c, batch * M, N, ldc_m * 2);
+    if (kEpi == kEpiF32Rows) rc = make_output_map_f32(&mc, c, batch * M, N, ldc_m * 4, 32, kBM, true);
+    if (kEpi == kEpiF32Cols) rc = make_output_map_f32(&mc, c, batch * N, M, ldc_n * 4, kBM, 32, false);
     if (rc != SW_OK) return rc;
     GemmArgs args;
     args.sfa = sfa;
@@ -564,13 +576,15 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.katoms = (int)((K / 32 + 3) / 4);
     args.beta_one = beta_one;
     args.out_bf16 = out_dtype == SW_OUT_BF16;
+    args.batch = (int)batch;
+    args.c_batch = c_batch;
     auto kernel = mx_gemm_kernel<FMT, BN, kStages, kEpi>;
     SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
                 "set gemm smem");
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t tiles = (M / kBM) * (N / BN);
+    const int64_t tiles = batch * (M / kBM) * (N / BN);
     int grid = (int)std::min<int64_t>(tiles, sms);
     if (max_ctas > 0) grid = std::min(grid, max_ctas);  // leave SMs to concurrent work (a collective)
     SW_CUDA_TRY(launch_pdl(kernel, grid, Cf::kThreads, Cf::kSmemBytes, stream, ma, mb, mc, args), "mx_gemm launch");
@@ -581,11 +595,15 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
 }  // namespace
 }  // namespace sw
 
-extern "C" int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
-                             const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
-                             int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
-                             int max_ctas, void* stream) {
-    using namespace sw;
+namespace sw {
+namespace {
+
+// Checks and dispatch shared by the entry points; `batch` problems stacked as
+// described at sw_mx_gemm_batched (1 for one contraction).
+int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a, const uint8_t* b,
+                 int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n,
+                 int64_t M, int64_t N, int64_t K, int beta_one, int64_t batch, int64_t c_batch, int max_ctas,
+                 void* stream) {
     if (fmt_a != fmt_b) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: mixed operand formats are not supported");
     if (fmt_a != SW_MX_E4M3 && fmt_a != SW_MX_E2M1) return fail(SW_ERR_INVALID, "sw_mx_gemm: unknown format %d", fmt_a);
     if (out_dtype != SW_OUT_F32 && out_dtype != SW_OUT_BF16)
@@ -599,6 +617,9 @@ extern "C" int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda
                     "sw_mx_gemm: needs M %% 128 == 0, N %% 128 == 0, K %% %lld == 0 (got %lld x %lld x %lld)",
                     (long long)kq, (long long)M, (long long)N, (long long)K);
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: extent too large");
+    if (batch < 1 || c_batch < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: bad batch count or result stride");
+    if (batch * M > INT32_MAX || batch * N > INT32_MAX || batch * (M / 128) * (N / 128) > INT32_MAX)
+        return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: stacked extent too large");
     const int64_t row_bytes = fmt_a == SW_MX_E4M3 ? K : K / 2;
     if (lda < row_bytes || ldb < row_bytes || lda % 16 != 0 || ldb % 16 != 0)
         return fail(SW_ERR_INVALID, "sw_mx_gemm: payload pitches must cover a row and be multiples of 16 bytes");
@@ -614,16 +635,18 @@ extern "C" int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda
     const bool aligned_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0;
     const int esize = out_dtype == SW_OUT_BF16 ? 2 : 4;
     int epi = kEpiDirect;
+    // (a batched launch stages its results only when they stack without gaps)
     if (!beta_one && N % 256 == 0 && aligned_c) {
-        if (ldc_n == 1 && (ldc_m * esize) % 16 == 0 && ldc_m >= N)
+        if (ldc_n == 1 && (ldc_m * esize) % 16 == 0 && ldc_m >= N && (batch == 1 || c_batch == M * ldc_m))
             epi = out_dtype == SW_OUT_BF16 ? kEpiBf16Rows : kEpiF32Rows;
-        else if (out_dtype == SW_OUT_F32 && ldc_m == 1 && (ldc_n * 4) % 16 == 0 && ldc_n >= M)
+        else if (out_dtype == SW_OUT_F32 && ldc_m == 1 && (ldc_n * 4) % 16 == 0 && ldc_n >= M &&
+                 (batch == 1 || c_batch == N * ldc_n))
             epi = kEpiF32Cols;
     }
     int rc;
 #define SW_GEMM(F, BNV, ST, EPI) \
     launch_gemm<F, BNV, ST, EPI>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K, beta_one, \
-                                 max_ctas, s)
+                                 batch, c_batch, max_ctas, s)
 #define SW_GEMM_FMT(F)                                                                  \
     (epi == kEpiBf16Rows  ? SW_GEMM(F, 256, 3, kEpiBf16Rows)                             \
      : epi == kEpiF32Rows ? SW_GEMM(F, 256, 3, kEpiF32Rows)                              \
@@ -635,6 +658,26 @@ extern "C" int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda
 #undef SW_GEMM
     if (rc != SW_OK) return rc;
     return ok();
+}
+
+}  // namespace
+}  // namespace sw
+
+extern "C" int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
+                             const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
+                             int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N, int64_t K, int beta_one,
+                             int max_ctas, void* stream) {
+    return sw::mx_gemm_impl(fmt_a, fmt_b, a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K,
+                            beta_one, 1, 0, max_ctas, stream);
+}
+
+extern "C" int sw_mx_gemm_batched(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
+                                  const uint8_t* b, int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype,
+                                  int64_t ldc_m, int64_t ldc_n, int64_t batch_stride_c, int64_t batch, int64_t M,
+                                  int64_t N, int64_t K, int beta_one, void* stream) {
+    if (batch == 0) return sw::ok();
+    return sw::mx_gemm_impl(fmt_a, fmt_b, a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K,
+                            beta_one, batch, batch_stride_c, 0, stream);
 }
 
 extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,

@@ -138,6 +138,23 @@ def mx_gemm(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, 
                                 ldc_m, ldc_n, M, N_, K, int(beta_one), int(max_ctas), c_void_p(stream)))
 
 
+def mx_gemm_batched(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int, c_ptr: int,
+                    batch: int, M: int, N_: int, K: int, *, out_bf16: bool = False, ldc_m: int | None = None,
+                    ldc_n: int = 1, batch_stride_c: int | None = None, beta_one: bool = False,
+                    stream: int = 0) -> None:
+    """C_p = A_p B_p^T for p < batch over stacked MX operands (A: [batch M, K],
+    B: [batch N, K], TC128 scales of each stack) in one launch (see
+    sw_mx_gemm_batched).  C_p defaults to the p-th [M, N] row-major block."""
+    if ldc_m is None:
+        ldc_m = N_
+    if batch_stride_c is None:
+        batch_stride_c = M * ldc_m if ldc_n == 1 else N_ * ldc_n
+    N.check(N.lib.sw_mx_gemm_batched(fmt, fmt, c_void_p(a_ptr), lda, c_void_p(sfa_ptr), c_void_p(b_ptr), ldb,
+                                     c_void_p(sfb_ptr), c_void_p(c_ptr),
+                                     N.SW_OUT_BF16 if out_bf16 else N.SW_OUT_F32, ldc_m, ldc_n, batch_stride_c,
+                                     batch, M, N_, K, int(beta_one), c_void_p(stream)))
+
+
 def matmul_f32(a_ptr: int, sam: int, sak: int, b_ptr: int, sbn: int, sbk: int, c_ptr: int, scm: int, scn: int,
                M: int, N_: int, K: int, *, acc64: bool = False, stream: int = 0) -> None:
     """C[m, n] = sum_k A[m, k] B[n, k] with binary32 products, summed in binary32
