@@ -146,6 +146,55 @@ class CudaBatchedContraction(Operation):
         return (dl, dr)
 
 
+def _mx_planes(fmt: int, ptr: int, sb: int, sr: int, sk: int, batch: int, rows: int, K: int, device: int):
+    """Stacked MX planes of batch x [rows, K] Float32 views (element strides
+    sb, sr, sk), quantised along K: one [batch rows, K] operand with its TC128
+    scales, as sw_mx_gemm_batched reads them."""
+    from . import kernels
+    from .carrier import CUDA
+
+    rb = kernels.mx_row_bytes(fmt, K)
+    katoms = (K // 32 + 3) // 4
+    payload = CUDA(batch * rows * K, dtype=DType.E4M3 if fmt == N.SW_MX_E4M3 else DType.E2M1, empty=True,
+                   device=device)
+    scales = CUDA(kernels.scale_bytes_tc128(batch * rows, K // 32), dtype=DType.E8M0, empty=True, device=device)
+    if batch == 1 or sb == rows * sr:  # the problems' rows stack into one view
+        kernels.mx_quantize(fmt, ptr, batch * rows, K, sr, sk, payload.data_ptr, rb, scales.data_ptr)
+    else:
+        for q in range(batch):
+            kernels.mx_quantize(fmt, ptr + 4 * q * sb, rows, K, sr, sk, payload.data_ptr + q * rows * rb, rb,
+                                scales.data_ptr + q * (rows // 128) * katoms * 512)
+    return payload, scales, rb
+
+
+class CudaMxBatchedContraction(CudaBatchedContraction):
+    """The batched contraction with both inputs quantised to an MX format
+    along the contracted symbol (``ctx["fmt"]``) and contracted by one
+    batched block-scaled launch (``sw_mx_gemm_batched``) into the Float32
+    result layout of the plain path.  Gradients are the Float32 contractions
+    of the unquantised inputs (straight through the quantisation), as the
+    plain path computes them."""
+
+    def _forward(self, lhs: Any, rhs: Any) -> Tensor:
+        from . import kernels
+        from .carrier import CUDA
+
+        p = self.ctx["plan"]
+        fmt = self.ctx["fmt"]
+        plan = resolve_operation_plan("matmul", lhs.carrier.dtype(), rhs.carrier.dtype())
+        require_capability(CUDA, plan)
+        dev = lhs.carrier.device
+        out = Tensor(CUDA(p["layout"].cosize, empty=True, device=dev), 0, p["layout"])
+        a = lhs.carrier.data_ptr + 4 * lhs.offset
+        b = rhs.carrier.data_ptr + 4 * rhs.offset
+        pa, sa, rb = _mx_planes(fmt, a, p["sab"], p["sam"], p["sak"], p["batch"], p["M"], p["K"], dev)
+        pb, sb, _ = _mx_planes(fmt, b, p["sbb"], p["sbn"], p["sbk"], p["batch"], p["N"], p["K"], dev)
+        kernels.mx_gemm_batched(fmt, pa.data_ptr, rb, sa.data_ptr, pb.data_ptr, rb, sb.data_ptr,
+                                out.carrier.data_ptr, p["batch"], p["M"], p["N"], p["K"], ldc_m=p["scm"],
+                                ldc_n=p["scn"], batch_stride_c=p["scb"])
+        return out
+
+
 def _plan_like_output(gradient: Tensor, p: dict) -> dict:
     syms = p["out_syms"]
     st = {}
@@ -165,12 +214,22 @@ def _strides_in(t: Tensor, syms: list[str], p: dict, side: str) -> dict:
     return out
 
 
-def einsum(lhs: Any, rhs: Any, description: str) -> Tensor:
+def einsum(lhs: Any, rhs: Any, description: str, *, fmt: str | None = None) -> Tensor:
     """``sw.einsum(lhs, rhs, description)`` for CUDA-carrier tensors, with the
-    batched fast path described in the module docstring."""
+    batched fast path described in the module docstring.
+
+    ``fmt`` ("MXFP8_E4M3" or "MXFP4") computes that fast path on the
+    block-scaled tensor cores instead: both inputs quantised along the
+    contracted symbol, one batched MX contraction, Float32 result.  It needs
+    the fast path's shape with a free symbol on each side, both free extents
+    multiples of 128 and the contracted one of 128 (E4M3) or 256 (E2M1); other
+    einsums with ``fmt`` raise NotImplementedError."""
     from strideweave.einops import einsum as reference_einsum
 
+    from . import kernels
     from .carrier import CUDA
+
+    code = kernels.mx_format(fmt) if fmt is not None else None
 
     if (isinstance(lhs, Tensor) and isinstance(rhs, Tensor) and isinstance(lhs.carrier, CUDA)
             and isinstance(rhs.carrier, CUDA) and lhs.carrier.dtype() is DType.Float32
@@ -188,12 +247,24 @@ def einsum(lhs: Any, rhs: Any, description: str) -> Tensor:
             p["i"] = next((s for s in ls if s not in shared), None)
             p["j"] = next((s for s in rs if s not in shared), None)
             p["out_syms"] = os_
-            op = CudaBatchedContraction()
+            if code is not None:
+                kq = 128 if code == N.SW_MX_E4M3 else 256
+                if not (p["i"] and p["j"] and p["M"] % 128 == 0 and p["N"] % 128 == 0 and p["K"] % kq == 0):
+                    raise NotImplementedError(
+                        f"einsum with fmt={fmt!r} needs a free symbol on each side, free extents that are "
+                        f"multiples of 128 and a contracted extent that is a multiple of {kq}")
+                op = CudaMxBatchedContraction()
+                op.ctx["fmt"] = code
+            else:
+                op = CudaBatchedContraction()
             op.ctx["plan"] = p
             op.ctx["lhs_syms"] = ls
             op.ctx["rhs_syms"] = rs
             return op.forward(lhs, rhs)
+    if code is not None:
+        raise NotImplementedError(f"einsum with fmt={fmt!r} needs two unswizzled Float32 CUDA tensors in the shape "
+                                  "of a batched contraction (one batch and one contracted symbol)")
     return reference_einsum(lhs, rhs, description)
 
 
-__all__ = ["CudaBatchedContraction", "einsum"]
+__all__ = ["CudaBatchedContraction", "CudaMxBatchedContraction", "einsum"]

@@ -112,3 +112,88 @@ def test_fast_path_gradients_match_the_reference_lowering():
     for (da, db) in grads:
         assert rel_frobenius(da, want_a) <= TOL
         assert rel_frobenius(db, want_b) <= TOL
+
+
+def col_major_values(t, shape):
+    """A result in the canonical column-major layout, read in one copy."""
+    flat = t.carrier.to_numpy()
+    strides, acc = [], 1
+    for n in shape:
+        strides.append(acc * 4)
+        acc *= n
+    return np.lib.stride_tricks.as_strided(flat, shape, strides).copy()
+
+
+def dequantised(code, x):
+    """x [rows, K] through the oracle's MX quantisation (bit-exact with the device's) and back."""
+    from oracle import oracle as O
+
+    p, s = O.mx_quantize(code, np.ascontiguousarray(x), scale_layout=1)
+    return O.mx_dequantize(code, p, s, x.shape[0], x.shape[1], scale_layout=1).astype(np.float64)
+
+
+@pytest.mark.parametrize("fmt", ["MXFP8_E4M3", "MXFP4"])
+@pytest.mark.parametrize("desc", ["b i k, b j k -> b i j", "i b k, k b j -> i j b"])
+def test_mx_fast_path_contracts_the_quantised_inputs(fmt, desc):
+    # fmt= quantises both inputs along the contracted symbol and runs one
+    # batched block-scaled contraction: the result is the contraction of the
+    # dequantised operands, in the plain path's result layout
+    from oracle import oracle as O
+    from strideweave_b200 import einsum
+
+    code = O.E4M3 if fmt == "MXFP8_E4M3" else O.E2M1
+    rng = np.random.default_rng(4)
+    B, I, J, K = 3, 256, 128, 512
+    if desc.startswith("b"):
+        a = rng.standard_normal((B, I, K)).astype(np.float32)
+        b = (rng.standard_normal((B, J, K)) * 0.1).astype(np.float32)
+        a_bik, b_bjk, out_shape = a, b, (B, I, J)
+    else:  # lhs (i, b, k), rhs (k, b, j): strided views, one quantisation per problem
+        a = rng.standard_normal((I, B, K)).astype(np.float32)
+        b = (rng.standard_normal((K, B, J)) * 0.1).astype(np.float32)
+        a_bik, b_bjk, out_shape = a.transpose(1, 0, 2), b.transpose(1, 2, 0), (I, J, B)
+    ta, tb = cuda_tensor(a), cuda_tensor(b)
+    mx = einsum.einsum(ta, tb, desc, fmt=fmt)
+    assert type(mx.autograd_ctx).__name__ == "CudaMxBatchedContraction"
+    plain = einsum.einsum(cuda_tensor(a), cuda_tensor(b), desc)
+    assert mx.layout == plain.layout
+    want = np.stack([dequantised(code, a_bik[q]) @ dequantised(code, b_bjk[q]).T for q in range(B)])
+    if out_shape == (I, J, B):
+        want = want.transpose(1, 2, 0)
+    got = col_major_values(mx, out_shape)
+    assert rel_frobenius(got, want) <= TOL
+
+
+def test_mx_fast_path_gradients_pass_straight_through():
+    # the gradients of the MX path are the plain path's (Float32 contractions
+    # of the unquantised inputs), bit for bit
+    from strideweave_b200 import einsum
+
+    rng = np.random.default_rng(5)
+    B, I, J, K = 2, 128, 256, 256
+    a = rng.standard_normal((B, I, K)).astype(np.float32)
+    b = rng.standard_normal((B, J, K)).astype(np.float32)
+    g = rng.standard_normal((J, I, B)).astype(np.float32)  # canonical column-major (b, i, j)
+    grads = []
+    for kw in ({}, {"fmt": "MXFP8_E4M3"}):
+        ta, tb = cuda_tensor(a), cuda_tensor(b)
+        r = einsum.einsum(ta, tb, "b i k, b j k -> b i j", **kw)
+        from strideweave_b200 import CUDA
+
+        r.backward(Tensor(CUDA.from_numpy(g.ravel()), 0, r.layout))
+        grads.append((ta.grad.carrier.to_numpy(), tb.grad.carrier.to_numpy()))
+    np.testing.assert_array_equal(grads[0][0], grads[1][0])
+    np.testing.assert_array_equal(grads[0][1], grads[1][1])
+
+
+def test_mx_fast_path_refuses_what_it_cannot_tile():
+    from strideweave_b200 import einsum
+
+    a = np.zeros((2, 100, 256), np.float32)
+    b = np.zeros((2, 128, 256), np.float32)
+    with pytest.raises(NotImplementedError):
+        einsum.einsum(cuda_tensor(a), cuda_tensor(b), "b i k, b j k -> b i j", fmt="MXFP8_E4M3")
+    with pytest.raises(NotImplementedError):
+        einsum.einsum(cuda_tensor(b), cuda_tensor(b), "b i k, b j k -> b i j", fmt="MXFP6")
+    with pytest.raises(NotImplementedError):  # no batch symbol: not the batched shape
+        einsum.einsum(cuda_tensor(b[0]), cuda_tensor(b[0]), "i k, j k -> i j", fmt="MXFP8_E4M3")
