@@ -71,6 +71,13 @@ def test_invalid_arguments_are_rejected_before_any_device_work(native):
                                            c_void_p(16), c_void_p(16), 0, 128, 1, 128, 128, 1024, 0, None))
     with pytest.raises(ValueError, match="16-byte aligned"):
         kernels.mx_gemm(1, 17, 1024, 16, 16, 1024, 16, 16, 128, 128, 1024)
+    with pytest.raises(ValueError, match="bad batch count"):
+        kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, -1, 128, 256, 1024)
+    with pytest.raises(ValueError, match="bad batch count"):
+        kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 2, 128, 256, 1024, batch_stride_c=-1)
+    with pytest.raises(NotImplementedError, match="stacked extent too large"):
+        kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 1 << 24, 1024, 256, 1024)
+    kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 0, 128, 256, 1024)  # no problems: no work
     with pytest.raises(ValueError, match="unknown format"):
         kernels.mx_quantize(7, 16, 4, 32, 32, 1, 16, 32, 16)
     with pytest.raises(ValueError, match="payload pitch"):
