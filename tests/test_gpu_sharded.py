@@ -5,8 +5,8 @@ one contraction of the whole problem.
   contraction bit for bit (each output tile is the same tile with the same
   K order).
 * Two ranks, where the box has two GPUs: the M-split rows match bit for bit;
-  the K-split sums two K halves, which stays within the 2e-3 relative
-  Frobenius bound (it measures about 1e-7).  The collective runs through
+  the K-split sums two K halves in another order, so it is held to the
+  path's 2e-3 relative Frobenius bound.  The collective runs through
   torch.distributed, then through the C-ABI NCCL communicator, with the same
   result.
 """
