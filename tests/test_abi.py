@@ -78,6 +78,23 @@ def test_invalid_arguments_are_rejected_before_any_device_work(native):
     with pytest.raises(NotImplementedError, match="stacked extent too large"):
         kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 1 << 24, 1024, 256, 1024)
     kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 0, 128, 256, 1024)  # no problems: no work
+    # the NCCL wrappers check their arguments before they load NCCL
+    from ctypes import byref
+
+    from strideweave_b200.sharding import NcclCommunicator
+
+    with pytest.raises(ValueError, match="128 bytes"):
+        NcclCommunicator(2, 0, b"too short")
+    ident = (native.ctypes.c_uint8 * native.SW_NCCL_ID_BYTES)()
+    comm = native.c_void_p()
+    with pytest.raises(ValueError, match="bad rank"):
+        native.check(native.lib.sw_nccl_comm_init(byref(comm), 2, 2, ident))
+    with pytest.raises(ValueError, match="null"):
+        native.check(native.lib.sw_nccl_get_unique_id(None))
+    with pytest.raises(ValueError, match="bad argument"):
+        native.check(native.lib.sw_nccl_reduce_scatter_f32(c_void_p(16), c_void_p(16), -1, c_void_p(16), None))
+    native.check(native.lib.sw_nccl_all_gather_f32(c_void_p(16), c_void_p(16), 0, c_void_p(16), None))  # empty
+    native.check(native.lib.sw_nccl_comm_destroy(None))  # no communicator: nothing to do
     with pytest.raises(ValueError, match="unknown format"):
         kernels.mx_quantize(7, 16, 4, 32, 32, 1, 16, 32, 16)
     with pytest.raises(ValueError, match="payload pitch"):
