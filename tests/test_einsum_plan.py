@@ -45,3 +45,18 @@ def test_plan_falls_back_outside_its_shape():
     two = Tensor(CPU(200, dtype=DType.Float32), 0, Layout(Shape([2, 3, [2, 3]]), Stride([30, 10, [1, 5]])))
     rhs6 = t((2, 4, 6), (24, 6, 1))
     assert _plan(two, rhs6, "b i k, b j k -> b i j") is None       # k is two strides
+
+
+def test_mx_format_requests_never_fall_back_silently():
+    # einsum(..., fmt=...) asks for the block-scaled tensor cores: tensors that
+    # cannot take that path (here host tensors) and unknown formats raise, and
+    # nothing is computed by the reference lowering in their place
+    from strideweave_b200.einsum import einsum
+
+    lhs = t((2, 128, 256), (128 * 256, 256, 1))
+    rhs = t((2, 128, 256), (128 * 256, 256, 1))
+    with pytest.raises(NotImplementedError, match="CUDA tensors"):
+        einsum(lhs, rhs, "b i k, b j k -> b i j", fmt="MXFP8_E4M3")
+    with pytest.raises(NotImplementedError, match="MXFP6"):
+        einsum(lhs, rhs, "b i k, b j k -> b i j", fmt="MXFP6")
+    assert einsum(lhs, rhs, "b i k, b j k -> b i j").layout.shape == Shape([2, 128, 128])  # no fmt: reference
