@@ -172,7 +172,10 @@ int sw_reduce_f32(const sw_reduce_plan* plan, const float* x, int64_t x_size,
  * device address, so make that first call before any stream capture.  All
  * calls share the one array and each clears its counters on its own stream:
  * calls that overlap on the GPU (other streams, other host threads) race and
- * produce wrong results, so order them on one stream. */
+ * produce wrong results, so order them on one stream.  The array's address
+ * is looked up once per device and kept for the life of the process: after a
+ * cudaDeviceReset (or any reset of the primary context) this entry point is
+ * not supported. */
 int sw_reduce_f32_noalloc(const sw_reduce_plan* plan, const float* x, int64_t x_size,
                           void* out, void* stream);
 
@@ -324,9 +327,12 @@ int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
  * A_p is rows [p M, (p + 1) M) of one [batch M, K] MX operand (payload pitch
  * lda, SW_SCALES_TC128 scales of the whole stack), B_p rows [p N, (p + 1) N)
  * of one [batch N, K] operand.  C_p starts batch_stride_c elements after
- * C_(p-1) and has the pitches ldc_m / ldc_n; row-major results with
- * batch_stride_c = M ldc_m and column-major ones with N ldc_n are written
- * by the staged epilogues.  Other arguments and errors as sw_mx_gemm. */
+ * C_(p-1) and has the pitches ldc_m / ldc_n.  The C_p must be disjoint:
+ * with batch > 1, a batch_stride_c below one problem's span
+ * (M-1) ldc_m + (N-1) ldc_n + 1 is refused with SW_ERR_INVALID.  Row-major
+ * results with batch_stride_c = M ldc_m and column-major ones with
+ * batch_stride_c = N ldc_n are written by the staged epilogues; any other
+ * stride stores from registers.  Other arguments and errors as sw_mx_gemm. */
 int sw_mx_gemm_batched(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
                        const uint8_t* scales_a, const uint8_t* b, int64_t ldb,
                        const uint8_t* scales_b, void* c, int out_dtype,

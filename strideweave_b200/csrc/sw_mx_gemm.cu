@@ -627,6 +627,12 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
          reinterpret_cast<uintptr_t>(scales_b)) & 15)
         return fail(SW_ERR_INVALID, "sw_mx_gemm: payload and scale planes must be 16-byte aligned");
     if (ldc_m < 1 || ldc_n < 1) return fail(SW_ERR_INVALID, "sw_mx_gemm: output pitches must be positive");
+    // Stacked results must not overlap: CTAs of different problems store (and,
+    // with beta_one, read back) their tiles concurrently.
+    if (batch > 1 && c_batch < (M - 1) * ldc_m + (N - 1) * ldc_n + 1)
+        return fail(SW_ERR_INVALID,
+                    "sw_mx_gemm_batched: batch_stride_c %lld is smaller than one problem's result span %lld",
+                    (long long)c_batch, (long long)((M - 1) * ldc_m + (N - 1) * ldc_n + 1));
     if (max_ctas < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: max_ctas must be >= 0 (0 = every SM)");
     cudaStream_t s = (cudaStream_t)stream;
     // Results without accumulation, with a unit pitch on either side, take a

@@ -1194,7 +1194,9 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 // The device address of g_static_scratch on the current device.  In host code
 // the array's name stands for a host-side shadow, never a device address, so
-// it is looked up once per device with that device current.
+// it is looked up once per device with that device current.  The cached
+// address belongs to the device's primary context; a device reset, which
+// creates a new context, is not supported by this entry point.
 int static_scratch(void** out) {
     static std::mutex mu;
     static void* addr[kMaxDevices] = {};

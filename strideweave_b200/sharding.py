@@ -26,9 +26,9 @@ a reduce-scatter and an allocator. On GPUs these are the tcgen05 MX GEMM and
 NCCL (through `torch.distributed`). The CPU tests run the same schedule with
 numpy and `gloo`.
 
-The reference has no distributed code; this realises the north
-star's "sharding of large contractions across the 8 GPUs by M-split, or by
-K-split with an NCCL reduce-scatter".
+The reference has no distributed code: it runs every operation on one host
+carrier.  This module shards large contractions across the GPUs of a node by
+M-split, or by K-split with an NCCL reduce-scatter.
 """
 
 from __future__ import annotations

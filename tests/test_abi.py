@@ -78,6 +78,13 @@ def test_invalid_arguments_are_rejected_before_any_device_work(native):
     with pytest.raises(NotImplementedError, match="stacked extent too large"):
         kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 1 << 24, 1024, 256, 1024)
     kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 0, 128, 256, 1024)  # no problems: no work
+    # stacked results that overlap are refused (one problem spans 127 * 256 + 255 + 1 elements)
+    for stride in (0, 1, 128 * 256 - 1):
+        with pytest.raises(ValueError, match="smaller than one problem's result span"):
+            kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 2, 128, 256, 1024, batch_stride_c=stride)
+    with pytest.raises(ValueError, match="result span 32768"):  # column-major: (127) * 1 + 255 * 128 + 1
+        kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 2, 128, 256, 1024, ldc_m=1, ldc_n=128,
+                                batch_stride_c=100)
     # the NCCL wrappers check their arguments before they load NCCL
     from ctypes import byref
 
