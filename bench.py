@@ -1,18 +1,28 @@
 """Benchmark of the B200 StrideWeave carrier hot path.
 
-Default workload: layout-aware Float32 reductions - sum,
-max and argmax over mode 1 of X[8192 x 4096] ~ U(-1, 1), on (a) a row-major
-layout, (b) a transposed stride layout and (c) a hierarchical tiled layout
-((128,64),(32,128)) stored through a 3-bit swizzle.  One step = the 9
-reductions.  The line also carries the MX contractions of configs 1 and 3
-(MXFP8 / MXFP4, M=N=K=8192) measured on the same device.
+Headline workload, at every world size: the sharded MXFP8 contraction
+C[65536 x 16384] = A[65536 x 16384] . B[16384 x 16384]^T (inputs N(0, 1), E4M3
+payloads with E8M0 scales per 32-block along K, fp32 accumulation, Float32 C),
+M-split across the N GPUs: rank r contracts its 65536/N rows of A against a
+replica of B, with no collective on the data path.  One step = one pass over
+the whole C.  `value` is the whole-job TFLOP/s (2 M N K over the slowest
+rank's device time), `scaling` "strong" (the problem is fixed as N grows).
+
+The same line carries, under `k_split`, the K-split of the same contraction
+(each rank a K/N slice, Float32 partials reduce-scattered over NVLink with
+the C-ABI NCCL communicator, 8 N-chunks overlapping the next chunk's
+contraction) with the reduce-scatter timed alone as its communication floor;
+under `parity`, a sampled block of every rank's C checked against a float64
+product of the device-dequantised operands (and, for the M-split, against a
+single contraction of the same rows, bit for bit); and, at one GPU, the
+layout-aware reductions, MX quantisation, the 8192^3 contractions and the MLP
+training step of the other configurations.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Inputs are larger than L2 (each layout's X is 128 MiB, and consecutive
-launches read different buffers), timing is by CUDA events on the launching
-stream, and the multi-GPU value is the max over ranks (weak scaling: each
-rank reduces its own X, there is no collective on the data path).
+Operands (1.25 GiB per rank at N = 1, 0.38 GiB at N = 8) are larger than L2;
+timing is by CUDA events on the launching stream; the multi-GPU time is the
+max over ranks.
 """
 
 from __future__ import annotations
@@ -32,6 +42,18 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# ---- the headline: the sharded MXFP8 contraction --------------------------------
+M5, N5, K5 = 65536, 16384, 16384
+FLOP5 = 2.0 * M5 * N5 * K5
+K_CHUNKS = 8
+PARITY_TOL = 2e-3  # relative Frobenius error of the contraction path
+# DRAM bytes (read + write) per launch of the M-split contraction at one GPU,
+# from ncu on the per-rank shape of eight GPUs (8192 x 16384 x 16384, the
+# committed capture) scaled by the 8x rows: A reads and C writes grow with the
+# rows, and so do B's re-reads (one pass of B per raster group of row tiles).
+NCU_TRAFFIC_GEMM_8192_ROWS = None
+
+# ---- the layout-aware reductions (config 2) ---------------------------------------
 R, C = 8192, 4096
 X_BYTES = R * C * 4
 RED_BYTES = X_BYTES + R * 4  # algorithmic bytes of one reduction launch
@@ -75,6 +97,17 @@ def load_peaks() -> dict:
         d = json.loads(p.read_text())
         return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+METRIC = "sharded MXFP8 contraction TFLOP/s"
+
+
+def headline_config(world: int) -> dict:
+    """The `config` of the JSON line, the same in both arms."""
+    return {"workload": "config5_sharded_mxfp8_65536x16384x16384", "M": M5, "N": N5, "K": K5,
+            "split": "M (B replicated, no collective)", "parallelism": f"M-split x{world}",
+            "formats": "E4M3 payload, E8M0 scale per 32 along K, fp32 accumulate, Float32 C",
+            "l2": "operands larger than L2 (1.25 GiB at one GPU, 0.38 GiB per rank at eight)"}
 
 
 class ClockSampler:
@@ -132,132 +165,435 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------
-# reference arm: the reference CPU carrier on the host cores
+# reference arm: the reference CPU carrier's matmul on the host cores
+
+
+def reference_matmul_rate(rows_per_thread: int, cols: int, reps: int, warmup: int,
+                          threads: int | None = None) -> tuple[float, int, str]:
+    """Time the reference CPU carrier's Float32 matmul (``sw.matmul``, the
+    contraction the MX contraction replaces, run on dequantised operands) on a
+    bounded sample of the headline workload: ``rows_per_thread`` rows of A per
+    host thread against ``cols`` rows of B, K = 16384, every thread a zero-copy
+    row slice (the reference kernel is single-threaded and releases the GIL).
+    Returns (TFLOP/s, threads, sample description)."""
+    sys.path.append(str(ROOT / "baseline" / "_ref"))
+    import strideweave as sw
+    from strideweave import CPU, Layout, Shape, Stride, Tensor
+    from concurrent.futures import ThreadPoolExecutor
+
+    threads = threads or os.cpu_count() or 1
+    rows = rows_per_thread * threads
+    rng = np.random.default_rng(0)
+    # N(0, 1) stand-ins for the dequantised operands (values do not change the
+    # CPU kernel's speed)
+    a = rng.standard_normal((rows, K5), dtype=np.float32)
+    b = rng.standard_normal((cols, K5), dtype=np.float32)
+    ta = Tensor(CPU(a.size, pointer=a.ctypes.data), 0, Layout(Shape([rows, K5]), Stride([K5, 1])))
+    tb = Tensor(CPU(b.size, pointer=b.ctypes.data), 0, Layout(Shape([cols, K5]), Stride([K5, 1])))
+
+    def job(t: int) -> None:
+        with sw.no_grad():
+            sw.matmul(ta[t * rows_per_thread:(t + 1) * rows_per_thread, :], tb)
+
+    with ThreadPoolExecutor(threads) as pool:
+        for _ in range(warmup):
+            list(pool.map(job, range(threads)))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            list(pool.map(job, range(threads)))
+        dt = (time.perf_counter() - t0) / max(reps, 1)
+    tflops = 2.0 * rows * cols * K5 / dt / 1e12
+    sample = (f"{rows} rows of A x {cols} rows of B (K = {K5}) per step, {rows_per_thread} rows per host thread; "
+              f"the reference CPU carrier's Float32 matmul on dequantised-operand stand-ins")
+    return tflops, threads, sample
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    sys.path.append(str(ROOT / "baseline" / "_ref"))
     try:
-        import strideweave as sw
-        from strideweave import CPU, Layout, Shape, Stride, Tensor
+        sys.path.append(str(ROOT / "baseline" / "_ref"))
+        import strideweave  # noqa: F401
     except Exception as exc:  # pragma: no cover - reported, not raised
         print(json.dumps({"impl": "reference", "unavailable": f"reference not importable: {exc}"}))
         return
-    from concurrent.futures import ThreadPoolExecutor
-
-    rng = np.random.default_rng(0)
-    x = rng.uniform(-1, 1, size=(R, C)).astype(np.float32)
-    # The reference cannot place a tensor through a Swizzle: layout (c) runs on
-    # the tiled layout over un-swizzled storage (the logical data it reduces is
-    # the same).
-    stores = {
-        "rowmajor": np.ascontiguousarray(x).ravel(),
-        "transposed": np.ascontiguousarray(x.T).ravel(),
-        "tiled_swizzled": np.ascontiguousarray(x.reshape(64, 128, 128, 32).transpose(0, 2, 1, 3)).ravel(),
-    }
-    layouts = {
-        "rowmajor": Layout(Shape([R, C]), Stride([C, 1])),
-        "transposed": Layout(Shape([R, C]), Stride([1, R])),
-        "tiled_swizzled": Layout(Shape([[128, 64], [32, 128]]), Stride([[32, 128 * 32 * 128], [1, 128 * 32]])),
-    }
-    threads = os.cpu_count() or 1
-    fns = {"reduce_sum": sw.reduce_sum, "reduce_max": sw.reduce_max, "argmax": sw.argmax}
-    carriers = {k: CPU(v.size, pointer=v.ctypes.data) for k, v in stores.items()}
-
-    def slice_job(layout, op, lo, hi):
-        # rows lo..hi of the kept mode as a zero-copy view (the reference
-        # kernels are single-threaded; slices run on separate host threads)
-        base = Tensor(carriers[layout], 0, layouts[layout])
-        view = base[lo:hi, :] if layout != "tiled_swizzled" else None
-        if view is None:
-            # tiled layout: slice whole 128-row tiles through the outer leaf
-            tlo, thi = lo // 128, hi // 128
-            view = Tensor(carriers[layout], tlo * 128 * 32 * 128,
-                          Layout(Shape([[128, thi - tlo], [32, 128]]), Stride([[32, 128 * 32 * 128], [1, 128 * 32]])))
-        with sw.no_grad():
-            return fns[op](view, "a b -> a")
-
-    bounds = [(i * R // threads // 128 * 128, (i + 1) * R // threads // 128 * 128) for i in range(threads)]
-    bounds[-1] = (bounds[-1][0], R)
-
-    def step(pool):
-        futures = [pool.submit(slice_job, lay, op, lo, hi) for op in OPS for lay in LAYOUTS for lo, hi in bounds
-                   if hi > lo]
-        for f in futures:
-            f.result()
-
-    with ThreadPoolExecutor(threads) as pool:
-        for _ in range(args.warmup):
-            step(pool)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            step(pool)
-        dt = (time.perf_counter() - t0) / args.steps
-    value = 9 * RED_BYTES / dt / 1e9
+    tflops, threads, sample = reference_matmul_rate(rows_per_thread=2, cols=2048, reps=args.steps,
+                                                    warmup=args.warmup)
+    ms = FLOP5 / (tflops * 1e12) * 1e3
     print(json.dumps({
-        "impl": "reference", "metric": "reduction HBM GB/s", "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2_reductions_8192x4096", "ops": list(OPS), "layouts": list(LAYOUTS)},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
-                         "sample": "full X[8192x4096] per step, kept rows split over host threads"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": round(tflops, 8), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+        "config": headline_config(args.gpus),
+        "cpu_baseline": {"value": round(tflops, 8), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(tflops, 8), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "ms_per_step extrapolates the sample's rate to the whole 65536 x 16384 x 16384 contraction",
     }))
+
+
+def cpu_baseline_sample() -> dict:
+    """The reference CPU carrier on a bounded sample (rank 0, N = 1 only)."""
+    try:
+        tflops, threads, sample = reference_matmul_rate(rows_per_thread=2, cols=2048, reps=2, warmup=1)
+        kind = "reference"
+    except ImportError:  # no installed reference: the oracle's restatement of its matmul
+        from oracle import oracle as O
+
+        rng = np.random.default_rng(0)
+        a = rng.standard_normal((4, K5), dtype=np.float32)
+        b = rng.standard_normal((512, K5), dtype=np.float32)
+        t0 = time.perf_counter()
+        O.matmul(a, b)
+        tflops = 2.0 * 4 * 512 * K5 / (time.perf_counter() - t0) / 1e12
+        threads, kind = 1, "port"
+        sample = f"4 rows of A x 512 rows of B (K = {K5}), the oracle's restatement of the reference matmul"
+    return {"value": round(tflops, 8), "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample}
+
+
+# ---------------------------------------------------------------------------------
+# the headline: config 5, the sharded MXFP8 contraction
+
+
+def quantize_generated(torch, N, kernels, fmt, rows, cols, seed, sigma=1.0, block=8192):
+    """Device planes of a seeded N(0, sigma^2) [rows, cols] operand, generated
+    and quantised in row blocks (bounded Float32 staging)."""
+    rb = kernels.mx_row_bytes(fmt, cols)
+    katoms = (cols // 32 + 3) // 4
+    pay = N.DeviceBuffer(rows * rb)
+    sc = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, cols // 32))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    for r0 in range(0, rows, block):
+        n = min(block, rows - r0)
+        x = torch.randn((n, cols), generator=gen, device="cuda", dtype=torch.float32) * sigma
+        kernels.mx_quantize(fmt, x.data_ptr(), n, cols, cols, 1, pay.ptr + r0 * rb, rb,
+                            sc.ptr + (r0 // 128) * katoms * 512)
+        N.synchronize()  # x is released by torch's allocator on its own stream
+        del x
+    return pay, sc
+
+
+def max_over_ranks(torch, dist, world, value: float) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_steps(N, fn, steps: int, warmup: int, torch, dist, world) -> float:
+    """Mean device ms of `fn` over `steps` calls on the legacy default stream
+    (events on that stream), max over ranks."""
+    for _ in range(warmup):
+        fn()
+    N.synchronize()
+    if world > 1:
+        dist.barrier()
+    N.synchronize()
+    e0, e1 = N.Event(timing=True), N.Event(timing=True)
+    e0.record(0)
+    for _ in range(steps):
+        fn()
+    e1.record(0)
+    ms = e0.elapsed_ms(e1) / steps
+    N.synchronize()
+    if world > 1:
+        dist.barrier()
+    return max_over_ranks(torch, dist, world, ms)
+
+
+def dequantized_rows(N, kernels, fmt, planes, row0: int, rows: int, k: int) -> np.ndarray:
+    """Float32 image of operand rows [row0, row0 + rows) (whole 128-row scale
+    groups), by the device dequantiser."""
+    rb = kernels.mx_row_bytes(fmt, k)
+    katoms = (k // 32 + 3) // 4
+    out = N.DeviceBuffer(4 * rows * k)
+    kernels.mx_dequantize(fmt, planes[0].ptr + row0 * rb, rb, planes[1].ptr + (row0 // 128) * katoms * 512, rows, k,
+                          out.ptr, k)
+    host = np.empty((rows, k), np.float32)
+    N.synchronize()
+    out.download(host)
+    return host
+
+
+def result_block(N, op, row0: int, n0: int, rows: int = 128, cols: int = 256) -> np.ndarray:
+    """C[row0 : row0 + rows, n0 : n0 + cols] of the rank's result (local rows)."""
+    plan = op.plan
+    if plan.mode == "m" or plan.chunks == 1:
+        base, pitch, col = op.out.data_ptr, plan.N, n0
+    else:
+        c = n0 // plan.chunk_cols
+        base, pitch, col = op.out.data_ptr + 4 * c * plan.rows_local * plan.chunk_cols, plan.chunk_cols, \
+            n0 % plan.chunk_cols
+    span = np.empty((rows, pitch), np.float32)
+    N.synchronize()
+    N.check(N.lib.sw_memcpy_d2h(N.c_void_p(span.ctypes.data), N.c_void_p(base + 4 * row0 * pitch), span.nbytes,
+                                None))
+    return span[:, col:col + cols].copy()
+
+
+def sharded_parity(torch, dist, N, kernels, fmt, op, a, b, world, rank) -> dict:
+    """A 128 x 256 block of this rank's C against the float64 product of the
+    device-dequantised operands (the dequantiser is bit-exact with the CPU
+    oracle in the tests), summed over every rank's K slice for a K-split; for
+    an M-split also against a single contraction of the same rows, which must
+    be bit-identical.  Returns the worst error over ranks."""
+    plan = op.plan
+    rng = np.random.default_rng(4242 + 31 * rank + (1 if plan.mode == "k" else 0))
+    g_local = int(rng.integers(0, plan.rows_local // 128))
+    row0 = g_local * 128                                   # in this rank's C rows
+    n0 = int(rng.integers(0, plan.N // 256)) * 256         # whole 256-wide tile, inside one chunk
+    got = result_block(N, op, row0, n0).astype(np.float64)
+    out = {"sample": f"C rows [{plan.row0 + row0}, +128) x cols [{n0}, +256) on each rank"}
+    if plan.mode == "m":
+        da = dequantized_rows(N, kernels, fmt, a, row0, 128, plan.k_local).astype(np.float64)
+        db = dequantized_rows(N, kernels, fmt, b, n0, 256, plan.k_local).astype(np.float64)
+        want = da @ db.T
+        # the same rows as one contraction on this GPU
+        rb = kernels.mx_row_bytes(fmt, plan.k_local)
+        katoms = (plan.k_local // 32 + 3) // 4
+        single = N.DeviceBuffer(4 * 128 * 256)
+        kernels.mx_gemm(fmt, a[0].ptr + row0 * rb, rb, a[1].ptr + g_local * katoms * 512, b[0].ptr + n0 * rb, rb,
+                        b[1].ptr + (n0 // 128) * katoms * 512, single.ptr, 128, 256, plan.k_local)
+        one = np.empty((128, 256), np.float32)
+        N.synchronize()
+        single.download(one)
+        bit_exact = bool(np.array_equal(one.astype(np.float64), got))
+    else:
+        # every rank contributes its K slice to every rank's sample
+        samples = [(plan.row0 + row0, n0)]
+        if world > 1:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, samples[0])
+            samples = gathered
+        mine = []
+        for grow0, gn0 in samples:
+            da = dequantized_rows(N, kernels, fmt, a, grow0, 128, plan.k_local).astype(np.float64)
+            db = dequantized_rows(N, kernels, fmt, b, gn0, 256, plan.k_local).astype(np.float64)
+            mine.append(da @ db.T)
+        if world > 1:
+            parts = [None] * world
+            dist.all_gather_object(parts, mine)
+            want = sum(p[rank] for p in parts)
+        else:
+            want = mine[0]
+        bit_exact = None
+    err = float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-300))
+    out["rel_frobenius"] = max_over_ranks(torch, dist, world, err)
+    if bit_exact is not None:
+        flag = max_over_ranks(torch, dist, world, 0.0 if bit_exact else 1.0)
+        out["single_contraction_bit_exact"] = flag == 0.0
+    out["tol"] = PARITY_TOL
+    out["ok"] = out["rel_frobenius"] <= PARITY_TOL and out.get("single_contraction_bit_exact", True)
+    return out
+
+
+def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
+    """Config 5 at this world size: the M-split (headline), its end-to-end
+    pass from host memory, and the K-split with its communication floor."""
+    from strideweave_b200.sharding import MXShardedContraction, NcclCommunicator, ShardPlan
+
+    fmt = N.SW_MX_E4M3
+    res: dict = {}
+    # ---- M-split ----
+    mp = ShardPlan("m", world, rank, M5, N5, K5)
+    a = quantize_generated(torch, N, kernels, fmt, mp.rows_local, K5, seed=7000 + rank)
+    b = quantize_generated(torch, N, kernels, fmt, N5, K5, seed=9000)
+    op = MXShardedContraction(mp, fmt, a, b)
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))).__enter__()
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak_seconds:  # clocks settle under load
+        op.run()
+        N.synchronize()
+    ms = time_steps(N, op.run, args.steps, args.warmup, torch, dist, world)
+    time.sleep(0.25)
+    clocks.__exit__(None, None, None)
+    res["m"] = {"ms": ms, "tflops": FLOP5 / (ms / 1e3) / 1e12, "launch_flop": mp.local_flops,
+                "clocks": clocks.summary()}
+    N.raise_device_status()
+    res["m"]["parity"] = sharded_parity(torch, dist, N, kernels, fmt, op, a, b, world, rank)
+
+    # ---- end to end: Float32 operands in pinned host memory -> quantise ->
+    # contract -> C back to host, every step ----
+    rows, k = mp.rows_local, K5
+    pin_a = torch.empty((rows, k), dtype=torch.float32).pin_memory()
+    pin_b = torch.empty((N5, k), dtype=torch.float32).pin_memory()
+    pin_c = torch.empty((rows, N5), dtype=torch.float32).pin_memory()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5000 + rank)
+    for host in (pin_a, pin_b):  # fill from device draws (host RNG over GiBs is slow)
+        for r0 in range(0, host.shape[0], 8192):
+            host[r0:r0 + 8192].copy_(torch.randn((min(8192, host.shape[0] - r0), k), generator=gen, device="cuda"))
+    torch.cuda.synchronize()
+    fa, fb = N.DeviceBuffer(4 * rows * k), N.DeviceBuffer(4 * N5 * k)
+    rb = kernels.mx_row_bytes(fmt, k)
+
+    def e2e_step():
+        N.check(N.lib.sw_memcpy_h2d(N.c_void_p(fa.ptr), N.c_void_p(pin_a.data_ptr()), fa.nbytes, None))
+        N.check(N.lib.sw_memcpy_h2d(N.c_void_p(fb.ptr), N.c_void_p(pin_b.data_ptr()), fb.nbytes, None))
+        kernels.mx_quantize(fmt, fa.ptr, rows, k, k, 1, a[0].ptr, rb, a[1].ptr)
+        kernels.mx_quantize(fmt, fb.ptr, N5, k, k, 1, b[0].ptr, rb, b[1].ptr)
+        op.run()
+        N.check(N.lib.sw_memcpy_d2h(N.c_void_p(pin_c.data_ptr()), N.c_void_p(op.out.data_ptr), pin_c.numel() * 4,
+                                    None))
+
+    e2e_ms = time_steps(N, e2e_step, max(2, min(args.steps, 3)), 1, torch, dist, world)
+    res["e2e"] = {"value": FLOP5 / (e2e_ms / 1e3) / 1e12, "ms": e2e_ms,
+                  "h2d": world * (fa.nbytes + fb.nbytes), "d2h": world * pin_c.numel() * 4}
+    N.raise_device_status()
+    del pin_a, pin_b, pin_c, fa, fb, op, a, b
+    N.synchronize()
+    torch.cuda.empty_cache()
+
+    # ---- K-split ----
+    kp = ShardPlan("k", world, rank, M5, N5, K5, chunks=K_CHUNKS)
+    comm = None
+    if world > 1:
+        ids = [NcclCommunicator.new_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        comm = NcclCommunicator(world, rank, ids[0])
+    a = quantize_generated(torch, N, kernels, fmt, M5, kp.k_local, seed=8000 + rank)
+    b = quantize_generated(torch, N, kernels, fmt, N5, kp.k_local, seed=9500 + rank)
+    op = MXShardedContraction(kp, fmt, a, b, comm=comm)
+    ksteps = max(3, args.steps // 4)
+    kms = time_steps(N, op.run, ksteps, min(args.warmup, 2), torch, dist, world)
+    res["k"] = {"ms": kms, "tflops": FLOP5 / (kms / 1e3) / 1e12, "chunks": K_CHUNKS, "comm_sms": kp.comm_sms}
+    N.raise_device_status()
+    res["k"]["parity"] = sharded_parity(torch, dist, N, kernels, fmt, op, a, b, world, rank)
+    if comm is not None:
+        # the reduce-scatter alone: all 8 chunks of Float32 partials (4 GiB per
+        # rank), on the collective's stream, with every SM free
+        count = kp.rows_local * kp.chunk_cols
+        cs = op.comm_stream.handle
+
+        def comm_only():
+            for c in range(kp.chunks):
+                comm.reduce_scatter_f32(op._chunk_out(c), op.partials[c % len(op.partials)].data_ptr, count, cs)
+            ev = N.Event()
+            ev.record(cs)
+            ev.wait(0)
+
+        cms = time_steps(N, comm_only, 3, 1, torch, dist, world)
+        moved = (world - 1) / world * 4.0 * M5 * N5  # bytes each rank sends (and receives)
+        compute_ms = res["m"]["ms"]  # the same FLOP per rank as the M-split's contraction
+        bound = max(compute_ms, cms)
+        res["k"]["comm_floor"] = {"ms": cms, "busbw_gbs": moved / (cms / 1e3) / 1e9,
+                                  "bytes_per_rank": moved, "compute_ms": compute_ms, "bound_ms": bound,
+                                  "frac_of_bound": bound / kms}
+        op.close()
+        comm.close()
+    else:
+        op.close()
+    del op, a, b
+    N.synchronize()
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------------
+# config 2: the layout-aware reductions (one GPU)
+
+
+def bench_reductions(torch, N, kernels, args) -> dict:
+    """Sum, max and argmax over mode 1 of X[8192 x 4096] ~ U(-1, 1) on a
+    row-major, a transposed and a tiled + swizzled layout; one step = the 9
+    reductions, consecutive launches reading different 128 MiB buffers."""
+    rng = np.random.default_rng(1234)
+    x = rng.uniform(-1, 1, size=(R, C)).astype(np.float32)
+    host = {lay: storage_of(lay, x) for lay in LAYOUTS}
+    dev = {lay: N.DeviceBuffer(X_BYTES) for lay in LAYOUTS}
+    for lay in LAYOUTS:
+        dev[lay].upload(host[lay])
+    outs = {(op, lay): N.DeviceBuffer(R * 4) for op in OPS for lay in LAYOUTS}
+    N.synchronize()
+    order = [(op, lay) for op in OPS for lay in LAYOUTS]
+    # plans are built once: the timed loop is one C call per launch
+    plans = {}
+    for op in OPS:
+        for lay in LAYOUTS:
+            kept, red, swz = plan_of(lay)
+            plans[(op, lay)] = kernels.make_reduce_plan(op, 0, kept, red, swz)
+
+    def launch_on(op, lay, ptr):
+        N.check(N.lib.sw_reduce_f32(N.ctypes.byref(plans[(op, lay)]), N.c_void_p(ptr), R * C,
+                                    N.c_void_p(outs[(op, lay)].ptr), None))
+
+    def step():
+        for op, lay in order:
+            launch_on(op, lay, dev[lay].ptr)
+
+    ms_per_step = time_steps(N, step, args.steps, args.warmup, torch, None, 1)
+    # per-kernel durations: each kernel back to back over two copies of its
+    # input (256 MiB > L2), one event pair per run of launches
+    spare = {lay: N.DeviceBuffer(X_BYTES) for lay in LAYOUTS}
+    for lay in LAYOUTS:
+        N.check(N.lib.sw_memcpy_d2d(N.c_void_p(spare[lay].ptr), N.c_void_p(dev[lay].ptr), X_BYTES, None))
+    per_kernel = {}
+    runs = max(6, args.steps // 3)
+    for op in OPS:
+        for lay in LAYOUTS:
+            bufs = (dev[lay].ptr, spare[lay].ptr)
+            launch_on(op, lay, bufs[0])
+            k0, k1 = N.Event(timing=True), N.Event(timing=True)
+            k0.record(0)
+            for r in range(runs):
+                launch_on(op, lay, bufs[(r + 1) % 2])
+            k1.record(0)
+            per_kernel[(op, lay)] = k0.elapsed_ms(k1) / runs
+    # the timed reduce_max agrees with the sequential rule
+    check = np.empty(R, dtype=np.float32)
+    outs[("reduce_max", "rowmajor")].download(check)
+    assert np.array_equal(check, x.max(axis=1)), "timed reduce_max disagrees with numpy"
+    # end to end: pinned host input -> device -> 9 reductions -> host
+    pinned = {lay: torch.from_numpy(host[lay]).pin_memory() for lay in LAYOUTS}
+    res_host = torch.empty(R * 9, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        for lay in LAYOUTS:
+            N.check(N.lib.sw_memcpy_h2d(N.c_void_p(dev[lay].ptr), N.c_void_p(pinned[lay].data_ptr()), X_BYTES, None))
+        step()
+        for j, key in enumerate(order):
+            N.check(N.lib.sw_memcpy_d2h(N.c_void_p(res_host.data_ptr() + 4 * R * j), N.c_void_p(outs[key].ptr),
+                                        R * 4, None))
+
+    e2e_ms = time_steps(N, e2e_step, max(3, args.steps // 4), 1, torch, None, 1)
+    peaks = load_peaks()
+    by_layout = {lay: sum(per_kernel[(op, lay)] for op in OPS) for lay in LAYOUTS}
+    dominant = max(by_layout, key=by_layout.get)
+    achieved = RED_BYTES / (by_layout[dominant] / 3 / 1e3) / 1e9
+    N.raise_device_status()
+    return {
+        "gbs": round(9 * RED_BYTES / (ms_per_step / 1e3) / 1e9, 2), "ms_per_step": round(ms_per_step, 4),
+        "config": "config 2: X[8192 x 4096] ~ U(-1,1); sum, max, argmax over mode 1 on row-major, transposed and "
+                  "tiled ((128,64),(32,128)) + 3-bit swizzle layouts; inputs larger than L2, rotated",
+        "roofline": {"bound": "hbm", "kernel": f"sw_reduce_f32[{dominant}]", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": NCU_TRAFFIC.get(dominant),
+                     "per_kernel_gbs": {f"{op}/{lay}": round(RED_BYTES / (per_kernel[(op, lay)] / 1e3) / 1e9, 1)
+                                        for op, lay in order}},
+        "e2e": {"value": round(9 * RED_BYTES / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": 3 * X_BYTES, "d2h_bytes_per_step": 9 * R * 4},
+    }
 
 
 # ---------------------------------------------------------------------------------
 # our arm
 
 
-def cpu_baseline_sample() -> dict:
-    """The reference CPU carrier on a bounded sample (rank 0, N=1 only)."""
-    sys.path.append(str(ROOT / "baseline" / "_ref"))
-    try:
-        import strideweave as sw
-        from strideweave import CPU, Layout, Shape, Stride, Tensor
-        kind = "reference"
-    except Exception:
-        sw = None
-        kind = "port"
-    rng = np.random.default_rng(1)
-    rows = 2048  # a quarter of X: ~1/4 of the config's work per op
-    x = rng.uniform(-1, 1, size=(rows, C)).astype(np.float32)
-    t0 = time.perf_counter()
-    if kind == "reference":
-        store_a = np.ascontiguousarray(x).ravel()
-        store_b = np.ascontiguousarray(x.T).ravel()
-        ta = Tensor(CPU(store_a.size, pointer=store_a.ctypes.data), 0, Layout(Shape([rows, C]), Stride([C, 1])))
-        tb = Tensor(CPU(store_b.size, pointer=store_b.ctypes.data), 0, Layout(Shape([rows, C]), Stride([1, rows])))
-        with sw.no_grad():
-            for fn in (sw.reduce_sum, sw.reduce_max, sw.argmax):
-                fn(ta, "a b -> a")
-                fn(tb, "a b -> a")
-        n_ops = 6
-    else:
-        from oracle import oracle as O
-        flat = np.ascontiguousarray(x).ravel()
-        for k in ("sum", "max", "argmax"):
-            O.reduce(k, flat, 0, [(rows, C)], [(C, 1)])
-        n_ops = 3
-    dt = time.perf_counter() - t0
-    gbs = n_ops * (rows * C * 4 + rows * 4) / dt / 1e9
-    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
-            "sample": f"{n_ops} reductions over X[{rows}x{C}] (row-major and transposed), single-threaded kernels"}
-
-
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-gemm", action="store_true", help="skip the contraction measurements")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="at one GPU, skip the secondary measurements (reductions, quantise, 8192^3, MLP)")
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed busy time under the clock sampler before the timed region")
-    ap.add_argument("--profile-case", choices=["reduce", "quantize", "dual", "mxfp8", "mxfp4", "mlp"],
+    ap.add_argument("--profile-case", choices=["reduce", "quantize", "dual", "mxfp8", "mxfp4", "mlp", "sharded",
+                                               "misc"],
                     help="run a short, fixed sequence of launches for ncu and exit (no timing)")
     ap.add_argument("--reps", type=int, default=2, help="rounds of launches of --profile-case")
     args = ap.parse_args()
@@ -277,200 +613,76 @@ def main() -> None:
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
 
     from strideweave_b200 import _native as N
     from strideweave_b200 import kernels
 
     N.set_device(local)
-    stream = torch.cuda.current_stream()
-    s = stream.cuda_stream
-
-    rng = np.random.default_rng(1234 + rank)
-    x = rng.uniform(-1, 1, size=(R, C)).astype(np.float32)
-    host = {lay: storage_of(lay, x) for lay in LAYOUTS}
-    dev = {lay: N.DeviceBuffer(X_BYTES) for lay in LAYOUTS}
-    for lay in LAYOUTS:
-        dev[lay].upload(host[lay])
-    outs = {(op, lay): N.DeviceBuffer(R * 4) for op in OPS for lay in LAYOUTS}
-    N.synchronize()
-
-    # consecutive launches read different 128 MiB buffers (> L2)
-    order = [(op, lay) for op in OPS for lay in LAYOUTS]
-
-    # plans are built once: the timed loop is one C call per launch, so the
-    # host stays ahead of the device
-    plans = {}
-    for op in OPS:
-        for lay in LAYOUTS:
-            kept, red, swz = plan_of(lay)
-            plans[(op, lay)] = kernels.make_reduce_plan(op, 0, kept, red, swz)
-    stream_arg = N.c_void_p(s)
-
-    def launch_on(op, lay, ptr):
-        N.check(N.lib.sw_reduce_f32(N.ctypes.byref(plans[(op, lay)]), N.c_void_p(ptr), R * C,
-                                    N.c_void_p(outs[(op, lay)].ptr), stream_arg))
-
-    def launch(op, lay):
-        launch_on(op, lay, dev[lay].ptr)
-
-    clocks = ClockSampler(local).__enter__()
-    for _ in range(args.warmup):
-        for op, lay in order:
-            launch(op, lay)
-    torch.cuda.synchronize()
-    # keep the device busy ~1 s under the clock sampler before timing
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < args.soak_seconds:
-        for op, lay in order:
-            launch(op, lay)
-        torch.cuda.synchronize()
-
-    # -------- timed region: device-resident inputs --------
-    # One event pair brackets the K steps: an event recorded between two
-    # launches costs the stream a few microseconds, which the step itself
-    # does not spend.
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    start.record(stream)
-    for it in range(args.steps):
-        for op, lay in order:
-            launch(op, lay)
-    end.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    total_ms = start.elapsed_time(end)
-    t = torch.tensor([total_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    ms_per_step = max_ms / args.steps
-    value = world * 9 * RED_BYTES / (ms_per_step / 1e3) / 1e9
-
-    # -------- per-kernel durations (roofline): each kernel launched back to
-    # back over rotating inputs, one event pair per run of launches --------
-    # A second copy of each layout alternates with the first, so consecutive
-    # launches read 256 MiB (> L2).
-    spare = {lay: N.DeviceBuffer(X_BYTES) for lay in LAYOUTS}
-    for lay in LAYOUTS:
-        N.check(N.lib.sw_memcpy_d2d(N.c_void_p(spare[lay].ptr), N.c_void_p(dev[lay].ptr), X_BYTES, stream_arg))
-    per_kernel = {}
-    runs = max(6, args.steps // 3)
-    for op in OPS:
-        for lay in LAYOUTS:
-            bufs = (dev[lay].ptr, spare[lay].ptr)
-            launch_on(op, lay, bufs[0])
-            k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            k0.record(stream)
-            for r in range(runs):
-                launch_on(op, lay, bufs[(r + 1) % 2])
-            k1.record(stream)
-            torch.cuda.synchronize()
-            per_kernel[(op, lay)] = k0.elapsed_time(k1) / runs
-    time.sleep(0.25)
-    clocks.__exit__(None, None, None)
-
-    # correctness spot check of what was timed (device vs the sequential rule)
-    check = np.empty(R, dtype=np.float32)
-    outs[("reduce_max", "rowmajor")].download(check)
-    assert np.array_equal(check, x.max(axis=1)), "timed reduce_max disagrees with numpy"
-
-    # -------- end-to-end: pinned host input -> device -> reduce -> host --------
-    pinned = {lay: torch.from_numpy(host[lay]).pin_memory() for lay in LAYOUTS}
-    res_host = torch.empty(R * 9, dtype=torch.float32).pin_memory()
-    e2e_steps = max(3, args.steps // 4)
-
-    def e2e_step():
-        for lay in LAYOUTS:
-            N.check(N.lib.sw_memcpy_h2d(N.c_void_p(dev[lay].ptr), N.c_void_p(pinned[lay].data_ptr()), X_BYTES,
-                                        N.c_void_p(s)))
-        for j, (op, lay) in enumerate(order):
-            launch(op, lay)
-        for j, (op, lay) in enumerate(order):
-            N.check(N.lib.sw_memcpy_d2h(N.c_void_p(res_host.data_ptr() + 4 * R * j), N.c_void_p(outs[(op, lay)].ptr),
-                                        R * 4, N.c_void_p(s)))
-
-    e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item()) / e2e_steps
-    e2e_value = world * 9 * RED_BYTES / (e2e_ms / 1e3) / 1e9
-
-    # -------- contractions (configs 1 and 3) on this device --------
-    contraction = None
-    quantize = None
-    sharded = None
-    mlp = None
-    if not args.no_gemm:
-        quantize = bench_quantize(torch, N, kernels, s, stream)
-        contraction = bench_gemm(torch, N, kernels, s, stream)
-        # config 5 at this world size (strong scaling of a fixed contraction)
-        sharded = {m: bench_sharded(torch, dist, N, kernels, m, world, rank) for m in ("m", "k")}
-        mlp = bench_mlp(torch, N)
+    sharded = bench_sharded(torch, dist, N, kernels, args, world, rank)
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras["reductions"] = bench_reductions(torch, N, kernels, args)
+        extras["quantize"] = bench_quantize(torch, N, kernels, 0, torch.cuda.current_stream())
+        extras["contraction"] = bench_gemm(torch, N, kernels, 0, torch.cuda.current_stream())
+        extras["mlp_step"] = bench_mlp(torch, N)
 
     if rank == 0:
         peaks = load_peaks()
-        by_layout = {lay: sum(per_kernel[(op, lay)] for op in OPS) for lay in LAYOUTS}
-        dominant = max(by_layout, key=by_layout.get)
-        dom_ms = by_layout[dominant] / 3
-        achieved = RED_BYTES / (dom_ms / 1e3) / 1e9
+        m = sharded["m"]
+        # MXFP8 block-scaled MMA runs at twice the dense bf16 rate; the measured
+        # cuBLAS bf16 burst figure stands for the clock and power of this pool
+        peak = 2.0 * peaks["bf16_tflops"]
+        kernel_tflops = m["launch_flop"] / (m["ms"] / 1e3) / 1e12
+        traffic = None
+        if NCU_TRAFFIC_GEMM_8192_ROWS is not None:
+            traffic = NCU_TRAFFIC_GEMM_8192_ROWS * (M5 // world) / 8192
+        k = sharded["k"]
         line = {
-            "metric": "reduction HBM GB/s",
-            "value": round(value, 2),
-            "unit": "GB/s",
+            "metric": METRIC,
+            "value": round(m["tflops"], 1),
+            "unit": "TFLOP/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": round(ms_per_step, 4),
+            "ms_per_step": round(m["ms"], 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "f32",
-            "data": "synthetic U(-1,1), seeded",
-            "config": {"workload": "config2_reductions_8192x4096", "ops": list(OPS), "layouts": list(LAYOUTS),
-                       "step": "9 reductions (3 ops x 3 layouts)", "l2": "inputs larger than L2, rotated",
-                       "parallelism": f"replicas x{world} (each rank its own X)"},
-            "roofline": {"bound": "hbm", "kernel": f"sw_reduce_f32[{dominant}]", "achieved": round(achieved, 1),
-                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "peak_source": peaks["source"], "traffic": NCU_TRAFFIC.get(dominant),
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, mean of the "
-                                           "layout's three kernels, from the committed --set full capture",
-                         "per_layout_gbs": {lay: round(3 * RED_BYTES / (by_layout[lay] / 1e3) / 1e9, 1)
-                                            for lay in LAYOUTS},
-                         "per_kernel_gbs": {f"{op}/{lay}": round(RED_BYTES / (per_kernel[(op, lay)] / 1e3) / 1e9, 1)
-                                            for op, lay in order}},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 3 * X_BYTES,
-                    "d2h_bytes_per_step": 9 * R * 4},
-            "gpu_launches": 9 * args.steps,
-            "clocks": clocks.summary(),
+            "dtype": "mxfp8 (e4m3 x e8m0), fp32 accumulate",
+            "data": "synthetic N(0,1), seeded per rank",
+            "config": headline_config(world),
+            "roofline": {"bound": "tensor", "kernel": "mx_gemm_kernel<E4M3, 256, 3, fp32 rows>",
+                         "achieved": round(kernel_tflops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(kernel_tflops / peak, 4),
+                         "peak_source": f"{peaks['source']}: 2 x bf16 dense burst (MXFP8 is twice the bf16 rate)",
+                         "traffic": traffic, "frac_of_spec_4500": round(kernel_tflops / 4500.0, 4)},
+            "e2e": {"value": round(sharded["e2e"]["value"], 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sharded["e2e"]["h2d"], "d2h_bytes_per_step": sharded["e2e"]["d2h"]},
+            "gpu_launches": world * args.steps,
+            "clocks": m["clocks"],
+            "parity": {"m_split": m["parity"], "k_split": k["parity"]},
+            "k_split": {key: (round(v, 4) if isinstance(v, float) else v) for key, v in k.items()
+                        if key not in ("parity",)},
         }
-        if quantize:
-            line["quantize"] = quantize
-        if contraction:
-            line["contraction"] = contraction
-        if sharded:
-            line["sharded_contraction"] = {"m_split": sharded["m"], "k_split": sharded["k"]}
-        if mlp:
-            line["mlp_step"] = mlp
+        if "comm_floor" in k:
+            line["k_split"]["comm_floor"] = {key: round(v, 4) if isinstance(v, float) else v
+                                             for key, v in k["comm_floor"].items()}
+        for key, v in extras.items():
+            line[key] = v
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line))
+    parity_ok = sharded["m"]["parity"]["ok"] and sharded["k"]["parity"]["ok"]
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not parity_ok:  # the line above says which check failed
+        raise SystemExit("sharded contraction parity check failed")
+
+
+# ---------------------------------------------------------------------------------
+# secondary measurements (one GPU)
 
 
 def bench_gemm(torch, N, kernels, s, stream) -> dict:
@@ -582,63 +794,6 @@ def bench_quantize(torch, N, kernels, s, stream) -> dict:
     return out
 
 
-def quantize_generated(torch, N, kernels, fmt, rows, cols, seed, sigma=1.0, block=8192):
-    """Device planes of a seeded N(0, sigma^2) [rows, cols] operand, generated
-    and quantised in row blocks (bounded Float32 staging)."""
-    rb = kernels.mx_row_bytes(fmt, cols)
-    katoms = (cols // 32 + 3) // 4
-    pay = N.DeviceBuffer(rows * rb)
-    sc = N.DeviceBuffer(kernels.scale_bytes_tc128(rows, cols // 32))
-    gen = torch.Generator(device="cuda")
-    gen.manual_seed(seed)
-    s = torch.cuda.current_stream().cuda_stream
-    for r0 in range(0, rows, block):
-        n = min(block, rows - r0)
-        x = torch.randn((n, cols), generator=gen, device="cuda", dtype=torch.float32) * sigma
-        kernels.mx_quantize(fmt, x.data_ptr(), n, cols, cols, 1, pay.ptr + r0 * rb, rb,
-                            sc.ptr + (r0 // 128) * katoms * 512, stream=s)
-        del x
-    return pay, sc
-
-
-def bench_sharded(torch, dist, N, kernels, mode, world, rank, steps=5, warmup=2) -> dict:
-    """Config 5: sharded MXFP8 contraction M=65536, N=16384, K=16384, inputs
-    N(0,1), at `world` GPUs; M-split (B replicated, no collective) or K-split
-    (NCCL reduce-scatter of Float32 partials, overlapped over 8 N-chunks; the
-    contractions leave 32 SMs to the collective so the two run side by side)."""
-    from strideweave_b200.sharding import MXShardedContraction, ShardPlan
-
-    M, Nn, K = 65536, 16384, 16384
-    fmt = N.SW_MX_E4M3
-    plan = ShardPlan(mode, world, rank, M, Nn, K, k_quantum=128, chunks=8 if mode == "k" else 1)
-    rows = plan.rows_local if mode == "m" else M
-    a = quantize_generated(torch, N, kernels, fmt, rows, plan.k_local, seed=7000 + rank)
-    b = quantize_generated(torch, N, kernels, fmt, Nn, plan.k_local, seed=9000 + (rank if mode == "k" else 0))
-    op = MXShardedContraction(plan, fmt, a, b)
-    for _ in range(warmup):
-        op.run()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        op.run()
-    e1.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / steps], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    tflops = 2.0 * M * Nn * K / (ms / 1e3) / 1e12
-    N.raise_device_status()
-    del op, a, b
-    torch.cuda.empty_cache()
-    return {"tflops": round(tflops, 1), "ms": round(ms, 3), "n_gpus": world, "scaling": "strong",
-            "config": f"MXFP8 M=65536 N=16384 K=16384, {'M-split' if mode == 'm' else 'K-split + NCCL reduce-scatter, 8 N-chunks, 32 SMs left to the collective'}"}
-
-
 def bench_mlp(torch, N, steps=5, warmup=2) -> dict:
     """Config 4: one MXFP8 MLP training step - 1024 -> 4096 -> 4096 -> 1024 with
     GELU, batch 8192, fp32 master weights N(0, 0.02), inputs and targets N(0, 1),
@@ -701,8 +856,14 @@ def profile_case(case: str, reps: int) -> None:
     launches per round).  dual: the two-way MXFP8 quantiser over a
     [4096 x 8192] hidden activation, with GELU then with GELU', `reps` rounds
     (2 launches per round).  mxfp8 / mxfp4: quantise two 8192 x 8192
-    operands, then `reps` contractions at M = N = K = 8192 (bf16 C).  mlp: the
-    MLP training step, `reps` steps after one warm-up step.
+    operands, then `reps` contractions at M = N = K = 8192 (bf16 C).  sharded:
+    the M-split contraction of one of eight ranks (8192 x 16384 x 16384,
+    Float32 C), `reps` launches.  mlp: the MLP training step, `reps` steps
+    after one warm-up step.  misc: one launch each, `reps` rounds, of the
+    kernels the other cases do not reach - the batched contraction, the
+    elementwise AXPY, the MSE loss and gradient, the Float32 contraction, the
+    reduction gradients, the view copy, the view quantiser, the scale
+    rewrite and the binary product.
     """
     from strideweave_b200 import _native as N
     from strideweave_b200 import kernels
@@ -757,6 +918,18 @@ def profile_case(case: str, reps: int) -> None:
                 for op in OPS:
                     kept, red, swz = plan_of(lay)
                     kernels.reduce_f32(op, bufs[lay].ptr, R * C, 0, kept, red, out.ptr, swizzle=swz)
+    elif case == "sharded":
+        import torch
+
+        fmt, rows = N.SW_MX_E4M3, M5 // 8
+        a = quantize_generated(torch, N, kernels, fmt, rows, K5, seed=7000)
+        b = quantize_generated(torch, N, kernels, fmt, N5, K5, seed=9000)
+        c = N.DeviceBuffer(4 * rows * N5)
+        rb = kernels.mx_row_bytes(fmt, K5)
+        for _ in range(reps):
+            kernels.mx_gemm(fmt, a[0].ptr, rb, a[1].ptr, b[0].ptr, rb, b[1].ptr, c.ptr, rows, N5, K5)
+    elif case == "misc":
+        profile_misc(N, kernels, reps)
     else:
         fmt = N.SW_MX_E4M3 if case == "mxfp8" else N.SW_MX_E2M1
         M = Nn = K = 8192
@@ -778,6 +951,54 @@ def profile_case(case: str, reps: int) -> None:
                             c.ptr, M, Nn, K, out_bf16=True)
     N.raise_device_status()
     print(f"profile case {case}: ok")
+
+
+def profile_misc(N, kernels, reps: int) -> None:
+    """One launch each of the secondary kernels, on inputs larger than L2
+    where the kernel is bandwidth-bound (see profile_case)."""
+    rng = np.random.default_rng(3)
+    n = 64 << 20  # 64 Mi floats: 256 MiB per operand
+    xa, xb = N.DeviceBuffer(4 * n), N.DeviceBuffer(4 * n)
+    xa.upload(rng.standard_normal(n, dtype=np.float32))
+    xb.upload(rng.standard_normal(n, dtype=np.float32))
+    loss, grad = N.DeviceBuffer(4), N.DeviceBuffer(4 * n)
+    # batched MX contraction: 4 problems of 2048 x 2048 x 4096, fp32 C stacked
+    fmt, bm, bk, nb = N.SW_MX_E4M3, 2048, 4096, 4
+    src = N.DeviceBuffer(4 * nb * bm * bk)
+    src.upload(rng.standard_normal(nb * bm * bk, dtype=np.float32))
+    pay = N.DeviceBuffer(nb * bm * bk)
+    sc = N.DeviceBuffer(kernels.scale_bytes_tc128(nb * bm, bk // 32))
+    kernels.mx_quantize(fmt, src.ptr, nb * bm, bk, bk, 1, pay.ptr, bk, sc.ptr)
+    cb = N.DeviceBuffer(4 * nb * bm * bm)
+    # Float32 contraction 1024^3 (the reference's own plan, SIMT)
+    mf = 1024
+    # reductions' gradients and the view copy over the transposed X[8192 x 4096]
+    go = N.DeviceBuffer(4 * R)
+    go.upload(rng.standard_normal(R, dtype=np.float32))
+    # view quantiser over the tiled + swizzled config-2 layout
+    vq_pay, vq_sc = N.DeviceBuffer(R * C), N.DeviceBuffer(kernels.scale_bytes_tc128(R, C // 32))
+    rm_sc = N.DeviceBuffer(R * (C // 32))
+    pair = N.ctypes.c_int64 * 2  # out[i, j] = x[i, j] * go[i]: leaves (R, C), go broadcast along j
+    shape, dense, bcast = pair(R, C), pair(C, 1), pair(1, 0)
+    for _ in range(reps):
+        kernels.mx_gemm_batched(fmt, pay.ptr, bk, sc.ptr, pay.ptr, bk, sc.ptr, cb.ptr, nb, bm, bm, bk)
+        N.check(N.lib.sw_elementwise_f32(N.SW_EW_AXPY, n, N.c_void_p(xa.ptr), N.c_void_p(xb.ptr), N.c_void_p(xa.ptr),
+                                         -1e-3, None))
+        N.check(N.lib.sw_mse_f32(n, N.c_void_p(xa.ptr), N.c_void_p(xb.ptr), N.c_void_p(loss.ptr), None,
+                                 N.c_void_p(grad.ptr), None))
+        kernels.matmul_f32(xa.ptr, mf, 1, xb.ptr, mf, 1, grad.ptr, 1, mf, mf, mf, mf)
+        for kind in ("reduce_sum", "reduce_max"):
+            kernels.reduce_backward_f32(kind, xa.ptr, R * C, 0, [(R, 1)], [(C, R)], [], go.ptr, grad.ptr,
+                                        [(R, C)], [(C, 1)], R * C)
+        kernels.copy_view_f32(xa.ptr, R * C, 0, [(R, 1)], [(C, R)], grad.ptr, R * C, 0, [(R, C)], [(C, 1)])
+        kernels.mx_quantize_view(fmt, xa.ptr, R * C, 0, [(128, 32), (64, 128 * 32 * 128)],
+                                 [(32, 1), (128, 128 * 32)], vq_pay.ptr, C, vq_sc.ptr, swizzle=SWZ)
+        kernels.mx_quantize(fmt, xa.ptr, R, C, C, 1, vq_pay.ptr, C, rm_sc.ptr, scale_layout=N.SW_SCALES_ROWMAJOR,
+                            ld_scales=C // 32)
+        kernels.mx_scales_to_tc128(rm_sc.ptr, C // 32, R, C // 32, vq_sc.ptr)
+        N.check(N.lib.sw_binary_f32(N.SW_BIN_MUL, 2, shape, N.c_void_p(xa.ptr), 0, dense, R * C, N.c_void_p(go.ptr),
+                                    0, bcast, R, N.c_void_p(grad.ptr), 0, dense, R * C, None))
+        N.synchronize()
 
 
 if __name__ == "__main__":

@@ -74,6 +74,20 @@ int sw_stream_create(void** stream);
 int sw_stream_destroy(void* stream);
 int sw_stream_synchronize(void* stream);
 
+/* SMs of the current device (the persistent contraction's CTA budget). */
+int sw_device_sm_count(int* count);
+
+/* Events order the streams of a sharded contraction (a chunk's collective
+ * after its contraction, a partial buffer's reuse after its collective) and
+ * time work on the device.  `timing` = 0 creates a lighter event that cannot
+ * be timed.  sw_event_elapsed_ms waits for `end`.  No reference counterpart:
+ * the reference runs one host thread on one carrier. */
+int sw_event_create(void** event, int timing);
+int sw_event_destroy(void* event);
+int sw_event_record(void* event, void* stream);
+int sw_stream_wait_event(void* stream, void* event);
+int sw_event_elapsed_ms(void* start, void* end, float* ms);
+
 /* CUDA graphs of a stream's work, for a step that repeats with the same
  * buffers (an MLP training step): capture starts on a stream from
  * sw_stream_create and ends in an executable graph; the graph can then be
@@ -257,6 +271,27 @@ int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t cols,
                    int64_t ld_payload, uint8_t* scales, int scale_layout,
                    int64_t ld_scales, void* stream);
 
+/* sw_mx_quantize over any hierarchical two-mode Float32 view: `view` is the
+ * lowered layout (its kept leaves give the rows, its reduced leaves the
+ * quantised axis, `kind` ignored), carrier flat index f holding element
+ * (r, c) as in sw_reduce_plan, through the carrier swizzle, within a carrier
+ * of x_size elements (checked before any launch).  Same planes, bit for bit,
+ * as sw_mx_quantize on the same logical values.  This is how a tiled or
+ * swizzled Float32 tensor (src/strideweave/core/layout.py:1374-1546,
+ * src/strideweave/core/swizzle.py:107-117) is quantised where it lies. */
+int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const float* x,
+                        int64_t x_size, uint8_t* payload, int64_t ld_payload,
+                        uint8_t* scales, int scale_layout, int64_t ld_scales,
+                        void* stream);
+
+/* Rewrites a row-major scale plane (scales[r * ld_src + kb], rows x kblocks)
+ * into the SW_SCALES_TC128 placement sw_mx_gemm reads, padding with 127.
+ * An MX tensor whose rows or blocks are not whole 128 x 4 atoms keeps its
+ * scales row-major (the reference's LevelExtent(0, 32) rule wants the scale
+ * plane's shape to be exactly rows x K/32); its contraction goes through this. */
+int sw_mx_scales_to_tc128(const uint8_t* src, int64_t ld_src, int64_t rows,
+                          int64_t kblocks, uint8_t* dst, void* stream);
+
 /* What sw_mx_quantize_dual quantises: S = x, gelu(x), or x * gelu'(h). */
 #define SW_XF_NONE 0
 #define SW_XF_GELU 1      /* S = x * Phi(x), as SW_EW_GELU                         */
@@ -294,12 +329,14 @@ int sw_mx_dequantize(int fmt, const uint8_t* payload, int64_t ld_payload,
 
 /* C[m, n] = sum_k A[m, k] * B[n, k] over MX operands, fp32 accumulation.
  * A: payload rows of K elements (K-major) with row pitch lda bytes, scales in
- * the SW_SCALES_TC128 placement for M x K/32; B likewise for N x K/32.
- * C[m, n] is written at c[m*ldc_m + n*ldc_n] (elements of out_dtype); either
- * pitch may be 1 (row- or column-major).  When `beta_one` is non-zero the
- * result is added to C's current fp32 contents instead of replacing them.
- * Requires fmt_a == fmt_b, M % 128 == 0, N % 128 == 0, K % 128 == 0 (E4M3) or
- * K % 256 == 0 (E2M1), 16-byte aligned payload pointers and pitches.
+ * the SW_SCALES_TC128 placement for M x K/32 (whole atoms: its padding blocks
+ * must hold finite scales, as sw_mx_quantize writes them); B likewise for
+ * N x K/32.  C[m, n] is written at c[m*ldc_m + n*ldc_n] (elements of
+ * out_dtype); either pitch may be 1 (row- or column-major).  When `beta_one`
+ * is non-zero the result is added to C's current fp32 contents instead of
+ * replacing them.  Any M and N (a ragged last tile is clipped); K a positive
+ * multiple of 32 (whole MX blocks).  Requires fmt_a == fmt_b and 16-byte
+ * aligned payload pointers and pitches.
  * Replaces CpuMatmulOperation::_forward
  * (src/strideweave/carriers/cpu/native/ops/matmul.cpp:45-113) for MX operands,
  * which the reference refuses (operation_policy.py:1407-1440). */
@@ -328,11 +365,14 @@ int sw_mx_gemm_ex(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
  * lda, SW_SCALES_TC128 scales of the whole stack), B_p rows [p N, (p + 1) N)
  * of one [batch N, K] operand.  C_p starts batch_stride_c elements after
  * C_(p-1) and has the pitches ldc_m / ldc_n.  The C_p must be disjoint:
- * with batch > 1, a batch_stride_c below one problem's span
- * (M-1) ldc_m + (N-1) ldc_n + 1 is refused with SW_ERR_INVALID.  Row-major
+ * with batch > 1, the three strides (batch_stride_c, ldc_m, ldc_n), taken in
+ * increasing order, must each exceed the span of the modes below them
+ * (stacked blocks and interleaved problems both qualify); other placements
+ * are refused with SW_ERR_INVALID.  Row-major
  * results with batch_stride_c = M ldc_m and column-major ones with
  * batch_stride_c = N ldc_n are written by the staged epilogues; any other
- * stride stores from registers.  Other arguments and errors as sw_mx_gemm. */
+ * stride stores from registers.  M and N must be multiples of 128 (whole
+ * scale atoms per problem).  Other arguments and errors as sw_mx_gemm. */
 int sw_mx_gemm_batched(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda,
                        const uint8_t* scales_a, const uint8_t* b, int64_t ldb,
                        const uint8_t* scales_b, void* c, int out_dtype,
@@ -392,6 +432,28 @@ int sw_binary_f32(int op, int rank, const int64_t* shape,
                   const float* b, int64_t b_offset, const int64_t* b_stride, int64_t b_size,
                   float* out, int64_t out_offset, const int64_t* out_stride, int64_t out_size,
                   void* stream);
+
+/* The elementwise arithmetic the reference's nn modules compose (a Linear's
+ * bias add, an MSE loss's difference, square and mean scale, and their
+ * gradients), each a binary32 operation per element as the CPU carrier's
+ * kernels do it. */
+#define SW_MAP_ADD 0      /* a + b: CpuAddOperation (ops/add.cpp)                          */
+#define SW_MAP_SUB 1      /* a - b: CpuSubOperation (ops/sub.cpp)                          */
+#define SW_MAP_MUL 2      /* a * b: the tensor-tensor mul (ops/scalar_mul.cpp)             */
+#define SW_MAP_SCALE 3    /* a * scalar: CpuScalarMulOperation (ops/scalar_mul.cpp)        */
+#define SW_MAP_POW 4      /* pow(a, scalar): the tensor ** weak-scalar CpuPowOperation     */
+#define SW_MAP_POW_GRAD 5 /* a * scalar * pow(b, scalar - 1): that pow's gradient (ops/pow.cpp:160-175),
+                           * a = incoming gradient, b = base                               */
+
+/* sw_binary_f32 generalised to the SW_MAP_* operations: the same shared-leaf
+ * walk and bounds checks; SCALE and POW read only `a` (b and its strides may
+ * be NULL).  pow with exponent 2 or 1 is the exact product the reference's
+ * std::pow gives; other exponents use the device powf. */
+int sw_map_f32(int op, int rank, const int64_t* shape,
+               const float* a, int64_t a_offset, const int64_t* a_stride, int64_t a_size,
+               const float* b, int64_t b_offset, const int64_t* b_stride, int64_t b_size,
+               float* out, int64_t out_offset, const int64_t* out_stride, int64_t out_size,
+               float scalar, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -44,6 +44,12 @@ SW_EW_GELU = 0
 SW_EW_GELU_GRAD = 1
 SW_EW_AXPY = 2
 SW_BIN_MUL = 0
+SW_MAP_ADD = 0
+SW_MAP_SUB = 1
+SW_MAP_MUL = 2
+SW_MAP_SCALE = 3
+SW_MAP_POW = 4
+SW_MAP_POW_GRAD = 5
 SW_XF_NONE = 0
 SW_XF_GELU = 1
 SW_XF_GELU_GRAD = 2
@@ -91,6 +97,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_stream_create": (c_int, [POINTER(c_void_p)]),
     "sw_stream_destroy": (c_int, [c_void_p]),
     "sw_stream_synchronize": (c_int, [c_void_p]),
+    "sw_device_sm_count": (c_int, [POINTER(c_int)]),
+    "sw_event_create": (c_int, [POINTER(c_void_p), c_int]),
+    "sw_event_destroy": (c_int, [c_void_p]),
+    "sw_event_record": (c_int, [c_void_p, c_void_p]),
+    "sw_stream_wait_event": (c_int, [c_void_p, c_void_p]),
+    "sw_event_elapsed_ms": (c_int, [c_void_p, c_void_p, POINTER(ctypes.c_float)]),
     "sw_probe_bounded_wait": (c_int, [c_int64, c_void_p]),
     "sw_nccl_get_unique_id": (c_int, [c_void_p]),
     "sw_nccl_comm_init": (c_int, [POINTER(c_void_p), c_int, c_int, c_void_p]),
@@ -118,6 +130,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p],
     ),
+    "sw_mx_quantize_view": (
+        c_int,
+        [c_int, POINTER(ReducePlan), c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p],
+    ),
+    "sw_mx_scales_to_tc128": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "sw_mx_quantize_dual": (
         c_int,
         [c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
@@ -167,6 +184,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, c_int, POINTER(c_int64), c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p, c_int64,
          POINTER(c_int64), c_int64, c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p],
+    ),
+    "sw_map_f32": (
+        c_int,
+        [c_int, c_int, POINTER(c_int64), c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p, c_int64,
+         POINTER(c_int64), c_int64, c_void_p, c_int64, POINTER(c_int64), c_int64, ctypes.c_float, c_void_p],
     ),
 }
 
@@ -284,3 +306,75 @@ class DeviceBuffer:
 
 def synchronize(stream: int | None = None) -> None:
     check(lib.sw_stream_synchronize(c_void_p(stream or 0)))
+
+
+def sm_count() -> int:
+    """SMs of the current device."""
+    n = c_int(0)
+    check(lib.sw_device_sm_count(ctypes.byref(n)))
+    return n.value
+
+
+class Stream:
+    """A non-blocking stream of the current device (``sw_stream_create``);
+    ``handle`` is the ``cudaStream_t`` the C entry points take."""
+
+    __slots__ = ("handle", "__weakref__")
+
+    def __init__(self) -> None:
+        s = c_void_p(0)
+        check(lib.sw_stream_create(ctypes.byref(s)))
+        self.handle = s.value or 0
+
+    def synchronize(self) -> None:
+        synchronize(self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib.sw_stream_destroy(c_void_p(self.handle)))
+            self.handle = 0
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order
+        try:
+            if self.handle:
+                lib.sw_stream_destroy(c_void_p(self.handle))
+                self.handle = 0
+        except Exception:
+            pass
+
+
+class Event:
+    """A CUDA event (``sw_event_*``): orders one stream after another's work,
+    or, created with ``timing=True``, times work on the device."""
+
+    __slots__ = ("handle", "__weakref__")
+
+    def __init__(self, timing: bool = False) -> None:
+        e = c_void_p(0)
+        check(lib.sw_event_create(ctypes.byref(e), int(bool(timing))))
+        self.handle = e.value or 0
+
+    def record(self, stream: int = 0) -> None:
+        check(lib.sw_event_record(c_void_p(self.handle), c_void_p(stream or 0)))
+
+    def wait(self, stream: int = 0) -> None:
+        """Work enqueued on ``stream`` after this call waits for the event."""
+        check(lib.sw_stream_wait_event(c_void_p(stream or 0), c_void_p(self.handle)))
+
+    def elapsed_ms(self, end: "Event") -> float:
+        ms = ctypes.c_float(0.0)
+        check(lib.sw_event_elapsed_ms(c_void_p(self.handle), c_void_p(end.handle), ctypes.byref(ms)))
+        return float(ms.value)
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib.sw_event_destroy(c_void_p(self.handle)))
+            self.handle = 0
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order
+        try:
+            if self.handle:
+                lib.sw_event_destroy(c_void_p(self.handle))
+                self.handle = 0
+        except Exception:
+            pass

@@ -600,6 +600,117 @@ int grid_for(int64_t items, int threads) {
     return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sm_count_mx()) * 16));
 }
 
+// ---- quantise: any hierarchical view, through a carrier swizzle ---------------
+// The source is a two-mode view lowered to leaves (first leaf fastest, as in
+// sw_reduce_plan): mode 0 gives the row, mode 1 the quantised axis.  A warp
+// takes one 32-block: lane i walks element 32 kb + i of row r to its carrier
+// flat index (leaf decomposition), through the swizzle, and the block's amax is
+// a warp reduction.  Every address is checked against the carrier size before
+// it is read; one outside (which the host's range check excludes) reads as NaN
+// and records SW_ERR_INVALID in the device error word.
+struct ViewLeaves {
+    int rank;
+    int64_t shape[SW_MAX_LEAVES];
+    int64_t stride[SW_MAX_LEAVES];
+};
+
+struct ViewPlan {
+    int64_t offset;
+    int64_t x_size;
+    ViewLeaves rows, cols;
+    int swz_rank;
+    int swz_bits[SW_MAX_SWIZZLE];
+    int swz_base[SW_MAX_SWIZZLE];
+    int swz_shift[SW_MAX_SWIZZLE];
+};
+
+__device__ __forceinline__ int64_t leaf_offset(const ViewLeaves& l, int64_t i) {
+    int64_t off = 0;
+#pragma unroll
+    for (int k = 0; k < SW_MAX_LEAVES; ++k) {
+        if (k < l.rank) {
+            const int64_t c = i % l.shape[k];
+            i /= l.shape[k];
+            off += c * l.stride[k];
+        }
+    }
+    return off;
+}
+
+// The carrier swizzle of src/strideweave/core/swizzle.py:107-117, stage by stage.
+__device__ __forceinline__ int64_t view_swizzle(const ViewPlan& p, int64_t f) {
+#pragma unroll
+    for (int i = 0; i < SW_MAX_SWIZZLE; ++i) {
+        if (i < p.swz_rank) {
+            const int64_t mask = (int64_t(1) << p.swz_bits[i]) - 1;
+            if (p.swz_shift[i] > 0) f ^= ((f >> (p.swz_base[i] + p.swz_shift[i])) & mask) << p.swz_base[i];
+            else f ^= ((f >> p.swz_base[i]) & mask) << (p.swz_base[i] - p.swz_shift[i]);
+        }
+    }
+    return f;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) quantize_view(const float* __restrict__ x, const ViewPlan p, int64_t rows,
+                                                     int64_t cols, uint8_t* __restrict__ payload, int64_t ldp,
+                                                     uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    pdl_enter();
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t units = rows * kblocks;
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t u = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+        const int64_t r = u / kblocks;
+        const int64_t kb = u - r * kblocks;
+        const int64_t c = kb * 32 + lane;
+        const bool live = c < cols;
+        float v = 0.0f;
+        if (live) {
+            const int64_t f = view_swizzle(p, p.offset + leaf_offset(p.rows, r) + leaf_offset(p.cols, c));
+            if (f >= 0 && f < p.x_size) {
+                v = __ldcs(x + f);
+            } else {
+                report_device_error(SW_ERR_INVALID);
+                v = __int_as_float(0x7FC00000);
+            }
+        }
+        const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(v) & 0x7FFFFFFFu);
+        uint8_t sc;
+        float inv;
+        bool special;
+        block_scale<FMT>(amax, sc, inv, special);
+        if (lane == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+        const float q = special ? 0.0f : __fmul_rn(v, inv);
+        if (FMT == SW_MX_E4M3) {
+            const uint32_t code = e4m3x4(q, 0.0f, 0.0f, 0.0f) & 0xFF;
+            if (live) payload[r * ldp + c] = uint8_t(code);
+        } else {
+            float eight[8] = {q, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            const uint32_t nib = e2m1x8(eight) & 0xF;
+            const uint32_t hi = __shfl_down_sync(0xFFFFFFFFu, nib, 1);
+            if (live && (lane & 1) == 0) {
+                uint8_t* dst = payload + r * ldp + c / 2;
+                if (c + 1 < cols) *dst = uint8_t(nib | (hi << 4));
+                else *dst = uint8_t((*dst & 0xF0) | nib);  // odd row length: the high nibble is not ours
+            }
+        }
+    }
+}
+
+// Row-major E8M0 scales -> the SW_SCALES_TC128 atom placement (padding left at
+// 127 by the caller), so a plane quantised with a row-major placement (rows or
+// blocks not whole atoms) can feed the tensor-core contraction.
+__global__ void __launch_bounds__(256) scales_to_tc128(const uint8_t* __restrict__ src, int64_t ld_src, int64_t rows,
+                                                       int64_t kblocks, uint8_t* __restrict__ dst) {
+    pdl_enter();
+    const int64_t total = rows * kblocks;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int64_t r = t / kblocks, kb = t - r * kblocks;
+        dst[scale_offset(SW_SCALES_TC128, r, kb, kblocks, 0)] = src[r * ld_src + kb];
+    }
+}
+
 }  // namespace
 }  // namespace sw
 
@@ -657,6 +768,98 @@ extern "C" int sw_mx_quantize(int fmt, const float* x, int64_t rows, int64_t col
                     "quantize_strided launch");
     }
     SW_LAUNCH_CHECK("sw_mx_quantize launch");
+    return ok();
+}
+
+extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const float* x, int64_t x_size,
+                                   uint8_t* payload, int64_t ld_payload, uint8_t* scales, int scale_layout,
+                                   int64_t ld_scales, void* stream) {
+    using namespace sw;
+    if (fmt != SW_MX_E4M3 && fmt != SW_MX_E2M1)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: unknown format %d", fmt);
+    if (scale_layout != SW_SCALES_ROWMAJOR && scale_layout != SW_SCALES_TC128)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: unknown scale layout %d", scale_layout);
+    if (!view) return fail(SW_ERR_INVALID, "sw_mx_quantize_view: null view");
+    if (view->kept_rank < 0 || view->kept_rank > SW_MAX_LEAVES || view->reduced_rank < 1 ||
+        view->reduced_rank > SW_MAX_LEAVES || view->swizzle_rank < 0 || view->swizzle_rank > SW_MAX_SWIZZLE)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: leaf or swizzle rank out of range");
+    ViewPlan p;
+    std::memset(&p, 0, sizeof(p));
+    p.offset = view->offset;
+    p.x_size = x_size;
+    int64_t rows = 1, cols = 1, lo = view->offset, hi = view->offset;
+    auto lower = [&](int rank, const int64_t* shape, const int64_t* stride, ViewLeaves& out, int64_t& n) -> bool {
+        out.rank = rank;
+        for (int l = 0; l < rank; ++l) {
+            if (shape[l] < 0) return false;
+            out.shape[l] = shape[l] > 0 ? shape[l] : 1;
+            out.stride[l] = stride[l];
+            n *= shape[l];
+            const int64_t span = (shape[l] > 0 ? shape[l] - 1 : 0) * stride[l];
+            if (span < 0) lo += span; else hi += span;
+        }
+        return true;
+    };
+    if (!lower(view->kept_rank, view->kept_shape, view->kept_stride, p.rows, rows) ||
+        !lower(view->reduced_rank, view->reduced_shape, view->reduced_stride, p.cols, cols))
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: negative extent");
+    p.swz_rank = view->swizzle_rank;
+    int top = -1;
+    for (int i = 0; i < view->swizzle_rank; ++i) {
+        p.swz_bits[i] = view->swizzle_bits[i];
+        p.swz_base[i] = view->swizzle_base[i];
+        p.swz_shift[i] = view->swizzle_shift[i];
+        // the constraints of SwizzleStage (src/strideweave/core/swizzle.py:44-60)
+        if (p.swz_bits[i] <= 0 || p.swz_base[i] < 0 || p.swz_shift[i] == 0 ||
+            std::abs(p.swz_shift[i]) < p.swz_bits[i] || p.swz_bits[i] + p.swz_base[i] + std::abs(p.swz_shift[i]) > 62)
+            return fail(SW_ERR_INVALID, "sw_mx_quantize_view: invalid swizzle stage %d", i);
+        const int tgt = p.swz_shift[i] > 0 ? p.swz_base[i] : p.swz_base[i] - p.swz_shift[i];
+        top = std::max(top, tgt + p.swz_bits[i] - 1);
+    }
+    if (rows == 0 || cols == 0) return ok();
+    if (!x || !payload || !scales) return fail(SW_ERR_INVALID, "sw_mx_quantize_view: null pointer");
+    if (lo < 0 || hi >= x_size)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: view addresses [%lld, %lld] outside carrier of %lld elements",
+                    (long long)lo, (long long)hi, (long long)x_size);
+    if (top >= 0) {
+        // a swizzle rewrites bits up to `top` only: addresses stay in their
+        // aligned 2^(top+1) window, which must lie inside the carrier
+        const int64_t win = int64_t(1) << (top + 1);
+        if ((hi / win + 1) * win - 1 >= x_size)
+            return fail(SW_ERR_INVALID, "sw_mx_quantize_view: swizzle may address past the carrier end");
+    }
+    const int64_t kblocks = (cols + 31) / 32;
+    const int64_t min_ldp = fmt == SW_MX_E4M3 ? cols : (cols + 1) / 2;
+    if (ld_payload < min_ldp)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: payload pitch %lld < row bytes %lld", (long long)ld_payload,
+                    (long long)min_ldp);
+    if (scale_layout == SW_SCALES_ROWMAJOR && ld_scales < kblocks)
+        return fail(SW_ERR_INVALID, "sw_mx_quantize_view: scale pitch smaller than blocks per row");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (scale_layout == SW_SCALES_TC128 && (rows % 128 != 0 || kblocks % 4 != 0))
+        SW_CUDA_TRY(cudaMemsetAsync(scales, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s),
+                    "scale padding fill");
+    const int grid = grid_for(rows * kblocks * 32, 256);
+    auto kernel = fmt == SW_MX_E4M3 ? quantize_view<SW_MX_E4M3> : quantize_view<SW_MX_E2M1>;
+    SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, x, p, rows, cols, payload, ld_payload, scales, scale_layout,
+                           ld_scales),
+                "quantize_view launch");
+    SW_LAUNCH_CHECK("sw_mx_quantize_view launch");
+    return ok();
+}
+
+extern "C" int sw_mx_scales_to_tc128(const uint8_t* src, int64_t ld_src, int64_t rows, int64_t kblocks, uint8_t* dst,
+                                     void* stream) {
+    using namespace sw;
+    if (rows < 0 || kblocks < 0) return fail(SW_ERR_INVALID, "sw_mx_scales_to_tc128: negative extent");
+    if (rows == 0 || kblocks == 0) return ok();
+    if (!src || !dst) return fail(SW_ERR_INVALID, "sw_mx_scales_to_tc128: null pointer");
+    if (ld_src < kblocks) return fail(SW_ERR_INVALID, "sw_mx_scales_to_tc128: source pitch smaller than blocks per row");
+    cudaStream_t s = (cudaStream_t)stream;
+    SW_CUDA_TRY(cudaMemsetAsync(dst, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s), "scale padding fill");
+    const int grid = grid_for(rows * kblocks, 256);
+    SW_CUDA_TRY(launch_pdl(scales_to_tc128, grid, 256, 0, s, src, ld_src, rows, kblocks, dst), "scales_to_tc128 launch");
+    SW_LAUNCH_CHECK("sw_mx_scales_to_tc128 launch");
     return ok();
 }
 

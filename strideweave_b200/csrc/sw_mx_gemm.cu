@@ -112,8 +112,10 @@ struct GemmArgs {
     void* c;
     int64_t ldc_m, ldc_n;
     int M, N, K;          // K in elements
-    int k_stages;         // K / elements-per-stage
+    int k_stages;         // ceil(payload row bytes / 128): the last stage may be partly past K
     int katoms;           // scale atoms per row group (ceil(K/128))
+    int row_bytes;        // payload bytes of one operand row (K or K/2)
+    int b_groups;         // 128-row groups in B's scale plane (ceil(batch N / 128))
     int beta_one;
     int out_bf16;
     int batch;            // stacked problems (block-diagonal), 1 for one contraction
@@ -164,8 +166,10 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
     // previous grid's tail; operands are read only after it completes
     pdl_enter();
 
-    const int num_m = args.M / kBM;
-    const int num_n = args.N / BN;
+    // ragged extents: the last tile row / column reaches past M / N; its
+    // operand rows there are zero-filled by TMA and its results are not stored
+    const int num_m = (args.M + kBM - 1) / kBM;
+    const int num_n = (args.N + BN - 1) / BN;
     const int per_batch = num_m * num_n;
     const int num_tiles = args.batch * per_batch;
     constexpr int kGroup = 8;  // M blocks per raster group (L2 reuse of B)
@@ -200,17 +204,26 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                 for (int ks = 0; ks < args.k_stages; ++ks) {
                     if (!ptx::mbar_wait(bar_empty + 8 * stage, phase ^ 1)) { alive = false; break; }
                     const uint32_t full = bar_full + 8 * stage;
-                    ptx::mbar_arrive_expect_tx(full, C::kStageTx);
+                    const int64_t atom0 = int64_t(ks) * C::kAtoms;
+                    // Scale atoms that exist: the last E2M1 stage of an odd atom
+                    // count has one, and B groups past the plane (a ragged N
+                    // whose last tile covers one 128-row group) have none.  The
+                    // payload boxes always count in full (TMA zero-fills past K).
+                    const int atoms = (int)min(int64_t(C::kAtoms), int64_t(args.katoms) - atom0);
+                    int b_groups_here = 0;
+#pragma unroll
+                    for (int g = 0; g < BN / 128; ++g) b_groups_here += (gb * (BN / 128) + g < args.b_groups) ? 1 : 0;
+                    ptx::mbar_arrive_expect_tx(full, C::kABytes + C::kBBytes + (1 + b_groups_here) * atoms * 512);
                     ptx::tma_load_2d(sbase + C::kOffA + stage * C::kABytes, &tmap_a, ks * kBKBytes, ga * kBM, full);
                     ptx::tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tmap_b, ks * kBKBytes, gb * BN, full);
-                    const int64_t atom0 = int64_t(ks) * C::kAtoms;
                     ptx::bulk_load(sbase + C::kOffSfa + stage * C::kSfaBytes,
-                                   args.sfa + (int64_t(ga) * args.katoms + atom0) * 512, C::kSfaBytes, full);
+                                   args.sfa + (int64_t(ga) * args.katoms + atom0) * 512, atoms * 512, full);
 #pragma unroll
                     for (int g = 0; g < BN / 128; ++g) {
+                        if (gb * (BN / 128) + g >= args.b_groups) continue;
                         ptx::bulk_load(sbase + C::kOffSfb + stage * C::kSfbBytes + g * C::kAtoms * 512,
                                        args.sfb + ((int64_t(gb) * (BN / 128) + g) * args.katoms + atom0) * 512,
-                                       C::kAtoms * 512, full);
+                                       atoms * 512, full);
                     }
                     issued[stage] += 1;
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -238,9 +251,15 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     const uint32_t sf_col = tmem + C::kSfCol0 + stage * C::kSfColsPerStage;
                     const uint32_t sfa_col = sf_col;
                     const uint32_t sfb_col = sf_col + C::kSfaCols;
-                    // scale atoms: shared memory -> TMEM (replicated per sub-partition)
+                    // the stage's real K: 32 payload bytes per MMA, the atoms the producer loaded
+                    const int atoms = min(C::kAtoms, args.katoms - ks * C::kAtoms);
+                    const int mmas = min(C::kMmaPerStage, (args.row_bytes - ks * kBKBytes + 31) / 32);
+                    // scale atoms: shared memory -> TMEM (replicated per sub-partition).
+                    // A B group past the plane was not loaded: its stale scales
+                    // only reach result columns past N, which are not stored.
 #pragma unroll
                     for (int a = 0; a < C::kAtoms; ++a) {
+                        if (a >= atoms) break;
                         ptx::tc_cp_32x128b_x4(sfa_col + 4 * a,
                                               ptx::smem_desc(sbase + C::kOffSfa + stage * C::kSfaBytes + a * 512, 0,
                                                              128, ptx::kLayoutNone));
@@ -255,6 +274,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     const uint32_t b_addr = sbase + C::kOffB + stage * C::kBBytes;
 #pragma unroll
                     for (int j = 0; j < C::kMmaPerStage; ++j) {
+                        if (j >= mmas) break;
                         // 32 payload bytes of K per MMA in both formats
                         const uint64_t adesc = ptx::smem_desc(a_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
                         const uint64_t bdesc = ptx::smem_desc(b_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
@@ -339,7 +359,9 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             if (leader && alive) {
 #pragma unroll
                 for (int g = 2 * half; g < 2 * half + 2; ++g)
-                    ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, (p * num_m + mb) * kBM, stage_addr + g * (kBM * 128));
+                    if (nb * BN + g * 64 < args.N)  // boxes partly past M or N are clipped by TMA
+                        ptx::tma_store_2d(&tmap_c, nb * BN + g * 64, (p * num_m + mb) * kBM,
+                                          stage_addr + g * (kBM * 128));
                 ptx::bulk_commit_group();
             }
         }
@@ -398,7 +420,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     ptx::fence_proxy_async_smem();
                 }
                 ptx::named_barrier(1 + half, 128);
-                if (leader && alive) {
+                if (leader && alive && nb * BN + chunk * 32 < args.N) {  // partial boxes are clipped by TMA
                     const uint32_t src = stage_addr + buf * kChunkBytes;
                     if (kEpi == kEpiF32Cols)
                         ptx::tma_store_2d(&tmap_c, mb * kBM, (p * num_n + nb) * BN + chunk * 32, src);
@@ -420,15 +442,18 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             if (!ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) break;
             ptx::tc_fence_after();
             const int64_t m = int64_t(mb) * kBM + row_in_tile;
+            const bool row_in = m < args.M;  // the last tile row of a ragged M reaches past it
 #pragma unroll 1
             for (int chunk = 0; chunk < BN / 32; ++chunk) {
                 uint32_t r[32];
                 ptx::tmem_ld_32x32b_x32(tmem + C::kAccCol + (uint32_t(quarter * 32) << 16) + chunk * 32, r);
                 ptx::tmem_ld_wait();
                 const int64_t n0 = int64_t(nb) * BN + chunk * 32;
+                if (!row_in || n0 >= args.N) continue;
+                const int ncols = (int)min(int64_t(32), int64_t(args.N) - n0);  // < 32 only in the last column chunk
                 if (args.out_bf16) {
                     __nv_bfloat16* cptr = static_cast<__nv_bfloat16*>(args.c) + p * args.c_batch;
-                    if (args.ldc_n == 1 && (((m * args.ldc_m + n0) & 7) == 0) &&
+                    if (ncols == 32 && args.ldc_n == 1 && (((m * args.ldc_m + n0) & 7) == 0) &&
                         ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
                         uint4* dst = reinterpret_cast<uint4*>(cptr + m * args.ldc_m + n0);
 #pragma unroll
@@ -447,6 +472,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     } else {
 #pragma unroll
                         for (int e = 0; e < 32; ++e) {
+                            if (e >= ncols) break;
                             __nv_bfloat16* p = cptr + m * args.ldc_m + (n0 + e) * args.ldc_n;
                             float f = __uint_as_float(r[e]);
                             if (args.beta_one) f += __bfloat162float(*p);
@@ -455,7 +481,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     }
                 } else {
                     float* cptr = static_cast<float*>(args.c) + p * args.c_batch;
-                    if (args.ldc_n == 1 && (((m * args.ldc_m + n0) & 3) == 0) &&
+                    if (ncols == 32 && args.ldc_n == 1 && (((m * args.ldc_m + n0) & 3) == 0) &&
                         ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
                         float4* dst = reinterpret_cast<float4*>(cptr + m * args.ldc_m + n0);
 #pragma unroll
@@ -471,6 +497,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     } else {
 #pragma unroll
                         for (int e = 0; e < 32; ++e) {
+                            if (e >= ncols) break;
                             float* p = cptr + m * args.ldc_m + (n0 + e) * args.ldc_n;
                             float f = __uint_as_float(r[e]);
                             if (args.beta_one) f += *p;
@@ -572,8 +599,10 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.M = (int)M;
     args.N = (int)N;
     args.K = (int)K;
-    args.k_stages = (int)(row_bytes / kBKBytes);
+    args.k_stages = (int)((row_bytes + kBKBytes - 1) / kBKBytes);
     args.katoms = (int)((K / 32 + 3) / 4);
+    args.row_bytes = (int)row_bytes;
+    args.b_groups = (int)((batch * N + 127) / 128);
     args.beta_one = beta_one;
     args.out_bf16 = out_dtype == SW_OUT_BF16;
     args.batch = (int)batch;
@@ -584,7 +613,7 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t tiles = batch * (M / kBM) * (N / BN);
+    const int64_t tiles = batch * ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
     int grid = (int)std::min<int64_t>(tiles, sms);
     if (max_ctas > 0) grid = std::min(grid, max_ctas);  // leave SMs to concurrent work (a collective)
     SW_CUDA_TRY(launch_pdl(kernel, grid, Cf::kThreads, Cf::kSmemBytes, stream, ma, mb, mc, args), "mx_gemm launch");
@@ -611,14 +640,20 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
     if (M < 0 || N < 0 || K < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: negative extent");
     if (M == 0 || N == 0) return ok();
     if (!a || !b || !scales_a || !scales_b || !c) return fail(SW_ERR_INVALID, "sw_mx_gemm: null pointer");
-    const int64_t kq = fmt_a == SW_MX_E4M3 ? 128 : 256;
-    if (M % 128 != 0 || N % 128 != 0 || K % kq != 0 || K == 0)
+    // Any M and N: the last tile row / column reaches past them, its operand
+    // rows are zero-filled by TMA and its results past M / N are not stored.
+    // K runs in whole 32-element MX blocks; past K the payload boxes are
+    // zero-filled and only the MMAs that reach real blocks are issued.
+    if (K % 32 != 0 || K == 0)
+        return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: needs K to be a positive multiple of 32 (got %lld x %lld x %lld)",
+                    (long long)M, (long long)N, (long long)K);
+    if (batch > 1 && (M % 128 != 0 || N % 128 != 0))
         return fail(SW_ERR_UNSUPPORTED,
-                    "sw_mx_gemm: needs M %% 128 == 0, N %% 128 == 0, K %% %lld == 0 (got %lld x %lld x %lld)",
-                    (long long)kq, (long long)M, (long long)N, (long long)K);
+                    "sw_mx_gemm_batched: needs M %% 128 == 0 and N %% 128 == 0 (got %lld x %lld)", (long long)M,
+                    (long long)N);
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: extent too large");
     if (batch < 1 || c_batch < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: bad batch count or result stride");
-    if (batch * M > INT32_MAX || batch * N > INT32_MAX || batch * (M / 128) * (N / 128) > INT32_MAX)
+    if (batch * M > INT32_MAX || batch * N > INT32_MAX || batch * ((M + 127) / 128) * ((N + 127) / 128) > INT32_MAX)
         return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: stacked extent too large");
     const int64_t row_bytes = fmt_a == SW_MX_E4M3 ? K : K / 2;
     if (lda < row_bytes || ldb < row_bytes || lda % 16 != 0 || ldb % 16 != 0)
@@ -628,11 +663,28 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
         return fail(SW_ERR_INVALID, "sw_mx_gemm: payload and scale planes must be 16-byte aligned");
     if (ldc_m < 1 || ldc_n < 1) return fail(SW_ERR_INVALID, "sw_mx_gemm: output pitches must be positive");
     // Stacked results must not overlap: CTAs of different problems store (and,
-    // with beta_one, read back) their tiles concurrently.
-    if (batch > 1 && c_batch < (M - 1) * ldc_m + (N - 1) * ldc_n + 1)
-        return fail(SW_ERR_INVALID,
-                    "sw_mx_gemm_batched: batch_stride_c %lld is smaller than one problem's result span %lld",
-                    (long long)c_batch, (long long)((M - 1) * ldc_m + (N - 1) * ldc_n + 1));
+    // with beta_one, read back) their tiles concurrently.  The (problem, m, n)
+    // -> element map is injective when, taking its three modes in order of
+    // stride, each stride exceeds the span of the modes below it; this admits
+    // stacked blocks and interleaved problems (a batch mode of stride 1) alike.
+    if (batch > 1) {
+        int64_t ext[3] = {batch, M, N}, str[3] = {c_batch, ldc_m, ldc_n};
+        for (int i = 0; i < 3; ++i)
+            for (int j = i + 1; j < 3; ++j)
+                if (str[j] < str[i]) { std::swap(str[i], str[j]); std::swap(ext[i], ext[j]); }
+        int64_t span = 0;
+        bool disjoint = true;
+        for (int i = 0; i < 3; ++i) {
+            if (ext[i] == 1) continue;
+            if (str[i] <= span) disjoint = false;
+            span += (ext[i] - 1) * str[i];
+        }
+        if (!disjoint)
+            return fail(SW_ERR_INVALID,
+                        "sw_mx_gemm_batched: results of the stacked problems may overlap (batch_stride_c %lld, "
+                        "ldc_m %lld, ldc_n %lld)",
+                        (long long)c_batch, (long long)ldc_m, (long long)ldc_n);
+    }
     if (max_ctas < 0) return fail(SW_ERR_INVALID, "sw_mx_gemm: max_ctas must be >= 0 (0 = every SM)");
     cudaStream_t s = (cudaStream_t)stream;
     // Results without accumulation, with a unit pitch on either side, take a
@@ -641,8 +693,12 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
     const bool aligned_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0;
     const int esize = out_dtype == SW_OUT_BF16 ? 2 : 4;
     int epi = kEpiDirect;
+    // 128 x 256 tiles unless the last one would be at most half used (then
+    // 128 x 128 tiles), and for stacked problems only whole 256-column tiles;
+    // a ragged last tile is clipped
+    const bool wide = N % 256 == 0 || (batch == 1 && N % 256 > 128);
     // (a batched launch stages its results only when they stack without gaps)
-    if (!beta_one && N % 256 == 0 && aligned_c) {
+    if (!beta_one && wide && aligned_c) {
         if (ldc_n == 1 && (ldc_m * esize) % 16 == 0 && ldc_m >= N && (batch == 1 || c_batch == M * ldc_m))
             epi = out_dtype == SW_OUT_BF16 ? kEpiBf16Rows : kEpiF32Rows;
         else if (out_dtype == SW_OUT_F32 && ldc_m == 1 && (ldc_n * 4) % 16 == 0 && ldc_n >= M &&
@@ -657,7 +713,7 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
     (epi == kEpiBf16Rows  ? SW_GEMM(F, 256, 3, kEpiBf16Rows)                             \
      : epi == kEpiF32Rows ? SW_GEMM(F, 256, 3, kEpiF32Rows)                              \
      : epi == kEpiF32Cols ? SW_GEMM(F, 256, 3, kEpiF32Cols)                              \
-     : N % 256 == 0       ? SW_GEMM(F, 256, 4, kEpiDirect)                               \
+     : wide               ? SW_GEMM(F, 256, 4, kEpiDirect)                               \
                           : SW_GEMM(F, 128, 4, kEpiDirect))
     rc = fmt_a == SW_MX_E4M3 ? SW_GEMM_FMT(SW_MX_E4M3) : SW_GEMM_FMT(SW_MX_E2M1);
 #undef SW_GEMM_FMT

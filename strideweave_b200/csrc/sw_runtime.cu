@@ -180,6 +180,47 @@ int sw_stream_synchronize(void* stream) {
     return ok();
 }
 
+int sw_device_sm_count(int* count) {
+    if (!count) return fail(SW_ERR_INVALID, "sw_device_sm_count: null output");
+    int dev = 0;
+    SW_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    SW_CUDA_TRY(cudaDeviceGetAttribute(count, cudaDevAttrMultiProcessorCount, dev), "SM count");
+    return ok();
+}
+
+int sw_event_create(void** event, int timing) {
+    if (!event) return fail(SW_ERR_INVALID, "sw_event_create: null output");
+    cudaEvent_t e;
+    SW_CUDA_TRY(cudaEventCreateWithFlags(&e, timing ? cudaEventDefault : cudaEventDisableTiming), "cudaEventCreate");
+    *event = (void*)e;
+    return ok();
+}
+
+int sw_event_destroy(void* event) {
+    if (!event) return ok();
+    SW_CUDA_TRY(cudaEventDestroy((cudaEvent_t)event), "cudaEventDestroy");
+    return ok();
+}
+
+int sw_event_record(void* event, void* stream) {
+    if (!event) return fail(SW_ERR_INVALID, "sw_event_record: null event");
+    SW_CUDA_TRY(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream), "cudaEventRecord");
+    return ok();
+}
+
+int sw_stream_wait_event(void* stream, void* event) {
+    if (!event) return fail(SW_ERR_INVALID, "sw_stream_wait_event: null event");
+    SW_CUDA_TRY(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0), "cudaStreamWaitEvent");
+    return ok();
+}
+
+int sw_event_elapsed_ms(void* start, void* end, float* ms) {
+    if (!start || !end || !ms) return fail(SW_ERR_INVALID, "sw_event_elapsed_ms: null argument");
+    SW_CUDA_TRY(cudaEventSynchronize((cudaEvent_t)end), "cudaEventSynchronize");
+    SW_CUDA_TRY(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end), "cudaEventElapsedTime");
+    return ok();
+}
+
 int sw_graph_capture_begin(void* stream) {
     if (!stream) return fail(SW_ERR_INVALID, "sw_graph_capture_begin: capture needs a stream from sw_stream_create");
     SW_CUDA_TRY(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal),

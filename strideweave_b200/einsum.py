@@ -248,11 +248,10 @@ def einsum(lhs: Any, rhs: Any, description: str, *, fmt: str | None = None) -> T
             p["j"] = next((s for s in rs if s not in shared), None)
             p["out_syms"] = os_
             if code is not None:
-                kq = 128 if code == N.SW_MX_E4M3 else 256
-                if not (p["i"] and p["j"] and p["M"] % 128 == 0 and p["N"] % 128 == 0 and p["K"] % kq == 0):
+                if not (p["i"] and p["j"] and p["M"] % 128 == 0 and p["N"] % 128 == 0 and p["K"] % 32 == 0):
                     raise NotImplementedError(
                         f"einsum with fmt={fmt!r} needs a free symbol on each side, free extents that are "
-                        f"multiples of 128 and a contracted extent that is a multiple of {kq}")
+                        f"multiples of 128 and a contracted extent that is a multiple of 32")
                 op = CudaMxBatchedContraction()
                 op.ctx["fmt"] = code
             else:

@@ -105,6 +105,24 @@ def mx_quantize(fmt: int, x_ptr: int, rows: int, cols: int, ld_row: int, ld_col:
                                  ld_payload, c_void_p(scales_ptr), scale_layout, ld_scales, c_void_p(stream)))
 
 
+def mx_quantize_view(fmt: int, x_ptr: int, x_size: int, offset: int, rows: Sequence[Leaf], cols: Sequence[Leaf],
+                     payload_ptr: int, ld_payload: int, scales_ptr: int, *, swizzle: Sequence[SwizzleStage] = (),
+                     scale_layout: int = N.SW_SCALES_TC128, ld_scales: int = 0, stream: int = 0) -> None:
+    """Quantise the view whose row mode has leaves ``rows`` and whose quantised
+    mode has leaves ``cols`` (first leaf fastest, flat indices through
+    ``swizzle``) into MX planes (see sw_mx_quantize_view)."""
+    plan = make_reduce_plan("reduce_sum", offset, rows, cols, swizzle)
+    N.check(N.lib.sw_mx_quantize_view(fmt, byref(plan), c_void_p(x_ptr), int(x_size), c_void_p(payload_ptr),
+                                      int(ld_payload), c_void_p(scales_ptr), scale_layout, int(ld_scales),
+                                      c_void_p(stream)))
+
+
+def mx_scales_to_tc128(src_ptr: int, ld_src: int, rows: int, kblocks: int, dst_ptr: int, *, stream: int = 0) -> None:
+    """Row-major scales -> the tensor-core atom placement (see sw_mx_scales_to_tc128)."""
+    N.check(N.lib.sw_mx_scales_to_tc128(c_void_p(src_ptr), int(ld_src), int(rows), int(kblocks), c_void_p(dst_ptr),
+                                        c_void_p(stream)))
+
+
 def mx_quantize_dual(fmt: int, transform: int, x_ptr: int, h_ptr: int, rows: int, cols: int, ld: int,
                      row_planes: tuple[int, int] | None, col_planes: tuple[int, int] | None, *,
                      scale_layout: int = N.SW_SCALES_TC128, stream: int = 0) -> None:

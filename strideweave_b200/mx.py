@@ -80,15 +80,39 @@ def _f32_operand(t: Any, name: str) -> tuple[int, int, int, int, int]:
     return t.carrier.data_ptr + 4 * t.offset, r[0], c[0], r[1], c[1]
 
 
+def _f32_view(t: Any, name: str) -> tuple[Any, list[tuple[int, int]], list[tuple[int, int]], list]:
+    """(carrier, row leaves, column leaves, swizzle stages) of a two-mode
+    Float32 CUDA tensor, leaves first-fastest with unit leaves dropped."""
+    from .carrier import CUDA
+    from .layout_plan import coalesce
+
+    if not isinstance(t, Tensor):
+        raise TypeError(f"{name} must be a Tensor")
+    t._require_single_subtensor("MX quantisation")
+    if not isinstance(t.carrier, CUDA) or t.carrier.dtype() is not DType.Float32:
+        raise TypeError(f"{name} must be a Float32 tensor on a CUDA carrier")
+    if len(t.layout) != 2:
+        raise ValueError(f"{name} must have a two-mode layout")
+    rows = coalesce(mode_leaves(t.layout, 0)) or [(1, 0)]
+    cols = coalesce(mode_leaves(t.layout, 1)) or [(1, 0)]
+    if len(rows) > N.SW_MAX_LEAVES or len(cols) > N.SW_MAX_LEAVES:
+        raise NotImplementedError(f"{name}: more than {N.SW_MAX_LEAVES} leaves in one mode")
+    return t.carrier, rows, cols, swizzle_stages(t.carrier)
+
+
 def quantize(t: Tensor, fmt: str = "MXFP8_E4M3") -> Tensor:
     """Quantise a Float32 CUDA tensor [rows, K] into an MX tensor, blocks of 32
-    along mode 1 (the mode a contraction sums over)."""
+    along mode 1 (the mode a contraction sums over).  Any layout: modes that
+    walk memory with one stride each take the strided kernels; hierarchical
+    (tiled) modes and swizzled carriers are quantised where they lie through
+    the view kernel, the same planes bit for bit."""
     from .carrier import CUDA
 
     if fmt not in FORMATS:
         raise NotImplementedError(f"no MX kernel for format {fmt!r}")
     mx_dtype, elem_dtype, code = FORMATS[fmt]
-    ptr, rows, K, ldr, ldc = _f32_operand(t, "tensor")
+    carrier, row_leaves, col_leaves, swz = _f32_view(t, "tensor")
+    rows, K = mode_size(t.layout, 0), mode_size(t.layout, 1)
     if K % 32 != 0:
         raise ValueError("MX quantisation needs the blocked mode to be a multiple of 32")
     kblocks = K // 32
@@ -96,9 +120,15 @@ def quantize(t: Tensor, fmt: str = "MXFP8_E4M3") -> Tensor:
     payload = CUDA(rows * K, dtype=elem_dtype, empty=True, device=t.carrier.device)
     scale_size = kernels.scale_bytes_tc128(rows, kblocks) if tc else rows * kblocks
     scales = CUDA(scale_size, dtype=DType.E8M0, empty=True, device=t.carrier.device)
-    kernels.mx_quantize(code, ptr, rows, K, ldr, ldc, payload.data_ptr, kernels.mx_row_bytes(code, K),
-                        scales.data_ptr, scale_layout=N.SW_SCALES_TC128 if tc else N.SW_SCALES_ROWMAJOR,
-                        ld_scales=0 if tc else kblocks)
+    placement = dict(scale_layout=N.SW_SCALES_TC128 if tc else N.SW_SCALES_ROWMAJOR, ld_scales=0 if tc else kblocks)
+    r1, c1 = single_stride(row_leaves), single_stride(col_leaves)
+    if not swz and r1 is not None and c1 is not None:
+        kernels.mx_quantize(code, carrier.data_ptr + 4 * t.offset, rows, K, r1[1], c1[1], payload.data_ptr,
+                            kernels.mx_row_bytes(code, K), scales.data_ptr, **placement)
+    else:
+        kernels.mx_quantize_view(code, carrier.data_ptr, carrier.size(), t.offset, row_leaves, col_leaves,
+                                 payload.data_ptr, kernels.mx_row_bytes(code, K), scales.data_ptr, swizzle=swz,
+                                 **placement)
     rep = TensorRepresentation(
         mx_dtype,
         (Subtensor(elem_dtype, payload, 0, payload_layout(rows, K)),
@@ -210,6 +240,20 @@ class MXPlanes:
         return self.scales.carrier.data_ptr + self.scales.offset
 
 
+def _scale_atoms(pl: MXPlanes, dev: int) -> Any:
+    """A row-major scale plane rewritten into the tensor-core atom placement,
+    as a fresh CUDA carrier (released in stream order after its last use)."""
+    from .carrier import CUDA
+
+    tmp = CUDA(kernels.scale_bytes_tc128(pl.rows, pl.kblocks), dtype=DType.E8M0, empty=True, device=dev)
+    kernels.mx_scales_to_tc128(pl.scales_ptr, pl.kblocks, pl.rows, pl.kblocks, tmp.data_ptr)
+    return tmp
+
+
+def _scales_ptr(source: Any) -> int:
+    return source.scales_ptr if isinstance(source, MXPlanes) else source.data_ptr
+
+
 def dequantize(mx: Tensor) -> Tensor:
     """Exact Float32 image of an MX tensor, [rows, K] row-major."""
     from .carrier import CUDA
@@ -253,15 +297,18 @@ class MxMatmul(Operation):
         out_dtype = DType.Float32 if out_dtype is None else out_dtype
         if out_dtype is not DType.Float32 and out_dtype is not BFloat16:
             raise NotImplementedError("MX contraction produces Float32 or BFloat16")
-        if not (pa.tc128 and pb.tc128):
-            raise NotImplementedError("the tensor-core contraction needs rows % 128 == 0 and K % 128 == 0 "
-                                      "(scale planes in the tensor-core atom placement)")
         M, Nn, K = pa.rows, pb.rows, pa.K
         layout = canonical_layout(a.layout.shape.top_level[0], b.layout.shape.top_level[0])
         self.ctx["output_layout"] = layout
-        out = CUDA(M * Nn, dtype=out_dtype, empty=True, device=pa.payload.carrier.device)
-        kernels.mx_gemm(pa.code, pa.payload_ptr, pa.ld_bytes, pa.scales_ptr, pb.payload_ptr, pb.ld_bytes,
-                        pb.scales_ptr, out.data_ptr, M, Nn, K, out_bf16=out_dtype is BFloat16, ldc_m=1, ldc_n=M)
+        dev = pa.payload.carrier.device
+        out = CUDA(M * Nn, dtype=out_dtype, empty=True, device=dev)
+        # Planes whose rows or blocks are not whole 128 x 4 atoms keep row-major
+        # scales; the kernel reads the atom placement, so those are rewritten
+        # into it first (1/32 of the payload bytes; released in stream order).
+        atoms = [pl if pl.tc128 else _scale_atoms(pl, dev) for pl in (pa, pb)]
+        kernels.mx_gemm(pa.code, pa.payload_ptr, pa.ld_bytes, _scales_ptr(atoms[0]), pb.payload_ptr, pb.ld_bytes,
+                        _scales_ptr(atoms[1]), out.data_ptr, M, Nn, K, out_bf16=out_dtype is BFloat16, ldc_m=1,
+                        ldc_n=M)
         return Tensor(out, 0, layout)
 
     def backward(self, gradient: Any) -> tuple[Any, ...]:
@@ -291,10 +338,11 @@ def linear_forward(x: Tensor, w: Tensor, fmt: str) -> Tensor:
     wp, OUT, IN2, wr, wc = _f32_operand(w, "weight")
     if IN != IN2:
         raise ValueError("Matmul inner dimensions must match")
-    q = 256 if code == N.SW_MX_E2M1 else 128
+    # each extent is the contracted (blocked) one of some contraction of the
+    # forward or the backward: whole 32-element MX blocks
     for name, n in (("batch", B), ("out", OUT), ("in", IN)):
-        if n % q != 0:
-            raise NotImplementedError(f"mx_linear needs {name} extent {n} to be a multiple of {q}")
+        if n % 32 != 0:
+            raise NotImplementedError(f"mx_linear needs {name} extent {n} to be a multiple of 32")
     dev = x.carrier.device
     qx = _quantize_view(xp, B, IN, xr, xc, code, dev)
     qw = _quantize_view(wp, OUT, IN, wr, wc, code, dev)

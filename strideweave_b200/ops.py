@@ -16,6 +16,7 @@ from __future__ import annotations
 
 from typing import Any
 
+from . import _native as N
 from . import kernels
 from ._host import (
     DType,
@@ -229,29 +230,40 @@ class CudaMatmul(CudaOperation):
 # ---- elementwise product (the union step of batched einsum) ------------------------
 
 
-def _binary_mul(a: Tensor, b: Tensor, out: Tensor) -> None:
-    """out = a * b elementwise over three views sharing one shape tree."""
+def _map(op: int, a: Tensor, b: Tensor | None, out: Tensor, scalar: float = 0.0, name: str = "elementwise") -> None:
+    """out = a (op) b, or (op)(a, scalar), elementwise over views sharing one
+    shape tree (sw_map_f32)."""
     import ctypes
 
     from . import _native as N
     from .layout_plan import all_leaves
 
-    for t, name in ((a, "lhs"), (b, "rhs"), (out, "output")):
+    views = [(a, "lhs"), (out, "output")] + ([(b, "rhs")] if b is not None else [])
+    for t, role in views:
         if t.carrier.swizzle is not None:
-            raise NotImplementedError(f"{name}: swizzled carriers are not supported by elementwise_mul")
-    la, lb, lo = all_leaves(a.layout), all_leaves(b.layout), all_leaves(out.layout)
+            raise NotImplementedError(f"{role}: swizzled carriers are not supported by {name}")
+    la, lo = all_leaves(a.layout), all_leaves(out.layout)
+    lb = all_leaves(b.layout) if b is not None else la
     if not (len(la) == len(lb) == len(lo)) or any(x[0] != y[0] or x[0] != z[0] for x, y, z in zip(la, lb, lo)):
-        raise ValueError("elementwise_mul operands must share one shape tree")
+        raise ValueError(f"{name} operands must share one shape tree")
     keep = [i for i, (e, _) in enumerate(lo) if e != 1]
     rank = len(keep)
     arr = ctypes.c_int64 * max(rank, 1)
     shape = arr(*[lo[i][0] for i in keep])
     sa, sb, so = (arr(*[leaves[i][1] for i in keep]) for leaves in (la, lb, lo))
-    N.check(N.lib.sw_binary_f32(
-        N.SW_BIN_MUL, rank, shape,
+    bt = b if b is not None else a
+    N.check(N.lib.sw_map_f32(
+        op, rank, shape,
         N.c_void_p(a.carrier.data_ptr), a.offset, sa, a.carrier.size(),
-        N.c_void_p(b.carrier.data_ptr), b.offset, sb, b.carrier.size(),
-        N.c_void_p(out.carrier.data_ptr), out.offset, so, out.carrier.size(), None))
+        N.c_void_p(bt.carrier.data_ptr), bt.offset, sb, bt.carrier.size(),
+        N.c_void_p(out.carrier.data_ptr), out.offset, so, out.carrier.size(), float(scalar), None))
+
+
+def _binary_mul(a: Tensor, b: Tensor, out: Tensor) -> None:
+    """out = a * b elementwise over three views sharing one shape tree."""
+    from . import _native as N
+
+    _map(N.SW_MAP_MUL, a, b, out, name="elementwise_mul")
 
 
 class CudaElementwiseMul(CudaOperation):
@@ -296,6 +308,174 @@ class CudaElementwiseMul(CudaOperation):
         return (dl, dr)
 
 
+# ---- the elementwise arithmetic of the reference's nn modules ---------------------
+#
+# A Linear's bias add, an MSE loss's difference, square and mean scale
+# (src/strideweave/nn/modules.py:40-176, friendly/ops.py:52) and their
+# gradients, so the reference's own modules train on CUDA-carrier tensors.
+
+
+def _copy(src: Tensor, dst: Tensor) -> None:
+    """dst = src value for value (NaN payloads kept) over one shape tree."""
+    from . import kernels
+    from .layout_plan import all_leaves
+
+    ls, ld = all_leaves(src.layout), all_leaves(dst.layout)
+    if len(ls) > N.SW_MAX_LEAVES:
+        raise NotImplementedError(f"more than {N.SW_MAX_LEAVES} leaves")
+    kernels.copy_view_f32(src.carrier.data_ptr, src.carrier.size(), src.offset, ls or [(1, 0)], [(1, 0)],
+                          dst.carrier.data_ptr, dst.carrier.size(), dst.offset, ld or [(1, 0)], [(1, 0)],
+                          swizzle=swizzle_stages(src.carrier))
+
+
+def _gradient_like(t: Tensor, gradient: Any) -> tuple[Tensor, Tensor]:
+    gradient = _cuda_tensor(gradient, "gradient")
+    if gradient.layout.shape != t.layout.shape:
+        raise ValueError("Tensor shapes must match")
+    return gradient, _new_result(t, injective_layout_for(t.layout), DType.Float32)
+
+
+class _CudaBinaryArithmetic(CudaOperation):
+    """Tensor (op) tensor, as the reference's cpu_binary_elementwise_forward
+    (src/strideweave/carriers/cpu/native/_cpu_binary.hpp:85-130): operands
+    aligned by ``_align_binary_operands`` (differentiable broadcast views),
+    the canonical layout of the common shape, one binary32 operation per
+    element."""
+
+    _name = ""
+    _op = -1
+
+    def _forward(self, lhs: Any, rhs: Any) -> Tensor:
+        from strideweave.carriers.operation_helpers import _align_binary_operands
+
+        lhs = _cuda_tensor(lhs, "lhs")
+        rhs = _cuda_tensor(rhs, "rhs")
+        if type(lhs.carrier) is not type(rhs.carrier):
+            raise TypeError("Tensor backing carriers must match")
+        lhs, rhs, result_layout = _align_binary_operands(lhs, rhs)
+        if len(self.inputs()) != 0:
+            self.store_inputs(lhs, rhs)  # the gradient flows through the broadcast views
+        plan = resolve_operation_plan(self._name, lhs.carrier.dtype(), rhs.carrier.dtype(),
+                                      options=self._execution_options)
+        require_capability(self._carrier_class(), plan)
+        result = _new_result(lhs, result_layout, DType.Float32)
+        _map(self._op, lhs, rhs, result, name=self._name)
+        return result
+
+
+class CudaAdd(_CudaBinaryArithmetic):
+    """lhs + rhs (CpuAddOperation, ops/add.cpp); both gradients are g."""
+
+    _name, _op = "add", N.SW_MAP_ADD
+
+    def backward(self, gradient: Any) -> tuple[Any, Any]:
+        lhs, rhs = self.inputs()
+        g, dl = _gradient_like(lhs, gradient)
+        _, dr = _gradient_like(rhs, gradient)
+        _copy(g, dl)
+        _copy(g, dr)
+        return (dl, dr)
+
+
+class CudaSub(_CudaBinaryArithmetic):
+    """lhs - rhs (CpuSubOperation, ops/sub.cpp:8-24); gradients g and -g."""
+
+    _name, _op = "sub", N.SW_MAP_SUB
+
+    def backward(self, gradient: Any) -> tuple[Any, Any]:
+        lhs, rhs = self.inputs()
+        g, dl = _gradient_like(lhs, gradient)
+        _, dr = _gradient_like(rhs, gradient)
+        _copy(g, dl)
+        _map(N.SW_MAP_SCALE, g, None, dr, -1.0, name="sub")
+        return (dl, dr)
+
+
+class CudaMul(CudaOperation):
+    """mul: a tensor times a weak scalar (CpuScalarMulOperation,
+    ops/scalar_mul.cpp), result and gradient g * scalar in the injective
+    canonical layout of the tensor; tensor times tensor as elementwise_mul."""
+
+    def _forward(self, tensor: Any, other: Any) -> Tensor:
+        if isinstance(other, Tensor):
+            self.ctx["tensor_rhs"] = True
+            from strideweave.carriers.operation_helpers import _align_binary_operands
+
+            lhs, rhs = _cuda_tensor(tensor, "lhs"), _cuda_tensor(other, "rhs")
+            lhs, rhs, result_layout = _align_binary_operands(lhs, rhs)
+            if len(self.inputs()) != 0:
+                self.store_inputs(lhs, rhs)
+            require_capability(self._carrier_class(), resolve_operation_plan(
+                "mul", lhs.carrier.dtype(), rhs.carrier.dtype(), options=self._execution_options))
+            result = _new_result(lhs, result_layout, DType.Float32)
+            _map(N.SW_MAP_MUL, lhs, rhs, result, name="mul")
+            return result
+        tensor = _cuda_tensor(tensor, "tensor")
+        require_capability(self._carrier_class(), resolve_operation_plan(
+            "mul", tensor.carrier.dtype(), other, options=self._execution_options))
+        scalar = float(other)
+        self.ctx["scalar"] = scalar
+        result = _new_result(tensor, injective_layout_for(tensor.layout), DType.Float32)
+        _map(N.SW_MAP_SCALE, tensor, None, result, scalar, name="mul")
+        return result
+
+    def backward(self, gradient: Any) -> tuple[Any, ...]:
+        inputs = self.inputs()
+        if self.ctx.get("tensor_rhs"):
+            lhs, rhs = inputs
+            g, dl = _gradient_like(lhs, gradient)
+            _, dr = _gradient_like(rhs, gradient)
+            _map(N.SW_MAP_MUL, g, rhs, dl, name="mul")
+            _map(N.SW_MAP_MUL, g, lhs, dr, name="mul")
+            return (dl, dr)
+        (tensor,) = inputs[:1]
+        g, dt = _gradient_like(tensor, gradient)
+        _map(N.SW_MAP_SCALE, g, None, dt, self.ctx["scalar"], name="mul")
+        return (dt,)
+
+
+class CudaPow(CudaOperation):
+    """A tensor raised to a weak-scalar exponent (CpuPowOperation,
+    ops/pow.cpp:66-101 forward, :160-175 gradient g * p * x^(p - 1)), in the
+    injective canonical layout of the tensor."""
+
+    def _forward(self, tensor: Any, exponent: Any) -> Tensor:
+        if isinstance(exponent, Tensor):
+            raise NotImplementedError("CUDA pow takes a scalar exponent")
+        tensor = _cuda_tensor(tensor, "tensor")
+        require_capability(self._carrier_class(), resolve_operation_plan(
+            "pow", tensor.carrier.dtype(), exponent, options=self._execution_options))
+        p = float(exponent)
+        self.ctx["exponent"] = p
+        result = _new_result(tensor, injective_layout_for(tensor.layout), DType.Float32)
+        _map(N.SW_MAP_POW, tensor, None, result, p, name="pow")
+        return result
+
+    def backward(self, gradient: Any) -> tuple[Any]:
+        (tensor,) = self.inputs()[:1]
+        g, dt = _gradient_like(tensor, gradient)
+        _map(N.SW_MAP_POW_GRAD, g, tensor, dt, self.ctx["exponent"], name="pow")
+        return (dt,)
+
+
+class CudaNeg(CudaOperation):
+    """-tensor (ops/neg.cpp); gradient -g."""
+
+    def _forward(self, tensor: Any) -> Tensor:
+        tensor = _cuda_tensor(tensor, "tensor")
+        require_capability(self._carrier_class(), resolve_operation_plan(
+            "neg", tensor.carrier.dtype(), options=self._execution_options))
+        result = _new_result(tensor, injective_layout_for(tensor.layout), DType.Float32)
+        _map(N.SW_MAP_SCALE, tensor, None, result, -1.0, name="neg")
+        return result
+
+    def backward(self, gradient: Any) -> tuple[Any]:
+        (tensor,) = self.inputs()[:1]
+        g, dt = _gradient_like(tensor, gradient)
+        _map(N.SW_MAP_SCALE, g, None, dt, -1.0, name="neg")
+        return (dt,)
+
+
 # ---- dispatch table ----------------------------------------------------------------
 
 
@@ -322,6 +502,11 @@ _OPS = {
     "argmax": CudaArgmax,
     "matmul": CudaMatmul,
     "elementwise_mul": CudaElementwiseMul,
+    "add": CudaAdd,
+    "sub": CudaSub,
+    "mul": CudaMul,
+    "pow": CudaPow,
+    "neg": CudaNeg,
 }
 
 
@@ -354,8 +539,15 @@ def declared_plans() -> list[Any]:
         resolve_operation_plan("matmul", f32, f32, accumulator_dtype=DType.Float64),
         resolve_operation_plan("gelu", f32),
         resolve_operation_plan("elementwise_mul", f32, f32),
+        resolve_operation_plan("add", f32, f32),
+        resolve_operation_plan("sub", f32, f32),
+        resolve_operation_plan("mul", f32, f32),
+        resolve_operation_plan("mul", f32, 1.0),
+        resolve_operation_plan("pow", f32, 2.0),
+        resolve_operation_plan("neg", f32),
     ]
 
 
-__all__ = ["CudaArgmax", "CudaElementwiseMul", "CudaMatmul", "CudaReduceMax", "CudaReduceSum", "UnsupportedOperationPlan",
-           "declared_plans", "make_operation"]
+__all__ = ["CudaAdd", "CudaArgmax", "CudaElementwiseMul", "CudaMatmul", "CudaMul", "CudaNeg", "CudaPow",
+           "CudaReduceMax", "CudaReduceSum", "CudaSub", "UnsupportedOperationPlan", "declared_plans",
+           "make_operation"]

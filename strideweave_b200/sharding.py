@@ -23,8 +23,9 @@ Two partitions of C[M, N] = A[M, K] . B[N, K]^T:
 
 The schedule is written once, against three callables: a chunk contraction,
 a reduce-scatter and an allocator. On GPUs these are the tcgen05 MX GEMM and
-NCCL (through `torch.distributed`). The CPU tests run the same schedule with
-numpy and `gloo`.
+NCCL, both through the C ABI (no torch on the data path: carrier storage,
+streams and events are the library's own). The CPU tests run the same
+schedule with numpy and `gloo`.
 
 The reference has no distributed code: it runs every operation on one host
 carrier.  This module shards large contractions across the GPUs of a node by
@@ -184,98 +185,125 @@ class NcclCommunicator:
 # ---- the GPU implementation ---------------------------------------------------------
 
 
+def _address(buf: Any) -> int:
+    """Device address of a buffer handle: a CUDA carrier, a DeviceBuffer or an int."""
+    if isinstance(buf, int):
+        return buf
+    if hasattr(buf, "data_ptr"):
+        ptr = buf.data_ptr
+        return ptr() if callable(ptr) else int(ptr)
+    return int(buf.ptr)
+
+
 class MXShardedContraction:
-    """Sharded MX contraction on this rank's GPU: tcgen05 MX GEMM for the local
-    products, NCCL (torch.distributed, backend "nccl") for the reduce-scatter.
+    """Sharded MX contraction on this rank's GPU, driven entirely through the
+    C ABI: the tcgen05 MX GEMM for the local products and, for a K-split over
+    several ranks, the C-ABI NCCL communicator for the reduce-scatter.
 
     `a_planes` / `b_planes` are this rank's operand shards as (payload, scales)
-    device buffers in the tensor-core placement: A rows [rows, k_local]
-    (M-split: rows = M/g; K-split: rows = M) and B [N, k_local].
+    device buffers (CUDA carriers, DeviceBuffers or addresses) in the
+    tensor-core placement: A rows [rows, k_local] (M-split: rows = M/g;
+    K-split: rows = M) and B [N, k_local].
+
+    The result lives on a CUDA carrier of this device: the rank's C rows
+    [M/g, N] in Float32, row-major for an M-split and chunk-major
+    (M/g, (Nc, chunks)) : (Nc, (1, M/g * Nc)) for a K-split, so each chunk's
+    reduce-scatter writes one contiguous block.  `run()` enqueues a step on
+    `stream` (default: the legacy default stream, where every carrier
+    operation is ordered) and returns that Tensor; the buffers are reused by
+    every step.
     """
 
     def __init__(self, plan: ShardPlan, fmt: int, a_planes: tuple[Any, Any], b_planes: tuple[Any, Any],
-                 group: Any = None, comm: NcclCommunicator | None = None) -> None:
-        import torch
-
+                 comm: NcclCommunicator | None = None, stream: int = 0) -> None:
         from . import _native as N
         from . import kernels
+        from ._host import DType, Layout, Shape, Stride, Tensor
+        from .carrier import CUDA
 
-        self.plan = plan
-        self.fmt = fmt
-        self.N = N
-        self.kernels = kernels
-        self.torch = torch
-        self.group = group
-        self.comm = comm  # reduce-scatter through the C ABI instead of torch.distributed
-        self.a_pay, self.a_sc = a_planes
-        self.b_pay, self.b_sc = b_planes
+        if plan.mode == "k" and plan.world > 1 and comm is None:
+            raise ValueError("a K-split over several ranks needs an NcclCommunicator for its reduce-scatter")
+        if comm is not None and (comm.world != plan.world or comm.rank != plan.rank):
+            raise ValueError("the communicator's world and rank must match the plan's")
+        self.plan, self.fmt, self.comm, self.stream = plan, fmt, comm, int(stream or 0)
+        self.N, self.kernels = N, kernels
+        self.a_pay, self.a_sc = (_address(x) for x in a_planes)
+        self.b_pay, self.b_sc = (_address(x) for x in b_planes)
         self.row_bytes = kernels.mx_row_bytes(fmt, plan.k_local)
         self.katoms = (plan.k_local // 32 + 3) // 4
-        dev = torch.device("cuda", torch.cuda.current_device())
-        rows = plan.rows_local if plan.mode == "m" else plan.M
-        if plan.mode == "m":
-            self.out = torch.empty(plan.rows_local * plan.N, dtype=torch.float32, device=dev)
-        else:
-            nbuf = min(2, plan.chunks)  # double-buffered partials
-            self.partials = [torch.empty(rows * plan.chunk_cols, dtype=torch.float32, device=dev)
-                             for _ in range(nbuf)]
-            self.outs = [torch.empty(plan.rows_local * plan.chunk_cols, dtype=torch.float32, device=dev)
-                         for _ in range(plan.chunks)]
-            self.comm_stream = torch.cuda.Stream(device=dev)
-            self.done = [torch.cuda.Event() for _ in range(plan.chunks)]
-            self.freed = [torch.cuda.Event() for _ in range(plan.chunks)]
-
-    def _contract(self, chunk: int, out: Any, ldc: int) -> None:
-        plan = self.plan
-        s = self.torch.cuda.current_stream().cuda_stream
-        rows = plan.rows_local if plan.mode == "m" else plan.M
-        if chunk < 0:
-            n0, ncols = 0, plan.N
-        else:
-            n0, ncols = chunk * plan.chunk_cols, plan.chunk_cols
-        b_ptr = self.b_pay.ptr + n0 * self.row_bytes
-        b_sc = self.b_sc.ptr + (n0 // 128) * self.katoms * 512
-        # a K-split's reduce-scatter of the previous chunk runs beside this
-        # contraction: leave it some SMs (the persistent GEMM fills every SM)
-        max_ctas = 0
+        dev = N.current_device()
+        mg = plan.rows_local
+        self.out = CUDA(mg * plan.N, dtype=DType.Float32, empty=True, device=dev)
+        shape, stride = plan.result_layout_tree()
+        self.result = Tensor(self.out, 0, Layout(Shape(shape), Stride(stride)))
+        # a K-split's reduce-scatter of one chunk runs beside the next chunk's
+        # contraction: the persistent GEMM then leaves comm_sms SMs free
+        self.max_ctas = 0
         if plan.mode == "k" and plan.world > 1 and plan.chunks > 1 and plan.comm_sms > 0:
-            sms = self.torch.cuda.get_device_properties(self.torch.cuda.current_device()).multi_processor_count
-            max_ctas = max(1, sms - plan.comm_sms)
-        self.kernels.mx_gemm(self.fmt, self.a_pay.ptr, self.row_bytes, self.a_sc.ptr, b_ptr, self.row_bytes, b_sc,
-                             out.data_ptr(), rows, ncols, plan.k_local, ldc_m=ldc, ldc_n=1, max_ctas=max_ctas,
-                             stream=s)
+            self.max_ctas = max(1, N.sm_count() - plan.comm_sms)
+        if plan.mode == "k":
+            nbuf = min(2, plan.chunks)  # double-buffered partials [M, Nc]
+            self.partials = [CUDA(plan.M * plan.chunk_cols, dtype=DType.Float32, empty=True, device=dev)
+                             for _ in range(nbuf)]
+            self.comm_stream = N.Stream()
+            self.done = [N.Event() for _ in range(plan.chunks)]
+            self.freed = [N.Event() for _ in range(plan.chunks)]
+            self.all_done = N.Event()
+        # the carriers come from the pool in the legacy default stream's order;
+        # the other streams may use them only once that point has passed
+        N.synchronize()
+
+    def _contract(self, chunk: int, out_ptr: int, ldc: int) -> None:
+        plan = self.plan
+        rows = plan.rows_local if plan.mode == "m" else plan.M
+        n0, ncols = (0, plan.N) if chunk < 0 else (chunk * plan.chunk_cols, plan.chunk_cols)
+        b_ptr = self.b_pay + n0 * self.row_bytes
+        b_sc = self.b_sc + (n0 // 128) * self.katoms * 512
+        self.kernels.mx_gemm(self.fmt, self.a_pay, self.row_bytes, self.a_sc, b_ptr, self.row_bytes, b_sc, out_ptr,
+                             rows, ncols, plan.k_local, ldc_m=ldc, ldc_n=1, max_ctas=self.max_ctas,
+                             stream=self.stream)
+
+    def _chunk_out(self, c: int) -> int:
+        plan = self.plan
+        return self.out.data_ptr + 4 * c * plan.rows_local * plan.chunk_cols
 
     def run(self) -> Any:
-        plan = self.plan
-        torch = self.torch
+        plan, N = self.plan, self.N
         if plan.mode == "m":
-            return run_msplit(plan, self._contract, self.out)
-        import torch.distributed as dist
-
-        compute = torch.cuda.current_stream()
-
-        def before_comm(c: int) -> None:
-            self.done[c].record(compute)
-            self.comm_stream.wait_event(self.done[c])
-
-        def reduce_scatter(out: Any, part: Any, c: int) -> None:
-            with torch.cuda.stream(self.comm_stream):
-                if self.comm is not None:
-                    self.comm.reduce_scatter_f32(out.data_ptr(), part.data_ptr(), out.numel(),
-                                                 self.comm_stream.cuda_stream)
-                elif plan.world == 1:
-                    out.copy_(part)
-                else:
-                    dist.reduce_scatter_tensor(out, part, op=dist.ReduceOp.SUM, group=self.group)
-                self.freed[c].record(self.comm_stream)
+            run_msplit(plan, self._contract, self.out.data_ptr)
+            return self.result
+        comm_stream = self.comm_stream.handle
+        nbuf = len(self.partials)
 
         def contract(c: int, part: Any, ldc: int) -> None:
-            if c >= len(self.partials):  # the buffer is reused: wait until its scatter finished
-                compute.wait_event(self.freed[c - len(self.partials)])
-            self._contract(c, part, ldc)
+            if c >= nbuf:  # the buffer is reused: its previous chunk's collective must have read it
+                self.freed[c - nbuf].wait(self.stream)
+            self._contract(c, part.data_ptr, ldc)
+
+        def before_comm(c: int) -> None:
+            self.done[c].record(self.stream)
+            self.done[c].wait(comm_stream)
+
+        def reduce_scatter(out_ptr: int, part: Any, c: int) -> None:
+            count = plan.rows_local * plan.chunk_cols
+            if self.comm is not None:
+                self.comm.reduce_scatter_f32(out_ptr, part.data_ptr, count, comm_stream)
+            else:  # one rank: its partial is the sum
+                N.check(N.lib.sw_memcpy_d2d(N.c_void_p(out_ptr), N.c_void_p(part.data_ptr), 4 * count,
+                                            N.c_void_p(comm_stream)))
+            self.freed[c].record(comm_stream)
 
         def after_all() -> None:
-            compute.wait_stream(self.comm_stream)
+            self.all_done.record(comm_stream)
+            self.all_done.wait(self.stream)
 
-        return run_ksplit(plan, contract, reduce_scatter, self.partials, self.outs, before_comm=before_comm,
-                          after_all=after_all)
+        outs = [self._chunk_out(c) for c in range(plan.chunks)]
+        run_ksplit(plan, contract, reduce_scatter, self.partials, outs, before_comm=before_comm, after_all=after_all)
+        return self.result
+
+    def close(self) -> None:
+        """Release the streams and events now (the carriers free themselves)."""
+        if self.plan.mode == "k":
+            for e in (*self.done, *self.freed, self.all_done):
+                e.close()
+            self.comm_stream.close()

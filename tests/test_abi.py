@@ -64,8 +64,10 @@ def test_scale_placement_matches_the_oracle(native):
 def test_invalid_arguments_are_rejected_before_any_device_work(native):
     from strideweave_b200 import kernels
 
-    with pytest.raises(NotImplementedError, match="M % 128"):
-        kernels.mx_gemm(1, 16, 1024, 16, 16, 1024, 16, 16, 100, 128, 1024)
+    with pytest.raises(NotImplementedError, match="K to be a positive multiple of 32"):
+        kernels.mx_gemm(1, 16, 1024, 16, 16, 1024, 16, 16, 100, 128, 1000)
+    with pytest.raises(NotImplementedError, match="needs M % 128 == 0 and N % 128 == 0"):
+        kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 2, 100, 128, 1024)
     with pytest.raises(NotImplementedError, match="mixed operand formats"):
         native.check(native.lib.sw_mx_gemm(1, 2, c_void_p(16), 1024, c_void_p(16), c_void_p(16), 1024,
                                            c_void_p(16), c_void_p(16), 0, 128, 1, 128, 128, 1024, 0, None))
@@ -78,11 +80,12 @@ def test_invalid_arguments_are_rejected_before_any_device_work(native):
     with pytest.raises(NotImplementedError, match="stacked extent too large"):
         kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 1 << 24, 1024, 256, 1024)
     kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 0, 128, 256, 1024)  # no problems: no work
-    # stacked results that overlap are refused (one problem spans 127 * 256 + 255 + 1 elements)
+    # stacked results that overlap are refused (a row-major problem spans 127 * 256 + 255 + 1 elements;
+    # the interleaved placement, batch stride 1 under pitches 2 and 256, is disjoint and runs on a GPU)
     for stride in (0, 1, 128 * 256 - 1):
-        with pytest.raises(ValueError, match="smaller than one problem's result span"):
+        with pytest.raises(ValueError, match="results of the stacked problems may overlap"):
             kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 2, 128, 256, 1024, batch_stride_c=stride)
-    with pytest.raises(ValueError, match="result span 32768"):  # column-major: (127) * 1 + 255 * 128 + 1
+    with pytest.raises(ValueError, match="may overlap"):  # column-major problems 100 elements apart
         kernels.mx_gemm_batched(1, 16, 1024, 16, 16, 1024, 16, 16, 2, 128, 256, 1024, ldc_m=1, ldc_n=128,
                                 batch_stride_c=100)
     # the NCCL wrappers check their arguments before they load NCCL
