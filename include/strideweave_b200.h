@@ -211,11 +211,15 @@ int sw_reduce_backward_f32(const sw_reduce_plan* plan, const float* x,
 
 /* Copies a two-mode Float32 view into another two-mode placement:
  * dst[dst.offset + kept_d(i) + reduced_d(j)] = src at (i, j) of `src_plan`
- * (through its swizzle), for every (i, j).  Both plans' leaves must have the
- * same mode sizes; `kind` fields are ignored.  This is how the carrier
+ * (each flat index through its own plan's swizzle), for every (i, j).  Both
+ * plans' leaves must have the same mode sizes; `kind` fields are ignored.
+ * Any 32-bit element copies bit for bit (Int32 views too).  This is how the carrier
  * materialises views no kernel walks directly (the reference's
  * _physical_values_for_layout / _detached_tensor_like,
- * src/strideweave/carriers/operation_helpers.py:194-245). */
+ * src/strideweave/carriers/operation_helpers.py:194-245), and how it scatters
+ * a tensor onto another through a mapping layout in one launch
+ * (CpuCarrier::scatter, src/strideweave/carriers/cpu/native/
+ * _cpu_carrier.hpp:521-540). */
 int sw_copy_view_f32(const sw_reduce_plan* src_plan, const float* src,
                      int64_t src_size, const sw_reduce_plan* dst_plan,
                      float* dst, int64_t dst_size, void* stream);

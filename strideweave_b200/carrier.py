@@ -34,6 +34,7 @@ import numpy as np
 
 from . import _native as N
 from ._host import BFloat16, Carrier, DType, Swizzle
+from .layout_plan import swizzle_map, swizzle_stages
 
 FLOAT32 = DType.Float32
 INT32 = DType.Int32
@@ -267,8 +268,37 @@ class CUDA(Carrier):
         offset = operator_index(mapping_offset)
         if offset < 0:
             raise ValueError("mapping_offset must be non-negative")
+        if self._scatter_on_device(to_scatter, scatter_onto.offset + offset, mapping):
+            return
         for logical in range(to_scatter.size()):
             self[scatter_onto.offset + offset + mapping.index(logical)] = to_scatter[logical]
+
+    def _scatter_on_device(self, to_scatter: Any, base: int, mapping: Any) -> bool:
+        """One view-copy launch: element i of to_scatter (its layout, through
+        its carrier's swizzle) lands at flat index base + mapping(i) of this
+        carrier (through this carrier's swizzle), as the reference's native
+        loop does element by element (src/strideweave/carriers/cpu/native/
+        _cpu_carrier.hpp:521-540).  32-bit dtypes on CUDA carriers of this
+        device; anything else returns False and takes the element loop."""
+        from . import kernels
+        from .layout_plan import all_leaves, coalesce, swizzle_stages
+
+        src = to_scatter.carrier
+        if (not isinstance(src, CUDA) or src.device != self._device or _BITS[self._dtype] != 32
+                or _BITS[src.dtype()] != 32 or src.dtype() is not self._dtype):
+            return False
+        src_leaves, dst_leaves = all_leaves(to_scatter.layout), all_leaves(mapping)
+        if len(src_leaves) > N.SW_MAX_LEAVES or len(dst_leaves) > N.SW_MAX_LEAVES:
+            src_leaves, dst_leaves = coalesce(src_leaves), coalesce(dst_leaves)
+            if len(src_leaves) > N.SW_MAX_LEAVES or len(dst_leaves) > N.SW_MAX_LEAVES:
+                return False
+        if to_scatter.size() == 0:
+            return True
+        kernels.copy_view_f32(src.data_ptr, src.size(), to_scatter.offset, src_leaves or [(1, 0)], [(1, 0)],
+                              self.data_ptr, self._size, base, dst_leaves or [(1, 0)], [(1, 0)],
+                              swizzle=swizzle_stages(src), dst_swizzle=swizzle_stages(self))
+        self._increment_version()
+        return True
 
     def dlpack_info(self) -> dict:
         if self._dtype not in (FLOAT32, INT32):
@@ -346,10 +376,21 @@ class CUDA(Carrier):
         """The flat index space as a host array in logical order (decoded for
         narrow float dtypes; E8M0 as scale values)."""
         N.synchronize()
+        d = self._dtype
+        if self._swizzle is not None and _BITS[d] == 32 and self._size:
+            # un-swizzle on the device (one view copy), then one download
+            from . import kernels
+
+            staged = N.DeviceBuffer(self._nbytes)
+            kernels.copy_view_f32(self.data_ptr, self._size, 0, [(self._size, 1)], [(1, 0)], staged.ptr, self._size,
+                                  0, [(self._size, 1)], [(1, 0)], swizzle=swizzle_stages(self))
+            out = np.empty(self._size, dtype=_NUMPY[d])
+            staged.download(out)
+            staged.free()
+            return out
         raw = np.empty(self._nbytes, dtype=np.uint8)
         if self._nbytes:
             self._buffer.download(raw)
-        d = self._dtype
         if d is E2M1:
             codes = np.empty(self._nbytes * 2, dtype=np.uint8)
             codes[0::2] = raw & 0xF
@@ -358,8 +399,7 @@ class CUDA(Carrier):
         else:
             phys = raw.view(_NUMPY[d])[: self._size]
         if self._swizzle is not None:
-            idx = np.fromiter((self._swizzle(i) for i in range(self._size)), dtype=np.int64, count=self._size)
-            phys = phys[idx]
+            phys = phys[swizzle_map(swizzle_stages(self), self._size)]
         if d is FLOAT32 or d is INT32:
             return phys.copy()
         if d is BOOL:
@@ -398,9 +438,8 @@ class CUDA(Carrier):
         if swizzle is not None:
             if dtype is E2M1:
                 raise NotImplementedError("swizzled E2M1 storage")
-            idx = np.fromiter((swizzle(i) for i in range(arr.size)), dtype=np.int64, count=arr.size)
             phys = np.empty_like(host)
-            phys[idx] = host
+            phys[swizzle_map([(int(s.bits), int(s.base), int(s.shift)) for s in swizzle.stages], arr.size)] = host
             host = phys
         if host.nbytes:
             out._buffer.upload(np.ascontiguousarray(host))

@@ -32,7 +32,19 @@ struct GradPlan {
     Leaves xk, xr, gk, gr;
     int swz_rank;
     int swz_bits[SW_MAX_SWIZZLE], swz_base[SW_MAX_SWIZZLE], swz_shift[SW_MAX_SWIZZLE];
+    int dswz_rank;  // the destination's carrier swizzle (view copies only)
+    int dswz_bits[SW_MAX_SWIZZLE], dswz_base[SW_MAX_SWIZZLE], dswz_shift[SW_MAX_SWIZZLE];
 };
+
+__device__ __forceinline__ int64_t swizzle_stages(int rank, const int* bits, const int* base, const int* shift,
+                                                  int64_t r) {
+    for (int s = 0; s < rank; ++s) {
+        const int64_t mask = (int64_t(1) << bits[s]) - 1;
+        if (shift[s] > 0) r ^= ((r >> (base[s] + shift[s])) & mask) << base[s];
+        else r ^= ((r >> base[s]) & mask) << (base[s] - shift[s]);
+    }
+    return r;
+}
 
 __device__ __forceinline__ int64_t decompose(const Leaves& l, int64_t i) {
     int64_t off = 0;
@@ -44,12 +56,7 @@ __device__ __forceinline__ int64_t decompose(const Leaves& l, int64_t i) {
 }
 
 __device__ __forceinline__ int64_t swz(const GradPlan& p, int64_t r) {
-    for (int s = 0; s < p.swz_rank; ++s) {
-        const int64_t mask = (int64_t(1) << p.swz_bits[s]) - 1;
-        if (p.swz_shift[s] > 0) r ^= ((r >> (p.swz_base[s] + p.swz_shift[s])) & mask) << p.swz_base[s];
-        else r ^= ((r >> p.swz_base[s]) & mask) << (p.swz_base[s] - p.swz_shift[s]);
-    }
-    return r;
+    return swizzle_stages(p.swz_rank, p.swz_bits, p.swz_base, p.swz_shift, r);
 }
 
 __device__ __forceinline__ float max_rule(float a, float b) {
@@ -121,7 +128,8 @@ __global__ void __launch_bounds__(256) copy_view_kernel(const float* __restrict_
          t += int64_t(gridDim.x) * blockDim.x) {
         const int64_t i = t / p.n_red, j = t % p.n_red;
         const int64_t f = swz(p, p.x_offset + decompose(p.xk, i) + decompose(p.xr, j));
-        const int64_t g = p.g_offset + decompose(p.gk, i) + decompose(p.gr, j);
+        const int64_t g = swizzle_stages(p.dswz_rank, p.dswz_bits, p.dswz_base, p.dswz_shift,
+                                         p.g_offset + decompose(p.gk, i) + decompose(p.gr, j));
         if (f < 0 || f >= p.x_size || g < 0 || g >= p.g_size) {
             report_device_error(SW_ERR_INVALID);
             continue;
@@ -233,6 +241,20 @@ extern "C" int sw_copy_view_f32(const sw_reduce_plan* src_plan, const float* src
         p.swz_base[s] = src_plan->swizzle_base[s];
         p.swz_shift[s] = src_plan->swizzle_shift[s];
     }
+    p.dswz_rank = dst_plan->swizzle_rank;
+    if (p.dswz_rank < 0 || p.dswz_rank > SW_MAX_SWIZZLE)
+        return fail(SW_ERR_INVALID, "sw_copy_view_f32: destination swizzle rank");
+    for (int s = 0; s < p.dswz_rank; ++s) {
+        p.dswz_bits[s] = dst_plan->swizzle_bits[s];
+        p.dswz_base[s] = dst_plan->swizzle_base[s];
+        p.dswz_shift[s] = dst_plan->swizzle_shift[s];
+    }
+    for (const sw_reduce_plan* q : {src_plan, dst_plan})
+        for (int s = 0; s < q->swizzle_rank; ++s)  // the constraints of SwizzleStage (core/swizzle.py:44-60)
+            if (q->swizzle_bits[s] <= 0 || q->swizzle_base[s] < 0 || q->swizzle_shift[s] == 0 ||
+                std::abs(q->swizzle_shift[s]) < q->swizzle_bits[s] ||
+                q->swizzle_bits[s] + q->swizzle_base[s] + std::abs(q->swizzle_shift[s]) > 62)
+                return fail(SW_ERR_INVALID, "sw_copy_view_f32: invalid swizzle stage %d", s);
     if (nk == 0 || nr == 0) return ok();
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

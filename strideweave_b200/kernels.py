@@ -70,10 +70,12 @@ def reduce_backward_f32(kind: str, x_ptr: int, x_size: int, x_offset: int, kept:
 def copy_view_f32(src_ptr: int, src_size: int, src_offset: int, src_kept: Sequence[Leaf],
                   src_reduced: Sequence[Leaf], dst_ptr: int, dst_size: int, dst_offset: int,
                   dst_kept: Sequence[Leaf], dst_reduced: Sequence[Leaf], *, swizzle: Sequence[SwizzleStage] = (),
-                  stream: int = 0) -> None:
-    """Copy a two-mode Float32 view into another placement (see sw_copy_view_f32)."""
+                  dst_swizzle: Sequence[SwizzleStage] = (), stream: int = 0) -> None:
+    """Copy a two-mode 32-bit view into another placement, the source's flat
+    indices through ``swizzle`` and the destination's through ``dst_swizzle``
+    (see sw_copy_view_f32)."""
     sp = make_reduce_plan("reduce_sum", src_offset, src_kept, src_reduced, swizzle)
-    dp = make_reduce_plan("reduce_sum", dst_offset, dst_kept, dst_reduced)
+    dp = make_reduce_plan("reduce_sum", dst_offset, dst_kept, dst_reduced, dst_swizzle)
     N.check(N.lib.sw_copy_view_f32(byref(sp), c_void_p(src_ptr), int(src_size), byref(dp), c_void_p(dst_ptr),
                                    int(dst_size), c_void_p(stream)))
 

@@ -80,6 +80,23 @@ def swizzle_stages(carrier: Any) -> list[tuple[int, int, int]]:
     return [(int(s.bits), int(s.base), int(s.shift)) for s in swz.stages]
 
 
+def swizzle_map(stages: list[tuple[int, int, int]], count: int) -> Any:
+    """Physical index of flat indices 0 .. count-1 under the XOR stages, all at
+    once: each stage r ^= ((r >> (base + shift)) & mask) << base, or for a
+    negative shift r ^= ((r >> base) & mask) << (base - shift), in order -
+    the map of src/strideweave/core/swizzle.py:107-117 over numpy arrays."""
+    import numpy as np
+
+    r = np.arange(count, dtype=np.int64)
+    for bits, base, shift in stages:
+        mask = (1 << bits) - 1
+        if shift > 0:
+            r ^= ((r >> (base + shift)) & mask) << base
+        else:
+            r ^= ((r >> base) & mask) << (base - shift)
+    return r
+
+
 def canonical_strides(shape_level: Any, stride: int = 1) -> tuple[Any, int]:
     """Column-major strides over a nested shape (the reference's canonical
     result layout, src/strideweave/carriers/cpu/native/_cpu_carrier.hpp:628-664)."""

@@ -23,6 +23,7 @@ import numpy as np
 
 from . import _native as N
 from ._host import DType  # makes `strideweave` importable (installed or baseline/_ref) first
+from .layout_plan import swizzle_stages
 
 from strideweave import CPU  # noqa: E402  (after _host)
 from strideweave.carriers.move import (  # noqa: E402
@@ -46,9 +47,16 @@ def _host_view(pointer: int, dtype: Any, count: int) -> np.ndarray:
     return np.frombuffer(buf, dtype=np_dtype, count=count)
 
 
-def _swizzle_map(carrier: Any, count: int) -> np.ndarray:
-    sw = carrier.swizzle
-    return np.fromiter((sw(i) for i in range(count)), dtype=np.int64, count=count)
+def _permute(src_ptr: int, src_size: int, src_offset: int, src_swizzle: list, dst_ptr: int, dst_size: int,
+             dst_offset: int, dst_swizzle: list) -> None:
+    """dst flat index (dst_offset + i, through dst_swizzle) = src flat index
+    (src_offset + i, through src_swizzle) for every i of the span: one
+    32-bit view copy on the device."""
+    from . import kernels
+
+    count = min(src_size - src_offset, dst_size - dst_offset)
+    kernels.copy_view_f32(src_ptr, src_size, src_offset, [(count, 1)], [(1, 0)], dst_ptr, dst_size, dst_offset,
+                          [(count, 1)], [(1, 0)], swizzle=src_swizzle, dst_swizzle=dst_swizzle)
 
 
 class CpuToCudaMoveOperation(MoveOperation):
@@ -64,10 +72,14 @@ class CpuToCudaMoveOperation(MoveOperation):
             return
         src = _host_view(tensor.carrier.pointer() + tensor.offset * 4, dtype, element_count)
         if destination.swizzle is not None:
-            phys = np.empty(destination.size(), dtype=src.dtype)
-            destination._buffer.download(phys)  # positions outside the span keep their values
-            phys[_swizzle_map(destination, element_count)] = src
-            destination._buffer.upload(phys)
+            # upload the span as it is, then permute it on the device into the
+            # swizzled placement (positions outside the span keep their values)
+            staged = N.DeviceBuffer(src.nbytes)
+            staged.upload(src)
+            _permute(staged.ptr, element_count, 0, [], destination.data_ptr, destination.size(), 0,
+                     swizzle_stages(destination))
+            N.synchronize()
+            staged.free()
         else:
             N.check(N.lib.sw_memcpy_h2d(c_void_p(destination.data_ptr), c_void_p(src.ctypes.data), src.nbytes, None))
         N.synchronize()  # the source is released as soon as this returns
@@ -88,11 +100,12 @@ class CudaToCpuMoveOperation(MoveOperation):
         dst = _host_view(destination.pointer(), dtype, element_count)
         src = tensor.carrier
         if src.swizzle is not None:
-            phys = np.empty(src.size(), dtype=dst.dtype)
-            src._buffer.download(phys)
-            N.synchronize()
-            idx = _swizzle_map(src, tensor.offset + element_count)[tensor.offset:]
-            dst[:] = phys[idx]
+            # gather the span out of the swizzled placement on the device, then
+            # one copy to the host
+            staged = N.DeviceBuffer(dst.nbytes)
+            _permute(src.data_ptr, src.size(), tensor.offset, swizzle_stages(src), staged.ptr, element_count, 0, [])
+            staged.download(dst)
+            staged.free()
         else:
             N.check(N.lib.sw_memcpy_d2h(c_void_p(dst.ctypes.data), c_void_p(src.data_ptr + tensor.offset * 4),
                                         dst.nbytes, None))

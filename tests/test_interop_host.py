@@ -68,3 +68,17 @@ def test_exported_capsule_life_cycle_needs_no_device():
         del cap
         gc.collect()
         assert ctypes.addressof(m) not in D._LIVE
+
+
+@pytest.mark.parametrize("stages", [[(3, 2, 3)], [(2, 4, -3)], [(3, 2, 3), (2, 7, -4)]])
+def test_vectorised_swizzle_map_equals_the_reference_swizzle(stages):
+    """The numpy swizzle map the carrier's host paths (moves, uploads, reads)
+    use equals the reference's Swizzle evaluated index by index."""
+    import numpy as np
+    from strideweave import Shape, Swizzle, SwizzleStage
+
+    from strideweave_b200.layout_plan import swizzle_map
+
+    size = 1 << 13
+    swz = Swizzle(Shape(size), *[SwizzleStage(bits=b, base=a, shift=s) for b, a, s in stages])
+    np.testing.assert_array_equal(swizzle_map(stages, size), [swz(i) for i in range(size)])
