@@ -95,8 +95,9 @@ def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 METRIC = "sharded MXFP8 contraction TFLOP/s"
@@ -631,8 +632,10 @@ def main() -> None:
         peaks = load_peaks()
         m = sharded["m"]
         # MXFP8 block-scaled MMA runs at twice the dense bf16 rate; the measured
-        # cuBLAS bf16 burst figure stands for the clock and power of this pool
-        peak = 2.0 * peaks["bf16_tflops"]
+        # cuBLAS bf16 figures stand for the clock and power of this pool.  The
+        # headline contraction runs back to back for over a second under the
+        # power cap, so its denominator is the sustained figure.
+        peak = 2.0 * peaks["bf16_tflops_sustained"]
         kernel_tflops = m["launch_flop"] / (m["ms"] / 1e3) / 1e12
         traffic = None
         if NCU_TRAFFIC_GEMM_8192_ROWS is not None:
@@ -655,8 +658,10 @@ def main() -> None:
             "roofline": {"bound": "tensor", "kernel": "mx_gemm_kernel<E4M3, 256, 3, fp32 rows>",
                          "achieved": round(kernel_tflops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(kernel_tflops / peak, 4),
-                         "peak_source": f"{peaks['source']}: 2 x bf16 dense burst (MXFP8 is twice the bf16 rate)",
-                         "traffic": traffic, "frac_of_spec_4500": round(kernel_tflops / 4500.0, 4)},
+                         "peak_source": f"{peaks['source']}: 2 x bf16 dense sustained (MXFP8 is twice the bf16 "
+                                        f"rate; the timed region runs under the power cap)",
+                         "traffic": traffic, "frac_of_burst": round(kernel_tflops / (2.0 * peaks["bf16_tflops"]), 4),
+                         "frac_of_spec_4500": round(kernel_tflops / 4500.0, 4)},
             "e2e": {"value": round(sharded["e2e"]["value"], 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": sharded["e2e"]["h2d"], "d2h_bytes_per_step": sharded["e2e"]["d2h"]},
             "gpu_launches": world * args.steps,

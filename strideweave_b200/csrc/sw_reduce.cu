@@ -503,6 +503,46 @@ __device__ __forceinline__ void exact_walk(const float* __restrict__ x, const Sw
 // swizzle, if any, commutes with doff).  U loads in flight per batch.
 template <class Op, class Ord, int U>
 __device__ __forceinline__ bool fast_walk(const float* ptr, int64_t doff, int iters, FastFold<Op, Ord>& f) {
+    if constexpr (Op::kKind == Kind::kArgmax) {
+        // A batch of U vectors is folded per component with max.NaN first
+        // (one instruction an element); only a component whose batch maximum
+        // beats its running maximum - rare once the walk is under way - is
+        // searched for the first step holding that maximum.  That is the
+        // sequential rule (larger wins, the earlier of equal values stays,
+        // -0 == +0); a NaN anywhere makes its batch maximum NaN, which never
+        // compares greater and marks the walk for the exact re-walk.
+        for (int t0 = 0; t0 < iters; t0 += U) {
+            float4 val[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                val[u] = t0 + u < iters ? load_stream4(ptr + int64_t(t0 + u) * doff)
+                                        : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            if (t0 == 0) f.init(val[0]);
+            float m[4] = {val[0].x, val[0].y, val[0].z, val[0].w};
+#pragma unroll
+            for (int u = 1; u < U; ++u) {
+                m[0] = max_nan(m[0], val[u].x);
+                m[1] = max_nan(m[1], val[u].y);
+                m[2] = max_nan(m[2], val[u].z);
+                m[3] = max_nan(m[3], val[u].w);
+            }
+            f.nanp = max_nan(f.nanp, max_nan(max_nan(m[0], m[1]), max_nan(m[2], m[3])));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (m[e] > f.v[e]) {
+                    int first = U - 1;
+#pragma unroll
+                    for (int u = U - 1; u >= 0; --u) {
+                        const float c = e == 0 ? val[u].x : e == 1 ? val[u].y : e == 2 ? val[u].z : val[u].w;
+                        if (c == m[e]) first = u;
+                    }
+                    f.v[e] = m[e];
+                    f.j[e] = Ord(t0 + first);
+                }
+            }
+        }
+        return !f.needs_exact();
+    }
     for (int t0 = 0; t0 < iters; t0 += U) {
         float4 val[U];
 #pragma unroll
