@@ -795,6 +795,32 @@ def bench_quantize(torch, N, kernels, s, stream) -> dict:
     out["mxfp8_dual_gelu_grad_4096x8192"] = {"us": round(us, 2), "gbs": round(gbs, 1),
                                              "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
                                              "bytes": moved}
+    # the view quantiser on config 2(c)'s placement: X[8192 x 4096] in
+    # 128 x 32 tiles through the 3-bit swizzle, quantised along mode 1 where
+    # it lies (two 128 MiB sources alternate)
+    kept, red, swz = plan_of("tiled_swizzled")
+    vpay = N.DeviceBuffer(R * C)
+    vsc = N.DeviceBuffer(kernels.scale_bytes_tc128(R, C // 32))
+    vsrc = [srcs[i].data_ptr() for i in range(2)]  # 256 MiB each: the first 128 MiB hold the tiled X
+
+    def qv(i):
+        kernels.mx_quantize_view(N.SW_MX_E4M3, vsrc[i % 2], R * C, 0, kept, red, vpay.ptr, C, vsc.ptr, swizzle=swz,
+                                 stream=s)
+    for i in range(4):
+        qv(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        qv(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    moved = R * C * 4 + R * C + kernels.scale_bytes_tc128(R, C // 32)
+    gbs = moved / (us * 1e3)
+    out["mxfp8_view_tiled_swizzled_8192x4096"] = {"us": round(us, 2), "gbs": round(gbs, 1),
+                                                  "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                                                  "bytes": moved}
     N.raise_device_status()
     return out
 

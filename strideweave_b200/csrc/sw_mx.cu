@@ -650,6 +650,46 @@ __device__ __forceinline__ int64_t view_swizzle(const ViewPlan& p, int64_t f) {
     return f;
 }
 
+// One element of a view at carrier flat index f (before the swizzle).  An
+// address outside the carrier (which the host's range check excludes) reads
+// as NaN and records SW_ERR_INVALID.
+__device__ __forceinline__ float view_load(const float* __restrict__ x, const ViewPlan& p, int64_t f) {
+    f = view_swizzle(p, f);
+    if (f >= 0 && f < p.x_size) return __ldcs(x + f);
+    report_device_error(SW_ERR_INVALID);
+    return __int_as_float(0x7FC00000);
+}
+
+// Quantises block kb of row r held one element per lane (lane i: column
+// c = 32 kb + i, `live` when c < cols): the warp's amax, the scale byte, the
+// lane's code; E2M1 lanes pair up into bytes.
+template <int FMT>
+__device__ __forceinline__ void quantize_lane_block(float v, bool live, int lane, int64_t r, int64_t kb, int64_t c,
+                                                    int64_t cols, int64_t kblocks, uint8_t* __restrict__ payload,
+                                                    int64_t ldp, uint8_t* __restrict__ scales, int layout,
+                                                    int64_t lds) {
+    const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(v) & 0x7FFFFFFFu);
+    uint8_t sc;
+    float inv;
+    bool special;
+    block_scale<FMT>(amax, sc, inv, special);
+    if (lane == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+    const float q = special ? 0.0f : __fmul_rn(v, inv);
+    if (FMT == SW_MX_E4M3) {
+        const uint32_t code = e4m3x4(q, 0.0f, 0.0f, 0.0f) & 0xFF;
+        if (live) payload[r * ldp + c] = uint8_t(code);
+    } else {
+        float eight[8] = {q, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t nib = e2m1x8(eight) & 0xF;
+        const uint32_t hi = __shfl_down_sync(0xFFFFFFFFu, nib, 1);
+        if (live && (lane & 1) == 0) {
+            uint8_t* dst = payload + r * ldp + c / 2;
+            if (c + 1 < cols) *dst = uint8_t(nib | (hi << 4));
+            else *dst = uint8_t((*dst & 0xF0) | nib);  // odd row length: the high nibble is not ours
+        }
+    }
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(256) quantize_view(const float* __restrict__ x, const ViewPlan p, int64_t rows,
                                                      int64_t cols, uint8_t* __restrict__ payload, int64_t ldp,
@@ -664,35 +704,73 @@ __global__ void __launch_bounds__(256) quantize_view(const float* __restrict__ x
         const int64_t kb = u - r * kblocks;
         const int64_t c = kb * 32 + lane;
         const bool live = c < cols;
-        float v = 0.0f;
-        if (live) {
-            const int64_t f = view_swizzle(p, p.offset + leaf_offset(p.rows, r) + leaf_offset(p.cols, c));
-            if (f >= 0 && f < p.x_size) {
-                v = __ldcs(x + f);
-            } else {
-                report_device_error(SW_ERR_INVALID);
-                v = __int_as_float(0x7FC00000);
+        const float v = live ? view_load(x, p, p.offset + leaf_offset(p.rows, r) + leaf_offset(p.cols, c)) : 0.0f;
+        quantize_lane_block<FMT>(v, live, lane, r, kb, c, cols, kblocks, payload, ldp, scales, layout, lds);
+    }
+}
+
+// The same, for views whose quantised mode starts with a leaf of a whole
+// number of 32-blocks (a tile row, a contiguous run): a warp walks 16
+// consecutive blocks of one row, lane i at run offset + i * stride of that
+// leaf, and steps from block to block with an odometer over the mode's
+// leaves instead of decomposing each element's ordinal.
+constexpr int kViewSegment = 16;  // blocks a warp walks per unit
+
+template <int FMT>
+__global__ void __launch_bounds__(256) quantize_view_runs(const float* __restrict__ x, const ViewPlan p, int64_t rows,
+                                                          int64_t cols, uint8_t* __restrict__ payload, int64_t ldp,
+                                                          uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    pdl_enter();
+    const int64_t kblocks = cols / 32;
+    const int64_t segs = (kblocks + kViewSegment - 1) / kViewSegment;
+    const int64_t units = rows * segs;
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    const int64_t s0 = p.cols.stride[0], e0 = p.cols.shape[0];
+    for (int64_t u = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+        const int64_t r = u / segs;
+        const int64_t kb0 = (u - r * segs) * kViewSegment;
+        const int64_t kb1 = min(kblocks, kb0 + kViewSegment);
+        const int64_t row = p.offset + leaf_offset(p.rows, r);
+        // odometer of the quantised mode at element 32 kb0 (lane-uniform)
+        int64_t key[SW_MAX_LEAVES];
+        int64_t col = 0, o = kb0 * 32;
+#pragma unroll
+        for (int k = 0; k < SW_MAX_LEAVES; ++k) {
+            if (k < p.cols.rank) {
+                key[k] = o % p.cols.shape[k];
+                o /= p.cols.shape[k];
+                col += key[k] * p.cols.stride[k];
             }
         }
-        const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(v) & 0x7FFFFFFFu);
-        uint8_t sc;
-        float inv;
-        bool special;
-        block_scale<FMT>(amax, sc, inv, special);
-        if (lane == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
-        const float q = special ? 0.0f : __fmul_rn(v, inv);
-        if (FMT == SW_MX_E4M3) {
-            const uint32_t code = e4m3x4(q, 0.0f, 0.0f, 0.0f) & 0xFF;
-            if (live) payload[r * ldp + c] = uint8_t(code);
-        } else {
-            float eight[8] = {q, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-            const uint32_t nib = e2m1x8(eight) & 0xF;
-            const uint32_t hi = __shfl_down_sync(0xFFFFFFFFu, nib, 1);
-            if (live && (lane & 1) == 0) {
-                uint8_t* dst = payload + r * ldp + c / 2;
-                if (c + 1 < cols) *dst = uint8_t(nib | (hi << 4));
-                else *dst = uint8_t((*dst & 0xF0) | nib);  // odd row length: the high nibble is not ours
+        // every block's element in flight first, then the folds
+        float v[kViewSegment];
+#pragma unroll
+        for (int b = 0; b < kViewSegment; ++b) {
+            if (kb0 + b >= kb1) break;
+            v[b] = view_load(x, p, row + col + lane * s0);
+            // 32 elements further along the mode: leaf 0 never splits a block
+            key[0] += 32;
+            col += 32 * s0;
+            if (key[0] == e0) {
+                key[0] = 0;
+                col -= e0 * s0;
+#pragma unroll
+                for (int k = 1; k < SW_MAX_LEAVES; ++k) {
+                    if (k >= p.cols.rank) break;
+                    key[k] += 1;
+                    col += p.cols.stride[k];
+                    if (key[k] < p.cols.shape[k]) break;
+                    col -= p.cols.shape[k] * p.cols.stride[k];
+                    key[k] = 0;
+                }
             }
+        }
+#pragma unroll
+        for (int b = 0; b < kViewSegment; ++b) {
+            if (kb0 + b >= kb1) break;
+            quantize_lane_block<FMT>(v[b], true, lane, r, kb0 + b, (kb0 + b) * 32 + lane, cols, kblocks, payload,
+                                     ldp, scales, layout, lds);
         }
     }
 }
@@ -839,8 +917,11 @@ extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const fl
     if (scale_layout == SW_SCALES_TC128 && (rows % 128 != 0 || kblocks % 4 != 0))
         SW_CUDA_TRY(cudaMemsetAsync(scales, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s),
                     "scale padding fill");
-    const int grid = grid_for(rows * kblocks * 32, 256);
-    auto kernel = fmt == SW_MX_E4M3 ? quantize_view<SW_MX_E4M3> : quantize_view<SW_MX_E2M1>;
+    const bool runs = p.cols.shape[0] % 32 == 0;  // blocks lie inside runs of the first leaf
+    const int64_t units = runs ? rows * ((kblocks + kViewSegment - 1) / kViewSegment) : rows * kblocks;
+    const int grid = grid_for(units * 32, 256);
+    auto kernel = runs ? (fmt == SW_MX_E4M3 ? quantize_view_runs<SW_MX_E4M3> : quantize_view_runs<SW_MX_E2M1>)
+                       : (fmt == SW_MX_E4M3 ? quantize_view<SW_MX_E4M3> : quantize_view<SW_MX_E2M1>);
     SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, x, p, rows, cols, payload, ld_payload, scales, scale_layout,
                            ld_scales),
                 "quantize_view launch");

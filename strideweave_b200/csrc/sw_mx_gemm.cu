@@ -420,12 +420,18 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     ptx::fence_proxy_async_smem();
                 }
                 ptx::named_barrier(1 + half, 128);
-                if (leader && alive && nb * BN + chunk * 32 < args.N) {  // partial boxes are clipped by TMA
-                    const uint32_t src = stage_addr + buf * kChunkBytes;
-                    if (kEpi == kEpiF32Cols)
-                        ptx::tma_store_2d(&tmap_c, mb * kBM, (p * num_n + nb) * BN + chunk * 32, src);
-                    else
-                        ptx::tma_store_2d(&tmap_c, nb * BN + chunk * 32, (p * num_m + mb) * kBM, src);
+                if (leader && alive) {
+                    // A chunk wholly past N (a ragged last tile) stores nothing,
+                    // but still commits a (then empty) group: the buffer-reuse
+                    // wait above counts one group per chunk.  Partial boxes are
+                    // clipped by TMA.
+                    if (nb * BN + chunk * 32 < args.N) {
+                        const uint32_t src = stage_addr + buf * kChunkBytes;
+                        if (kEpi == kEpiF32Cols)
+                            ptx::tma_store_2d(&tmap_c, mb * kBM, (p * num_n + nb) * BN + chunk * 32, src);
+                        else
+                            ptx::tma_store_2d(&tmap_c, nb * BN + chunk * 32, (p * num_m + mb) * kBM, src);
+                    }
                     ptx::bulk_commit_group();
                 }
             }

@@ -117,6 +117,9 @@ VIEWS = {
                        (3, 2, 3)),
     # blocks along a hierarchical, strided mode (a transposed tiled store)
     "transposed_tiled": (Layout(Shape([[32, 4], [128, 2]]), Stride([[1, 128 * 32], [32, 128 * 32 * 4]])), None),
+    # runs of 16 columns: every block spans two runs (the per-element walk)
+    "short_runs": (Layout(Shape([128, [16, 8]]), Stride([16, [1, 2048]])), None),
+    "short_runs_swizzled": (Layout(Shape([128, [16, 8]]), Stride([16, [1, 2048]])), (2, 4, 3)),
 }
 
 
