@@ -51,7 +51,7 @@ PARITY_TOL = 2e-3  # relative Frobenius error of the contraction path
 # from ncu on the per-rank shape of eight GPUs (8192 x 16384 x 16384, the
 # committed capture) scaled by the 8x rows: A reads and C writes grow with the
 # rows, and so do B's re-reads (one pass of B per raster group of row tiles).
-NCU_TRAFFIC_GEMM_8192_ROWS = None
+NCU_TRAFFIC_GEMM_8192_ROWS = 2874.225e6 + 574.960e6
 
 # ---- the layout-aware reductions (config 2) ---------------------------------------
 R, C = 8192, 4096

@@ -626,13 +626,11 @@ struct ViewPlan {
 
 __device__ __forceinline__ int64_t leaf_offset(const ViewLeaves& l, int64_t i) {
     int64_t off = 0;
-#pragma unroll
-    for (int k = 0; k < SW_MAX_LEAVES; ++k) {
-        if (k < l.rank) {
-            const int64_t c = i % l.shape[k];
-            i /= l.shape[k];
-            off += c * l.stride[k];
-        }
+#pragma unroll 1
+    for (int k = 0; k < l.rank; ++k) {
+        const int64_t c = i % l.shape[k];
+        i /= l.shape[k];
+        off += c * l.stride[k];
     }
     return off;
 }
@@ -737,11 +735,10 @@ __global__ void __launch_bounds__(256) quantize_view_runs(const float* __restric
         int64_t col = 0, o = kb0 * 32;
 #pragma unroll
         for (int k = 0; k < SW_MAX_LEAVES; ++k) {
-            if (k < p.cols.rank) {
-                key[k] = o % p.cols.shape[k];
-                o /= p.cols.shape[k];
-                col += key[k] * p.cols.stride[k];
-            }
+            if (k >= p.cols.rank) break;
+            key[k] = o % p.cols.shape[k];
+            o /= p.cols.shape[k];
+            col += key[k] * p.cols.stride[k];
         }
         // every block's element in flight first, then the folds
         float v[kViewSegment];
@@ -771,6 +768,78 @@ __global__ void __launch_bounds__(256) quantize_view_runs(const float* __restric
             if (kb0 + b >= kb1) break;
             quantize_lane_block<FMT>(v[b], true, lane, r, kb0 + b, (kb0 + b) * 32 + lane, cols, kblocks, payload,
                                      ldp, scales, layout, lds);
+        }
+    }
+}
+
+// The vectorised walk: the quantised mode starts with a unit-stride leaf of
+// whole 32-blocks, every other stride and the offset are multiples of 4, and
+// the swizzle (if any) keeps 16-byte chunks whole, so each lane reads four
+// consecutive elements with one 16-byte load.  A warp takes 32 consecutive
+// blocks of one row: lane j decomposes block j's offset once, and for each of
+// eight loads lane L takes block 4 s + L / 8 (eight lanes a block) by a
+// shuffle.  A block's amax is a three-step shuffle over its eight lanes; each
+// lane stores its four codes (E2M1: two bytes) and the block's first lane its
+// scale byte.
+constexpr int kViewVecSegment = 32;
+
+template <int FMT>
+__global__ void __launch_bounds__(256) quantize_view_vec(const float* __restrict__ x, const ViewPlan p, int64_t rows,
+                                                         int64_t cols, uint8_t* __restrict__ payload, int64_t ldp,
+                                                         uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    pdl_enter();
+    const int64_t kblocks = cols / 32;
+    const int64_t segs = (kblocks + kViewVecSegment - 1) / kViewVecSegment;
+    const int64_t units = rows * segs;
+    const int lane = threadIdx.x & 31;
+    const int sub = lane & 7;  // the lane's four elements: 4 sub .. 4 sub + 3 of its block
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t u = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+        const int64_t r = u / segs;
+        const int64_t kb0 = (u - r * segs) * kViewVecSegment;
+        const int64_t row = p.offset + leaf_offset(p.rows, r);
+        const int64_t mine = kb0 + lane < kblocks ? leaf_offset(p.cols, (kb0 + lane) * 32) : 0;
+        float4 q[kViewVecSegment / 4];
+#pragma unroll
+        for (int s = 0; s < kViewVecSegment / 4; ++s) {
+            const int b = 4 * s + (lane >> 3);
+            const int64_t boff = __shfl_sync(0xFFFFFFFFu, mine, b);
+            q[s] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (kb0 + b < kblocks) {
+                int64_t f = view_swizzle(p, row + boff + 4 * sub);
+                if (f >= 0 && f + 3 < p.x_size) {
+                    q[s] = __ldcs(reinterpret_cast<const float4*>(x + f));
+                } else {
+                    report_device_error(SW_ERR_INVALID);
+                    const float nan = __int_as_float(0x7FC00000);
+                    q[s] = make_float4(nan, nan, nan, nan);
+                }
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < kViewVecSegment / 4; ++s) {
+            const int64_t kb = kb0 + 4 * s + (lane >> 3);
+            const bool live = kb < kblocks;  // uniform over the block's eight lanes
+            uint32_t amax = max(max(__float_as_uint(q[s].x) & 0x7FFFFFFFu, __float_as_uint(q[s].y) & 0x7FFFFFFFu),
+                                max(__float_as_uint(q[s].z) & 0x7FFFFFFFu, __float_as_uint(q[s].w) & 0x7FFFFFFFu));
+            amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+            amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+            amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+            uint8_t sc;
+            float inv;
+            bool special;
+            block_scale<FMT>(amax, sc, inv, special);
+            if (!live) continue;
+            if (sub == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+            const float a = special ? 0.0f : __fmul_rn(q[s].x, inv), b = special ? 0.0f : __fmul_rn(q[s].y, inv);
+            const float c = special ? 0.0f : __fmul_rn(q[s].z, inv), d = special ? 0.0f : __fmul_rn(q[s].w, inv);
+            uint8_t* dst = payload + r * ldp;
+            if (FMT == SW_MX_E4M3) {
+                *reinterpret_cast<uint32_t*>(dst + kb * 32 + 4 * sub) = e4m3x4(a, b, c, d);
+            } else {
+                const float e[8] = {a, b, c, d, 0.0f, 0.0f, 0.0f, 0.0f};
+                *reinterpret_cast<uint16_t*>(dst + kb * 16 + 2 * sub) = uint16_t(e2m1x8(e) & 0xFFFF);
+            }
         }
     }
 }
@@ -918,10 +987,20 @@ extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const fl
         SW_CUDA_TRY(cudaMemsetAsync(scales, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s),
                     "scale padding fill");
     const bool runs = p.cols.shape[0] % 32 == 0;  // blocks lie inside runs of the first leaf
-    const int64_t units = runs ? rows * ((kblocks + kViewSegment - 1) / kViewSegment) : rows * kblocks;
+    // 16-byte loads: unit-stride runs, 4-aligned offsets, a swizzle that never
+    // touches the two lowest index bits, 4-byte payload rows
+    bool vec = runs && p.cols.stride[0] == 1 && p.offset % 4 == 0 && ld_payload % 4 == 0 &&
+               (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(payload) & 3) == 0;
+    for (int k = 0; k < p.rows.rank; ++k) vec = vec && p.rows.stride[k] % 4 == 0;
+    for (int k = 1; k < p.cols.rank; ++k) vec = vec && p.cols.stride[k] % 4 == 0;
+    for (int i = 0; i < p.swz_rank; ++i) vec = vec && p.swz_base[i] >= 2;
+    const int64_t units = vec    ? rows * ((kblocks + kViewVecSegment - 1) / kViewVecSegment)
+                          : runs ? rows * ((kblocks + kViewSegment - 1) / kViewSegment)
+                                 : rows * kblocks;
     const int grid = grid_for(units * 32, 256);
-    auto kernel = runs ? (fmt == SW_MX_E4M3 ? quantize_view_runs<SW_MX_E4M3> : quantize_view_runs<SW_MX_E2M1>)
-                       : (fmt == SW_MX_E4M3 ? quantize_view<SW_MX_E4M3> : quantize_view<SW_MX_E2M1>);
+    auto kernel = vec    ? (fmt == SW_MX_E4M3 ? quantize_view_vec<SW_MX_E4M3> : quantize_view_vec<SW_MX_E2M1>)
+                  : runs ? (fmt == SW_MX_E4M3 ? quantize_view_runs<SW_MX_E4M3> : quantize_view_runs<SW_MX_E2M1>)
+                         : (fmt == SW_MX_E4M3 ? quantize_view<SW_MX_E4M3> : quantize_view<SW_MX_E2M1>);
     SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, x, p, rows, cols, payload, ld_payload, scales, scale_layout,
                            ld_scales),
                 "quantize_view launch");

@@ -36,6 +36,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "sw_common.cuh"
 #include "sw_ptx.cuh"
@@ -100,6 +101,13 @@ struct Cfg {
     static constexpr uint32_t kStageTx = kABytes + kBBytes + kSfaBytes + kSfbBytes;
 };
 
+// A count known at compile time, passed where a runtime int also fits (the
+// full stages of the MMA issue loop unroll with it as a constant).
+template <int V>
+struct Count {
+    __device__ constexpr operator int() const { return V; }
+};
+
 // Instruction descriptor of a block-scaled MMA (E8M0 scales, K-major A and B).
 __device__ __forceinline__ uint32_t make_idesc(uint32_t fmt_code, int M, int N, uint32_t sfa_id, uint32_t sfb_id) {
     return (sfb_id << 4) | (fmt_code << 7) | (fmt_code << 10) | (uint32_t(N >> 3) << 17) | (1u << 23) |
@@ -116,6 +124,9 @@ struct GemmArgs {
     int katoms;           // scale atoms per row group (ceil(K/128))
     int row_bytes;        // payload bytes of one operand row (K or K/2)
     int b_groups;         // 128-row groups in B's scale plane (ceil(batch N / 128))
+    int ragged_k;         // the last stage holds fewer than kAtoms atoms or kMmaPerStage MMAs
+    int last_atoms;       // scale atoms of the last stage
+    int last_mmas;        // MMAs of the last stage (32 payload bytes each)
     int beta_one;
     int out_bf16;
     int batch;            // stacked problems (block-diagonal), 1 for one contraction
@@ -201,18 +212,18 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                 int p, mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int ga = p * num_m + mb, gb = p * num_n + nb;  // stacked row blocks
+                // Scale atoms that exist: the last E2M1 stage of an odd atom
+                // count has one, and B groups past the plane (a ragged N whose
+                // last tile covers one 128-row group) have none.  The payload
+                // boxes always count in full (TMA zero-fills past K).
+                int b_groups_here = 0;
+#pragma unroll
+                for (int g = 0; g < BN / 128; ++g) b_groups_here += (gb * (BN / 128) + g < args.b_groups) ? 1 : 0;
                 for (int ks = 0; ks < args.k_stages; ++ks) {
                     if (!ptx::mbar_wait(bar_empty + 8 * stage, phase ^ 1)) { alive = false; break; }
                     const uint32_t full = bar_full + 8 * stage;
                     const int64_t atom0 = int64_t(ks) * C::kAtoms;
-                    // Scale atoms that exist: the last E2M1 stage of an odd atom
-                    // count has one, and B groups past the plane (a ragged N
-                    // whose last tile covers one 128-row group) have none.  The
-                    // payload boxes always count in full (TMA zero-fills past K).
-                    const int atoms = (int)min(int64_t(C::kAtoms), int64_t(args.katoms) - atom0);
-                    int b_groups_here = 0;
-#pragma unroll
-                    for (int g = 0; g < BN / 128; ++g) b_groups_here += (gb * (BN / 128) + g < args.b_groups) ? 1 : 0;
+                    const int atoms = ks + 1 < args.k_stages ? C::kAtoms : args.last_atoms;
                     ptx::mbar_arrive_expect_tx(full, C::kABytes + C::kBBytes + (1 + b_groups_here) * atoms * 512);
                     ptx::tma_load_2d(sbase + C::kOffA + stage * C::kABytes, &tmap_a, ks * kBKBytes, ga * kBM, full);
                     ptx::tma_load_2d(sbase + C::kOffB + stage * C::kBBytes, &tmap_b, ks * kBKBytes, gb * BN, full);
@@ -251,45 +262,53 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     const uint32_t sf_col = tmem + C::kSfCol0 + stage * C::kSfColsPerStage;
                     const uint32_t sfa_col = sf_col;
                     const uint32_t sfb_col = sf_col + C::kSfaCols;
-                    // the stage's real K: 32 payload bytes per MMA, the atoms the producer loaded
-                    const int atoms = min(C::kAtoms, args.katoms - ks * C::kAtoms);
-                    const int mmas = min(C::kMmaPerStage, (args.row_bytes - ks * kBKBytes + 31) / 32);
-                    // scale atoms: shared memory -> TMEM (replicated per sub-partition).
-                    // A B group past the plane was not loaded: its stale scales
-                    // only reach result columns past N, which are not stored.
-#pragma unroll
-                    for (int a = 0; a < C::kAtoms; ++a) {
-                        if (a >= atoms) break;
-                        ptx::tc_cp_32x128b_x4(sfa_col + 4 * a,
-                                              ptx::smem_desc(sbase + C::kOffSfa + stage * C::kSfaBytes + a * 512, 0,
-                                                             128, ptx::kLayoutNone));
-#pragma unroll
-                        for (int g = 0; g < BN / 128; ++g)
-                            ptx::tc_cp_32x128b_x4(
-                                sfb_col + a * 4 * (BN / 128) + 4 * g,
-                                ptx::smem_desc(sbase + C::kOffSfb + stage * C::kSfbBytes + (g * C::kAtoms + a) * 512,
-                                               0, 128, ptx::kLayoutNone));
-                    }
                     const uint32_t a_addr = sbase + C::kOffA + stage * C::kABytes;
                     const uint32_t b_addr = sbase + C::kOffB + stage * C::kBBytes;
+                    // One stage: its scale atoms into TMEM (shared memory -> TMEM,
+                    // replicated per sub-partition), then its MMAs, 32 payload
+                    // bytes of K each.  Full stages run with the counts as
+                    // constants; only a ragged last stage passes fewer atoms
+                    // (those the producer loaded) and MMAs (those reaching real K
+                    // blocks).  A B group past the plane was not loaded: its
+                    // stale scales only reach result columns past N, which are
+                    // not stored.
+                    auto issue = [&](auto atoms, auto mmas) {
 #pragma unroll
-                    for (int j = 0; j < C::kMmaPerStage; ++j) {
-                        if (j >= mmas) break;
-                        // 32 payload bytes of K per MMA in both formats
-                        const uint64_t adesc = ptx::smem_desc(a_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
-                        const uint64_t bdesc = ptx::smem_desc(b_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
-                        const uint32_t accumulate = (ks > 0 || j > 0) ? 1u : 0u;
-                        if (FMT == SW_MX_E4M3) {
-                            const uint32_t idesc = make_idesc(fmt_code, kBM, BN, uint32_t(j), uint32_t(j));
-                            ptx::mma_mxf8f6f4(tmem + C::kAccCol, adesc, bdesc, idesc, accumulate, sfa_col, sfb_col);
-                        } else {
-                            const int atom = j / 2;
-                            const uint32_t sf_id = uint32_t((2 * j) % 4);
-                            const uint32_t idesc = make_idesc(fmt_code, kBM, BN, sf_id, sf_id);
-                            ptx::mma_mxf4(tmem + C::kAccCol, adesc, bdesc, idesc, accumulate, sfa_col + 4 * atom,
-                                          sfb_col + atom * 4 * (BN / 128));
+                        for (int a = 0; a < C::kAtoms; ++a) {
+                            if (a >= int(atoms)) break;
+                            ptx::tc_cp_32x128b_x4(sfa_col + 4 * a,
+                                                  ptx::smem_desc(sbase + C::kOffSfa + stage * C::kSfaBytes + a * 512,
+                                                                 0, 128, ptx::kLayoutNone));
+#pragma unroll
+                            for (int g = 0; g < BN / 128; ++g)
+                                ptx::tc_cp_32x128b_x4(
+                                    sfb_col + a * 4 * (BN / 128) + 4 * g,
+                                    ptx::smem_desc(sbase + C::kOffSfb + stage * C::kSfbBytes + (g * C::kAtoms + a) * 512,
+                                                   0, 128, ptx::kLayoutNone));
                         }
-                    }
+#pragma unroll
+                        for (int j = 0; j < C::kMmaPerStage; ++j) {
+                            if (j >= int(mmas)) break;
+                            const uint64_t adesc = ptx::smem_desc(a_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
+                            const uint64_t bdesc = ptx::smem_desc(b_addr + 32 * j, 0, 1024, ptx::kLayoutSwizzle128);
+                            const uint32_t accumulate = (ks > 0 || j > 0) ? 1u : 0u;
+                            if (FMT == SW_MX_E4M3) {
+                                const uint32_t idesc = make_idesc(fmt_code, kBM, BN, uint32_t(j), uint32_t(j));
+                                ptx::mma_mxf8f6f4(tmem + C::kAccCol, adesc, bdesc, idesc, accumulate, sfa_col,
+                                                  sfb_col);
+                            } else {
+                                const int atom = j / 2;
+                                const uint32_t sf_id = uint32_t((2 * j) % 4);
+                                const uint32_t idesc = make_idesc(fmt_code, kBM, BN, sf_id, sf_id);
+                                ptx::mma_mxf4(tmem + C::kAccCol, adesc, bdesc, idesc, accumulate, sfa_col + 4 * atom,
+                                              sfb_col + atom * 4 * (BN / 128));
+                            }
+                        }
+                    };
+                    if (ks + 1 < args.k_stages || !args.ragged_k)
+                        issue(Count<C::kAtoms>{}, Count<C::kMmaPerStage>{});
+                    else
+                        issue(args.last_atoms, args.last_mmas);
                     ptx::tc_commit(bar_empty + 8 * stage);  // frees the smem stage and its scale columns
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
@@ -609,6 +628,9 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.katoms = (int)((K / 32 + 3) / 4);
     args.row_bytes = (int)row_bytes;
     args.b_groups = (int)((batch * N + 127) / 128);
+    args.last_atoms = args.katoms - (args.k_stages - 1) * Cf::kAtoms;
+    args.last_mmas = (int)((row_bytes - int64_t(args.k_stages - 1) * kBKBytes + 31) / 32);
+    args.ragged_k = args.last_atoms != Cf::kAtoms || args.last_mmas != Cf::kMmaPerStage;
     args.beta_one = beta_one;
     args.out_bf16 = out_dtype == SW_OUT_BF16;
     args.batch = (int)batch;

@@ -115,6 +115,9 @@ VIEWS = {
     # the same tiles stored through the config-2(c) swizzle (16-byte chunks XOR row % 8)
     "tiled_swizzled": (Layout(Shape([[128, 2], [32, 4]]), Stride([[32, 128 * 32 * 4], [1, 128 * 32]])),
                        (3, 2, 3)),
+    # a swizzle that moves single elements (bits 1..2): the element-wise run walk
+    "tiled_swizzled_fine": (Layout(Shape([[128, 2], [32, 4]]), Stride([[32, 128 * 32 * 4], [1, 128 * 32]])),
+                            (2, 1, 4)),
     # blocks along a hierarchical, strided mode (a transposed tiled store)
     "transposed_tiled": (Layout(Shape([[32, 4], [128, 2]]), Stride([[1, 128 * 32], [32, 128 * 32 * 4]])), None),
     # runs of 16 columns: every block spans two runs (the per-element walk)
