@@ -457,15 +457,26 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
         comm = NcclCommunicator(world, rank, ids[0])
     a = quantize_generated(torch, N, kernels, fmt, M5, kp.k_local, seed=8000 + rank)
     b = quantize_generated(torch, N, kernels, fmt, N5, kp.k_local, seed=9500 + rank)
-    op = MXShardedContraction(kp, fmt, a, b, comm=comm)
     ksteps = max(3, args.steps // 4)
+    # the peer-memory K-split (the contraction writes each row block into its
+    # owner's slot over NVLink, owners sum their slots): the K-split of record
+    pp = ShardPlan("k", world, rank, M5, N5, K5, chunks=1)
+    op = MXShardedContraction(pp, fmt, a, b, comm=comm, transport="peer")
     kms = time_steps(N, op.run, ksteps, min(args.warmup, 2), torch, dist, world)
-    res["k"] = {"ms": kms, "tflops": FLOP5 / (kms / 1e3) / 1e12, "chunks": K_CHUNKS, "comm_sms": kp.comm_sms}
+    res["k"] = {"ms": kms, "tflops": FLOP5 / (kms / 1e3) / 1e12, "transport": "NVLink peer stores + ordered slot sum"}
     N.raise_device_status()
     res["k"]["parity"] = sharded_parity(torch, dist, N, kernels, fmt, op, a, b, world, rank)
+    op.close()
+    del op
+    # the same K-split with NCCL's reduce-scatter, chunked and overlapped
+    op = MXShardedContraction(kp, fmt, a, b, comm=comm)
+    nms = time_steps(N, op.run, ksteps, min(args.warmup, 2), torch, dist, world)
+    res["k"]["nccl"] = {"ms": nms, "tflops": FLOP5 / (nms / 1e3) / 1e12, "chunks": K_CHUNKS,
+                        "comm_sms": kp.comm_sms}
+    N.raise_device_status()
     if comm is not None:
-        # the reduce-scatter alone: all 8 chunks of Float32 partials (4 GiB per
-        # rank), on the collective's stream, with every SM free
+        # NCCL's reduce-scatter alone: all 8 chunks of Float32 partials (4 GiB
+        # per rank), on the collective's stream, with every SM free
         count = kp.rows_local * kp.chunk_cols
         cs = op.comm_stream.handle
 
@@ -482,7 +493,7 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
         bound = max(compute_ms, cms)
         res["k"]["comm_floor"] = {"ms": cms, "busbw_gbs": moved / (cms / 1e3) / 1e9,
                                   "bytes_per_rank": moved, "compute_ms": compute_ms, "bound_ms": bound,
-                                  "frac_of_bound": bound / kms}
+                                  "frac_of_bound": bound / kms, "frac_of_bound_nccl": bound / nms}
         op.close()
         comm.close()
     else:

@@ -129,6 +129,53 @@ int sw_nccl_reduce_scatter_f32(const float* send, float* recv, int64_t recv_coun
 int sw_nccl_all_gather_f32(const float* send, float* recv, int64_t send_count, void* comm, void* stream);
 int sw_nccl_comm_destroy(void* comm);
 
+/* The K-split over NVLink peer memory, without a collective library: every
+ * rank owns a landing buffer of `world` Float32 slots (one per writer) plus
+ * step flags; each rank's contraction writes its partial of every row block
+ * straight into the owner's slot (sw_mx_gemm_routed: plain peer stores, no
+ * TMA, no multicast), signals the owners, and each owner sums its slots in
+ * rank order (the same result bit for bit on every run).  No reference
+ * counterpart: the reference has no multi-device path.
+ *
+ * sw_ipc_alloc allocates device memory another process of the node can map
+ * and writes its SW_IPC_HANDLE_BYTES-byte handle; sw_ipc_open maps a peer's
+ * buffer from its handle (once per process and buffer), sw_ipc_close unmaps
+ * it, sw_ipc_free releases the owner's allocation. */
+#define SW_IPC_HANDLE_BYTES 64
+int sw_ipc_alloc(void** ptr, int64_t bytes, uint8_t* handle);
+int sw_ipc_open(const uint8_t* handle, void** ptr);
+int sw_ipc_close(void* ptr);
+int sw_ipc_free(void* ptr);
+
+/* Waits on `stream` until each of the `count` 32-bit step flags at `flags`
+ * (this GPU's memory, written by other ranks) reaches `target` (modulo 2^32).
+ * The wait is bounded by limit_ns: past it the kernel records SW_ERR_TIMEOUT
+ * for sw_device_status and returns, so a rank that died shows as a status. */
+int sw_peer_wait(const uint32_t* flags, int count, uint32_t target, int64_t limit_ns, void* stream);
+
+/* After a system-scope fence (every store the stream issued before it, peer
+ * stores included, is performed first), writes `value` to each of the
+ * `count` (at most 8) flags, each in some peer's memory. */
+int sw_peer_signal(uint32_t* const* flags, int count, uint32_t value, void* stream);
+
+/* out[i] = slots[i] + slots[slot_elems + i] + ... over `count` slots, in slot
+ * order (Float32 adds; slot_elems a multiple of 4, 16-byte aligned). */
+int sw_sum_slots_f32(const float* slots, int64_t slot_elems, int count, float* out, void* stream);
+
+/* sw_mx_gemm_ex with Float32 results routed by row block: C rows
+ * [q rows_per_dest, (q + 1) rows_per_dest) are written row-major with pitch
+ * ldc starting at dest[q] (q < ndest <= 8; rows_per_dest whole 128-row tiles,
+ * ndest * rows_per_dest = M; N and ldc multiples of 4).  A dest[q] may be
+ * another GPU's memory mapped with sw_ipc_open: each 128 x 32 chunk of a
+ * finished tile is staged in shared memory and leaves as whole 128-byte row
+ * segments by plain NVLink peer stores (N under 256 stores from registers),
+ * and the kernel fences them at system scope before it ends.  This is the
+ * contraction half of the peer-memory K-split. */
+int sw_mx_gemm_routed(int fmt, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
+                      const uint8_t* b, int64_t ldb, const uint8_t* scales_b,
+                      float* const* dest, int ndest, int64_t rows_per_dest, int64_t ldc,
+                      int64_t M, int64_t N, int64_t K, int max_ctas, void* stream);
+
 /* ---- layout-aware reductions -------------------------------------------- */
 
 #define SW_REDUCE_SUM 0

@@ -54,6 +54,7 @@ SW_XF_NONE = 0
 SW_XF_GELU = 1
 SW_XF_GELU_GRAD = 2
 SW_NCCL_ID_BYTES = 128
+SW_IPC_HANDLE_BYTES = 64
 
 
 class DeviceTimeout(RuntimeError):
@@ -184,6 +185,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, c_int, POINTER(c_int64), c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p, c_int64,
          POINTER(c_int64), c_int64, c_void_p, c_int64, POINTER(c_int64), c_int64, c_void_p],
+    ),
+    "sw_ipc_alloc": (c_int, [POINTER(c_void_p), c_int64, c_void_p]),
+    "sw_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "sw_ipc_close": (c_int, [c_void_p]),
+    "sw_ipc_free": (c_int, [c_void_p]),
+    "sw_peer_wait": (c_int, [c_void_p, c_int, ctypes.c_uint32, c_int64, c_void_p]),
+    "sw_peer_signal": (c_int, [POINTER(c_void_p), c_int, ctypes.c_uint32, c_void_p]),
+    "sw_sum_slots_f32": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "sw_mx_gemm_routed": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, POINTER(c_void_p), c_int, c_int64, c_int64,
+         c_int64, c_int64, c_int64, c_int, c_void_p],
     ),
     "sw_map_f32": (
         c_int,

@@ -67,6 +67,14 @@ constexpr int kEpiF32Rows = 2;
 constexpr int kEpiF32Cols = 3;
 constexpr int kOutBufs = 4;
 constexpr int kChunkBytes = kBM * 32 * 4;  // one 128 x 32 fp32 chunk
+constexpr int kMaxRouted = 8;              // destinations of a routed contraction (ranks of a node)
+
+// Where a routed contraction writes: row block q at dest[q] (see GemmArgs).
+struct Route {
+    int count;
+    int64_t rows_per_dest;
+    float* dest[kMaxRouted];
+};
 
 template <int FMT, int BN, int kStages, int kEpi>
 struct Cfg {
@@ -131,6 +139,12 @@ struct GemmArgs {
     int out_bf16;
     int batch;            // stacked problems (block-diagonal), 1 for one contraction
     int64_t c_batch;      // elements between consecutive problems' C (direct epilogue)
+    // routed results (Float32; staged rows epilogue, or the direct one for
+    // narrow N): C rows [q rows_per_dest, (q + 1) rows_per_dest) go to
+    // dest[q], row-major with pitch ldc_m
+    int routed;
+    int64_t rows_per_dest;
+    float* dest[kMaxRouted];
 };
 
 template <int FMT, int BN, int kStages, int kEpi>
@@ -439,7 +453,34 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     ptx::fence_proxy_async_smem();
                 }
                 ptx::named_barrier(1 + half, 128);
-                if (leader && alive) {
+                if (kEpi == kEpiF32Rows && args.routed && alive) {
+                    // Routed results: the half's 128 threads copy the staged
+                    // chunk to its owner's block, a warp writing four whole
+                    // 128-byte row segments per pass (full lines over NVLink),
+                    // as streaming stores: evict-first in L2, so the 4 bytes
+                    // per result do not push operand tiles out.
+                    // The next write of this buffer waits at the named barrier
+                    // above, which every thread meets after its reads here.
+                    // Thread t moves 16-byte unit u = t % 8 of rows t / 8 + 16 i
+                    // (i < 8): u and the swizzle (row % 8 = (t / 8) % 8) stay
+                    // fixed, so each pass is one shared load and one store at
+                    // constant strides.  N % 4 == 0: a unit is all in or out.
+                    const int tid = threadIdx.x - (64 + 128 * half);
+                    const int u = tid & 7, r0 = tid >> 3;
+                    const int64_t n = int64_t(nb) * BN + chunk * 32 + 4 * u;
+                    if (n < args.N) {
+                        const int owner = int(int64_t(mb) * kBM / args.rows_per_dest);
+                        const int64_t m0 = int64_t(mb) * kBM - int64_t(owner) * args.rows_per_dest + r0;
+                        float* g = args.dest[owner] + m0 * args.ldc_m + n;
+                        const int64_t g_step = 16 * args.ldc_m;
+                        const float4* s = reinterpret_cast<const float4*>(stage_out + buf * (kChunkBytes / 4) +
+                                                                          r0 * 32) + (u ^ (r0 & 7));
+                        const int rows_left = args.M - mb * kBM - r0;  // whole tiles in a routed launch
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            if (16 * i < rows_left) __stcs(reinterpret_cast<float4*>(g + i * g_step), s[i * 128]);
+                    }
+                } else if (leader && alive) {
                     // A chunk wholly past N (a ragged last tile) stores nothing,
                     // but still commits a (then empty) group: the buffer-reuse
                     // wait above counts one group per chunk.  Partial boxes are
@@ -456,6 +497,9 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             }
         }
         if (leader) ptx::bulk_wait_group0();
+        // routed results went to other GPUs: performed at system scope before
+        // the thread finishes (the signal that follows the kernel publishes them)
+        if (kEpi == kEpiF32Rows && args.routed) __threadfence_system();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int quarter = warp & 3;  // TMEM sub-partition this warp may access
@@ -466,8 +510,8 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             tile_coords(t, p, mb, nb);
             if (!ptx::mbar_wait(bar_tmem_full, tile_iter & 1)) break;
             ptx::tc_fence_after();
-            const int64_t m = int64_t(mb) * kBM + row_in_tile;
-            const bool row_in = m < args.M;  // the last tile row of a ragged M reaches past it
+            const int64_t m_tile = int64_t(mb) * kBM + row_in_tile;
+            const bool row_in = m_tile < args.M;  // the last tile row of a ragged M reaches past it
 #pragma unroll 1
             for (int chunk = 0; chunk < BN / 32; ++chunk) {
                 uint32_t r[32];
@@ -477,6 +521,7 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                 if (!row_in || n0 >= args.N) continue;
                 const int ncols = (int)min(int64_t(32), int64_t(args.N) - n0);  // < 32 only in the last column chunk
                 if (args.out_bf16) {
+                    const int64_t m = m_tile;
                     __nv_bfloat16* cptr = static_cast<__nv_bfloat16*>(args.c) + p * args.c_batch;
                     if (ncols == 32 && args.ldc_n == 1 && (((m * args.ldc_m + n0) & 7) == 0) &&
                         ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
@@ -506,6 +551,13 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
                     }
                 } else {
                     float* cptr = static_cast<float*>(args.c) + p * args.c_batch;
+                    int64_t m = m_tile;
+                    if (args.routed) {
+                        // the tile's rows belong to one owner: its block starts at dest[owner]
+                        const int owner = int(int64_t(mb) * kBM / args.rows_per_dest);
+                        cptr = args.dest[owner];
+                        m -= int64_t(owner) * args.rows_per_dest;
+                    }
                     if (ncols == 32 && args.ldc_n == 1 && (((m * args.ldc_m + n0) & 3) == 0) &&
                         ((reinterpret_cast<uintptr_t>(cptr) & 15) == 0)) {
                         float4* dst = reinterpret_cast<float4*>(cptr + m * args.ldc_m + n0);
@@ -534,6 +586,10 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
             ptx::tc_fence_before();
             ptx::mbar_arrive(bar_tmem_empty);
         }
+        // routed results went to other GPUs too: have them performed at
+        // system scope before this thread finishes (the signal that follows
+        // the kernel on its stream publishes them)
+        if (args.routed) __threadfence_system();
     }
 
     ptx::tc_fence_before();
@@ -599,7 +655,8 @@ int make_operand_map(CUtensorMap* map, const void* base, int64_t rows, int64_t r
 template <int FMT, int BN, int kStages, int kEpi>
 int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t* b, int64_t ldb,
                 const uint8_t* sfb, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n, int64_t M, int64_t N,
-                int64_t K, int beta_one, int64_t batch, int64_t c_batch, int max_ctas, cudaStream_t stream) {
+                int64_t K, int beta_one, int64_t batch, int64_t c_batch, int max_ctas, cudaStream_t stream,
+                const Route* route) {
     using Cf = Cfg<FMT, BN, kStages, kEpi>;
     const int64_t row_bytes = FMT == SW_MX_E4M3 ? K : K / 2;
     // the maps cover the stacked operands (batch * M rows of A, batch * N of B)
@@ -635,6 +692,9 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.out_bf16 = out_dtype == SW_OUT_BF16;
     args.batch = (int)batch;
     args.c_batch = c_batch;
+    args.routed = route != nullptr;
+    args.rows_per_dest = route ? route->rows_per_dest : 0;
+    for (int q = 0; q < kMaxRouted; ++q) args.dest[q] = route && q < route->count ? route->dest[q] : nullptr;
     auto kernel = mx_gemm_kernel<FMT, BN, kStages, kEpi>;
     SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
                 "set gemm smem");
@@ -660,7 +720,7 @@ namespace {
 int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a, const uint8_t* b,
                  int64_t ldb, const uint8_t* scales_b, void* c, int out_dtype, int64_t ldc_m, int64_t ldc_n,
                  int64_t M, int64_t N, int64_t K, int beta_one, int64_t batch, int64_t c_batch, int max_ctas,
-                 void* stream) {
+                 void* stream, const Route* route = nullptr) {
     if (fmt_a != fmt_b) return fail(SW_ERR_UNSUPPORTED, "sw_mx_gemm: mixed operand formats are not supported");
     if (fmt_a != SW_MX_E4M3 && fmt_a != SW_MX_E2M1) return fail(SW_ERR_INVALID, "sw_mx_gemm: unknown format %d", fmt_a);
     if (out_dtype != SW_OUT_F32 && out_dtype != SW_OUT_BF16)
@@ -726,7 +786,10 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
     // a ragged last tile is clipped
     const bool wide = N % 256 == 0 || (batch == 1 && N % 256 > 128);
     // (a batched launch stages its results only when they stack without gaps)
-    if (!beta_one && wide && aligned_c) {
+    if (route && wide) {
+        // routed: the staged chunks leave shared memory as whole row segments
+        epi = kEpiF32Rows;
+    } else if (!beta_one && wide && aligned_c && !route) {
         if (ldc_n == 1 && (ldc_m * esize) % 16 == 0 && ldc_m >= N && (batch == 1 || c_batch == M * ldc_m))
             epi = out_dtype == SW_OUT_BF16 ? kEpiBf16Rows : kEpiF32Rows;
         else if (out_dtype == SW_OUT_F32 && ldc_m == 1 && (ldc_n * 4) % 16 == 0 && ldc_n >= M &&
@@ -736,7 +799,7 @@ int mx_gemm_impl(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint
     int rc;
 #define SW_GEMM(F, BNV, ST, EPI) \
     launch_gemm<F, BNV, ST, EPI>(a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K, beta_one, \
-                                 batch, c_batch, max_ctas, s)
+                                 batch, c_batch, max_ctas, s, route)
 #define SW_GEMM_FMT(F)                                                                  \
     (epi == kEpiBf16Rows  ? SW_GEMM(F, 256, 3, kEpiBf16Rows)                             \
      : epi == kEpiF32Rows ? SW_GEMM(F, 256, 3, kEpiF32Rows)                              \
@@ -768,6 +831,32 @@ extern "C" int sw_mx_gemm_batched(int fmt_a, int fmt_b, const uint8_t* a, int64_
     if (batch == 0) return sw::ok();
     return sw::mx_gemm_impl(fmt_a, fmt_b, a, lda, scales_a, b, ldb, scales_b, c, out_dtype, ldc_m, ldc_n, M, N, K,
                             beta_one, batch, batch_stride_c, 0, stream);
+}
+
+extern "C" int sw_mx_gemm_routed(int fmt, const uint8_t* a, int64_t lda, const uint8_t* scales_a, const uint8_t* b,
+                                 int64_t ldb, const uint8_t* scales_b, float* const* dest, int ndest,
+                                 int64_t rows_per_dest, int64_t ldc, int64_t M, int64_t N, int64_t K, int max_ctas,
+                                 void* stream) {
+    using namespace sw;
+    if (ndest < 1 || ndest > kMaxRouted)
+        return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: 1 to %d destinations (got %d)", kMaxRouted, ndest);
+    if (!dest) return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: null destination list");
+    if (rows_per_dest <= 0 || rows_per_dest % 128 != 0 || rows_per_dest * ndest != M)
+        return fail(SW_ERR_INVALID,
+                    "sw_mx_gemm_routed: the %d destinations must each take whole 128-row tiles, M = %lld rows in all",
+                    ndest, (long long)M);
+    if (ldc < N || ldc % 4 != 0 || N % 4 != 0)
+        return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: N must be a multiple of 4 and ldc cover N, a multiple of 4");
+    Route route;
+    route.count = ndest;
+    route.rows_per_dest = rows_per_dest;
+    for (int q = 0; q < ndest; ++q) {
+        if (!dest[q] || (reinterpret_cast<uintptr_t>(dest[q]) & 15))
+            return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: destination %d is null or not 16-byte aligned", q);
+        route.dest[q] = dest[q];
+    }
+    return mx_gemm_impl(fmt, fmt, a, lda, scales_a, b, ldb, scales_b, dest[0], SW_OUT_F32, ldc, 1, M, N, K, 0, 1, 0,
+                        max_ctas, stream, &route);
 }
 
 extern "C" int sw_mx_gemm(int fmt_a, int fmt_b, const uint8_t* a, int64_t lda, const uint8_t* scales_a,

@@ -90,6 +90,20 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, int32_t c0, int32
                  "r"(c0), "r"(c1), "r"(src)
                  : "memory");
 }
+// An L2 policy that marks lines evict-first (results written once and not
+// read back by this kernel: they should not push operand tiles out of L2).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void tma_store_2d_hint(const void* tmap, int32_t c0, int32_t c1, uint32_t src,
+                                                  uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(c0), "r"(c1), "r"(src), "l"(policy)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed bulk store has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_group_read0() {

@@ -158,6 +158,18 @@ def mx_gemm(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, 
                                 ldc_m, ldc_n, M, N_, K, int(beta_one), int(max_ctas), c_void_p(stream)))
 
 
+def mx_gemm_routed(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int,
+                   dests: Sequence[int], rows_per_dest: int, ldc: int, M: int, N_: int, K: int, *, max_ctas: int = 0,
+                   stream: int = 0) -> None:
+    """Float32 C[m, n] = sum_k A[m, k] B[n, k] with row block q written at
+    dests[q] (row-major, pitch ldc), any of them a peer's memory (see
+    sw_mx_gemm_routed)."""
+    arr = (c_void_p * len(dests))(*[int(d) for d in dests])
+    N.check(N.lib.sw_mx_gemm_routed(fmt, c_void_p(a_ptr), lda, c_void_p(sfa_ptr), c_void_p(b_ptr), ldb,
+                                    c_void_p(sfb_ptr), arr, len(dests), rows_per_dest, ldc, M, N_, K, int(max_ctas),
+                                    c_void_p(stream)))
+
+
 def mx_gemm_batched(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int, c_ptr: int,
                     batch: int, M: int, N_: int, K: int, *, out_bf16: bool = False, ldc_m: int | None = None,
                     ldc_n: int = 1, batch_stride_c: int | None = None, beta_one: bool = False,

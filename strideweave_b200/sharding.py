@@ -215,16 +215,21 @@ class MXShardedContraction:
     """
 
     def __init__(self, plan: ShardPlan, fmt: int, a_planes: tuple[Any, Any], b_planes: tuple[Any, Any],
-                 comm: NcclCommunicator | None = None, stream: int = 0) -> None:
+                 comm: NcclCommunicator | None = None, stream: int = 0, transport: str = "nccl") -> None:
         from . import _native as N
         from . import kernels
         from ._host import DType, Layout, Shape, Stride, Tensor
         from .carrier import CUDA
 
+        if transport not in ("nccl", "peer"):
+            raise ValueError("transport must be 'nccl' (chunked reduce-scatter) or 'peer' (NVLink peer stores)")
         if plan.mode == "k" and plan.world > 1 and comm is None:
             raise ValueError("a K-split over several ranks needs an NcclCommunicator for its reduce-scatter")
         if comm is not None and (comm.world != plan.world or comm.rank != plan.rank):
             raise ValueError("the communicator's world and rank must match the plan's")
+        if transport == "peer" and plan.mode == "k" and plan.chunks != 1:
+            raise ValueError("the peer K-split writes whole rows: plan one chunk")
+        self.transport = transport if plan.mode == "k" else "nccl"
         self.plan, self.fmt, self.comm, self.stream = plan, fmt, comm, int(stream or 0)
         self.N, self.kernels = N, kernels
         self.a_pay, self.a_sc = (_address(x) for x in a_planes)
@@ -241,7 +246,10 @@ class MXShardedContraction:
         self.max_ctas = 0
         if plan.mode == "k" and plan.world > 1 and plan.chunks > 1 and plan.comm_sms > 0:
             self.max_ctas = max(1, N.sm_count() - plan.comm_sms)
-        if plan.mode == "k":
+        if self.transport == "peer":
+            self.landing = PeerLanding(plan.world, plan.rank, plan.rows_local * plan.N, comm)
+            self.step = 0
+        elif plan.mode == "k":
             nbuf = min(2, plan.chunks)  # double-buffered partials [M, Nc]
             self.partials = [CUDA(plan.M * plan.chunk_cols, dtype=DType.Float32, empty=True, device=dev)
                              for _ in range(nbuf)]
@@ -272,6 +280,9 @@ class MXShardedContraction:
         if plan.mode == "m":
             run_msplit(plan, self._contract, self.out.data_ptr)
             return self.result
+        if self.transport == "peer":
+            self._run_peer()
+            return self.result
         comm_stream = self.comm_stream.handle
         nbuf = len(self.partials)
 
@@ -301,9 +312,146 @@ class MXShardedContraction:
         run_ksplit(plan, contract, reduce_scatter, self.partials, outs, before_comm=before_comm, after_all=after_all)
         return self.result
 
+    def _run_peer(self) -> None:
+        """One K-split step over NVLink peer memory (see PeerLanding): wait
+        until every owner has summed this rank's previous contribution,
+        contract with each C row block routed into its owner's slot for this
+        rank, signal the owners, wait for every writer's signal, sum this
+        rank's slots in rank order into the result, free the writers' slots."""
+        plan, L, s = self.plan, self.landing, self.stream
+        self.step += 1
+        e = self.step & 0xFFFFFFFF
+        L.wait(L.consumed_flags, e - 1, s)
+        self.kernels.mx_gemm_routed(self.fmt, self.a_pay, self.row_bytes, self.a_sc, self.b_pay, self.row_bytes,
+                                    self.b_sc, L.dests(), plan.rows_local, plan.N, plan.M, plan.N, plan.k_local,
+                                    stream=s)
+        L.signal(L.written_flag_of, e, s)
+        L.wait(L.written_flags, e, s)
+        L.sum_into(self.out.data_ptr, s)
+        L.signal(L.consumed_flag_of, e, s)
+
     def close(self) -> None:
-        """Release the streams and events now (the carriers free themselves)."""
-        if self.plan.mode == "k":
-            for e in (*self.done, *self.freed, self.all_done):
-                e.close()
-            self.comm_stream.close()
+        """Release the streams, events and peer mappings now (the carriers
+        free themselves).  Every rank of a peer K-split calls it: it meets the
+        others first, so no rank frees memory another still writes."""
+        if self.plan.mode != "k":
+            return
+        if self.transport == "peer":
+            self.landing.close()
+            return
+        for e in (*self.done, *self.freed, self.all_done):
+            e.close()
+        self.comm_stream.close()
+
+
+class PeerLanding:
+    """This rank's landing buffer of a peer K-split and its view of the
+    others' (CUDA IPC within one node).
+
+    One device allocation holds `world` Float32 slots of `slot_elems`
+    elements (slot p: rank p's partial of the rows this rank owns) and two
+    arrays of `world` 32-bit step flags: written[p] (rank p finished writing
+    its slot) and consumed[p] (rank p, an owner, finished summing this rank's
+    contribution).  Other ranks write these flags over NVLink; flags only
+    grow, so a step waits for "at least e".  The handles are exchanged with an
+    all-gather on the NCCL communicator (the only collective the transport
+    uses, once, at set-up)."""
+
+    def __init__(self, world: int, rank: int, slot_elems: int, comm: NcclCommunicator | None,
+                 wait_limit_ns: int = 5_000_000_000) -> None:
+        from . import _native as N
+
+        if world > 8:
+            raise NotImplementedError("a peer K-split spans at most the 8 GPUs of one node")
+        if slot_elems % 4:
+            raise ValueError("slots must hold whole 16-byte vectors")
+        self.N, self.world, self.rank = N, world, rank
+        self.slot_elems = slot_elems
+        self.wait_limit_ns = wait_limit_ns
+        self.flags_off = 4 * world * slot_elems
+        nbytes = self.flags_off + 8 * world + 256
+        handle = (N.ctypes.c_uint8 * N.SW_IPC_HANDLE_BYTES)()
+        ptr = N.c_void_p()
+        N.check(N.lib.sw_ipc_alloc(N.ctypes.byref(ptr), nbytes, handle))
+        self.base = ptr.value
+        N.check(N.lib.sw_memset(N.c_void_p(self.base + self.flags_off), 0, 8 * world, None))
+        self.peers = [0] * world
+        self.peers[rank] = self.base
+        self.comm = comm
+        if world > 1:
+            import numpy as np
+
+            # exchange the 64-byte handles as 16 Float32 words each (an
+            # all-gather copies the bits)
+            words = N.SW_IPC_HANDLE_BYTES // 4
+            mine, everyone = N.DeviceBuffer(4 * words), N.DeviceBuffer(4 * words * world)
+            mine.upload(np.frombuffer(bytes(handle), dtype=np.uint8))
+            comm.all_gather_f32(everyone.ptr, mine.ptr, words)
+            N.synchronize()
+            host = np.empty(N.SW_IPC_HANDLE_BYTES * world, dtype=np.uint8)
+            everyone.download(host)
+            for q in range(world):
+                if q == rank:
+                    continue
+                h = (N.ctypes.c_uint8 * N.SW_IPC_HANDLE_BYTES).from_buffer_copy(
+                    host[q * N.SW_IPC_HANDLE_BYTES:(q + 1) * N.SW_IPC_HANDLE_BYTES].tobytes())
+                p = N.c_void_p()
+                N.check(N.lib.sw_ipc_open(h, N.ctypes.byref(p)))
+                self.peers[q] = p.value
+            self._rendezvous()  # every rank's flags are zero before any writes them
+
+    @property
+    def written_flags(self) -> int:
+        return self.base + self.flags_off
+
+    @property
+    def consumed_flags(self) -> int:
+        return self.base + self.flags_off + 4 * self.world
+
+    def written_flag_of(self, q: int) -> int:
+        """Owner q's written[this rank]."""
+        return self.peers[q] + self.flags_off + 4 * self.rank
+
+    def consumed_flag_of(self, q: int) -> int:
+        """Writer q's consumed[this rank]."""
+        return self.peers[q] + self.flags_off + 4 * (self.world + self.rank)
+
+    def dests(self) -> list[int]:
+        """Where this rank's row block q goes: owner q's slot for this rank."""
+        return [self.peers[q] + 4 * self.rank * self.slot_elems for q in range(self.world)]
+
+    def wait(self, flags: int, target: int, stream: int) -> None:
+        N = self.N
+        N.check(N.lib.sw_peer_wait(N.c_void_p(flags), self.world, target & 0xFFFFFFFF, self.wait_limit_ns,
+                                   N.c_void_p(stream)))
+
+    def signal(self, flag_of: Callable[[int], int], value: int, stream: int) -> None:
+        N = self.N
+        arr = (N.c_void_p * self.world)(*[flag_of(q) for q in range(self.world)])
+        N.check(N.lib.sw_peer_signal(arr, self.world, value & 0xFFFFFFFF, N.c_void_p(stream)))
+
+    def sum_into(self, out_ptr: int, stream: int) -> None:
+        N = self.N
+        N.check(N.lib.sw_sum_slots_f32(N.c_void_p(self.base), self.slot_elems, self.world, N.c_void_p(out_ptr),
+                                       N.c_void_p(stream)))
+
+    def _rendezvous(self) -> None:
+        N = self.N
+        tick, ticks = N.DeviceBuffer(4), N.DeviceBuffer(4 * self.world)
+        N.check(N.lib.sw_memset(N.c_void_p(tick.ptr), 0, 4, None))
+        N.synchronize()
+        self.comm.all_gather_f32(ticks.ptr, tick.ptr, 1)
+        N.synchronize()
+
+    def close(self) -> None:
+        N = self.N
+        if self.base is None:
+            return
+        N.synchronize()
+        if self.world > 1:
+            self._rendezvous()  # nobody writes into a buffer after this
+            for q, p in enumerate(self.peers):
+                if q != self.rank and p:
+                    N.check(N.lib.sw_ipc_close(N.c_void_p(p)))
+        N.check(N.lib.sw_ipc_free(N.c_void_p(self.base)))
+        self.base = None

@@ -105,6 +105,34 @@ def test_invalid_arguments_are_rejected_before_any_device_work(native):
         native.check(native.lib.sw_nccl_reduce_scatter_f32(c_void_p(16), c_void_p(16), -1, c_void_p(16), None))
     native.check(native.lib.sw_nccl_all_gather_f32(c_void_p(16), c_void_p(16), 0, c_void_p(16), None))  # empty
     native.check(native.lib.sw_nccl_comm_destroy(None))  # no communicator: nothing to do
+    # the peer-memory K-split's pieces check their arguments before any CUDA call
+    with pytest.raises(ValueError, match="1 to 8 destinations"):
+        kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16] * 9, 128, 256, 9 * 128, 256, 1024)
+    with pytest.raises(ValueError, match="whole 128-row tiles"):
+        kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16, 32], 100, 256, 200, 256, 1024)
+    with pytest.raises(ValueError, match="N must be a multiple of 4"):
+        kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16], 128, 260, 128, 258, 1024)
+    with pytest.raises(ValueError, match="destination 1 is null or not 16-byte aligned"):
+        kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16, 20], 128, 256, 256, 256, 1024)
+    with pytest.raises(ValueError, match="bad flag count"):
+        native.check(native.lib.sw_peer_wait(c_void_p(16), -1, 1, 1000, None))
+    with pytest.raises(ValueError, match="limit must lie"):
+        native.check(native.lib.sw_peer_wait(c_void_p(16), 2, 1, 0, None))
+    native.check(native.lib.sw_peer_wait(None, 0, 1, 1000, None))  # no flags: nothing to wait for
+    with pytest.raises(ValueError, match="at most 8 flags"):
+        native.check(native.lib.sw_peer_signal(None, 9, 1, None))
+    with pytest.raises(ValueError, match="null flag 1"):
+        native.check(native.lib.sw_peer_signal((c_void_p * 2)(16, None), 2, 1, None))
+    with pytest.raises(ValueError, match="bad extent"):
+        native.check(native.lib.sw_sum_slots_f32(c_void_p(16), 16, 0, c_void_p(16), None))
+    with pytest.raises(ValueError, match="whole 16-byte vectors"):
+        native.check(native.lib.sw_sum_slots_f32(c_void_p(16), 6, 2, c_void_p(16), None))
+    with pytest.raises(ValueError, match="bad argument"):
+        native.check(native.lib.sw_ipc_alloc(byref(comm), 0, ident))
+    with pytest.raises(ValueError, match="null argument"):
+        native.check(native.lib.sw_ipc_open(None, byref(comm)))
+    native.check(native.lib.sw_ipc_close(None))  # nothing mapped: nothing to do
+    native.check(native.lib.sw_ipc_free(None))
     with pytest.raises(ValueError, match="unknown format"):
         kernels.mx_quantize(7, 16, 4, 32, 32, 1, 16, 32, 16)
     with pytest.raises(ValueError, match="payload pitch"):

@@ -263,3 +263,36 @@ def test_mx_linear_on_extents_of_whole_blocks(fmt, code):
     assert rel_frobenius(y.carrier.to_numpy().reshape(OUT, B).T, want_y) <= EXACT
     assert rel_frobenius(xt.grad.carrier.to_numpy().reshape(B, IN), want_dx) <= EXACT
     assert rel_frobenius(wt.grad.carrier.to_numpy().reshape(OUT, IN), want_dw) <= EXACT
+
+
+@pytest.mark.parametrize("ndest,rows_per_dest", [(1, 128), (3, 256)])
+@pytest.mark.parametrize("N_,pad", [(1024, 0), (200, 4), (128, 0), (100, 8)])
+def test_routed_contraction_lands_each_row_block_at_its_destination(ndest, rows_per_dest, N_, pad):
+    """sw_mx_gemm_routed (the contraction half of the peer K-split), here with
+    every destination on this GPU: row block q equals rows
+    [q rows_per_dest, (q + 1) rows_per_dest) of the plain contraction bit for
+    bit, with pitch N + pad, and nothing past a block is written.  N = 1024
+    and 200 take the staged epilogue (whole 128-byte row segments), 128 and
+    100 the register one."""
+    from strideweave_b200 import kernels
+
+    fmt, K = O.E4M3, 256
+    M = ndest * rows_per_dest
+    rng = np.random.default_rng(N_ + ndest)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    b = (rng.standard_normal((N_, K)) * 0.02).astype(np.float32)
+    (pa, sa, ra), (pb, sb, rb) = quantize_rows(fmt, a), quantize_rows(fmt, b)
+    c = empty(4 * M * N_)
+    kernels.mx_gemm(fmt, pa.ptr, ra, sa.ptr, pb.ptr, rb, sb.ptr, c.ptr, M, N_, K)
+    want = to_host(c, (M, N_), np.float32)
+    ldc, guard = N_ + pad, 64
+    blocks = [empty(4 * (rows_per_dest * ldc + guard), fill=0xFF) for _ in range(ndest)]
+    kernels.mx_gemm_routed(fmt, pa.ptr, ra, sa.ptr, pb.ptr, rb, sb.ptr, [d.ptr for d in blocks], rows_per_dest,
+                           ldc, M, N_, K)
+    N.raise_device_status()
+    for q, d in enumerate(blocks):
+        flat = to_host(d, rows_per_dest * ldc + guard, np.float32)
+        assert (flat[rows_per_dest * ldc:].view(np.uint32) == 0xFFFFFFFF).all(), "stores past the block"
+        got = flat[:rows_per_dest * ldc].reshape(rows_per_dest, ldc)
+        np.testing.assert_array_equal(got[:, :N_], want[q * rows_per_dest:(q + 1) * rows_per_dest])
+        assert (got[:, N_:].view(np.uint32) == 0xFFFFFFFF).all(), "stores into the pitch padding"

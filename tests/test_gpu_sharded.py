@@ -93,6 +93,16 @@ def test_one_rank_splits_equal_one_contraction(fmt_name):
     # a second step on the same buffers gives the same result
     np.testing.assert_array_equal(ksplit_rows(plan, op.run()), want)
     op.close()
+    # the peer-memory transport at one rank: the routed contraction lands in
+    # the rank's own slot and the slot sum is a copy
+    pp = ShardPlan("k", 1, 0, M, NN, K)
+    peer = MXShardedContraction(pp, fmt, pa, pb, transport="peer")
+    for _ in range(2):
+        got = peer.run()
+        assert got.layout == Layout(Shape([M, NN]), Stride([NN, 1]))
+        np.testing.assert_array_equal(got.carrier.to_numpy().reshape(M, NN), want)
+    N.raise_device_status()
+    peer.close()
 
 
 def test_multi_rank_ksplit_needs_a_communicator():
@@ -129,10 +139,18 @@ def _rank(rank: int, world: int, ids, results) -> None:
         again = ksplit_rows(kp, op.run())
         N.synchronize()
         op.close()
+        # the peer-memory transport: row blocks written into the owners'
+        # slots over NVLink, slots summed in rank order (three steps, so the
+        # step flags cycle through the slot reuse)
+        pp = ShardPlan("k", world, rank, M, NN, K)
+        peer = MXShardedContraction(pp, fmt, pa, pb, comm=comm, transport="peer")
+        peers = [peer.run().carrier.to_numpy().reshape(pp.rows_local, NN) for _ in range(3)]
+        N.raise_device_status()
+        peer.close()
         comm.close()
-        results.put((rank, mp.row0, got_m.carrier.to_numpy().reshape(mp.rows_local, NN), got_k, again))
+        results.put((rank, mp.row0, got_m.carrier.to_numpy().reshape(mp.rows_local, NN), got_k, again, peers))
     except Exception as exc:  # reported to the parent, which fails the test
-        results.put((rank, repr(exc), None, None, None))
+        results.put((rank, repr(exc), None, None, None, None))
 
 
 def test_two_rank_splits_match_one_contraction():
@@ -160,10 +178,14 @@ def test_two_rank_splits_match_one_contraction():
     a, b = operand(1, M, K), operand(2, NN, K, 0.02)
     want = full_contraction(N.SW_MX_E4M3, a, b)
     for rank in range(world):
-        row0, m_rows, k_rows, again = got[rank]
+        row0, m_rows, k_rows, again, peers = got[rank]
         assert m_rows is not None, row0  # the rank's exception
         block = want[row0:row0 + M // world]
         np.testing.assert_array_equal(m_rows, block)
         err = np.linalg.norm(k_rows - block) / np.linalg.norm(block)
         assert err <= TOL, err
         np.testing.assert_array_equal(again, k_rows)  # the same step again, bit for bit
+        # two partials sum to the same binary32 in either order: the peer
+        # transport equals NCCL's reduce-scatter bit for bit, every step
+        for p in peers:
+            np.testing.assert_array_equal(p, k_rows)
