@@ -169,11 +169,14 @@ int sw_sum_slots_f32(const float* slots, int64_t slot_elems, int count, float* o
  * another GPU's memory mapped with sw_ipc_open: each 128 x 32 chunk of a
  * finished tile is staged in shared memory and leaves as whole 128-byte row
  * segments by plain NVLink peer stores (N under 256 stores from registers),
- * and the kernel fences them at system scope before it ends.  This is the
- * contraction half of the peer-memory K-split. */
+ * and the kernel fences them at system scope before it ends.  The walk over
+ * the tiles starts with row block `first` (0 <= first < ndest) and wraps
+ * around: ranks that start at different owners (rank r at r + 1, its own
+ * block last) keep every GPU receiving from one writer at a time.  This is
+ * the contraction half of the peer-memory K-split. */
 int sw_mx_gemm_routed(int fmt, const uint8_t* a, int64_t lda, const uint8_t* scales_a,
                       const uint8_t* b, int64_t ldb, const uint8_t* scales_b,
-                      float* const* dest, int ndest, int64_t rows_per_dest, int64_t ldc,
+                      float* const* dest, int ndest, int64_t rows_per_dest, int64_t ldc, int first,
                       int64_t M, int64_t N, int64_t K, int max_ctas, void* stream);
 
 /* ---- layout-aware reductions -------------------------------------------- */

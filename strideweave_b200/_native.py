@@ -196,7 +196,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_mx_gemm_routed": (
         c_int,
         [c_int, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, POINTER(c_void_p), c_int, c_int64, c_int64,
-         c_int64, c_int64, c_int64, c_int, c_void_p],
+         c_int, c_int64, c_int64, c_int64, c_int, c_void_p],
     ),
     "sw_map_f32": (
         c_int,

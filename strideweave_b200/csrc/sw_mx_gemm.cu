@@ -74,6 +74,7 @@ struct Route {
     int count;
     int64_t rows_per_dest;
     float* dest[kMaxRouted];
+    int first;  // the destination whose row block the walk starts with
 };
 
 template <int FMT, int BN, int kStages, int kEpi>
@@ -145,6 +146,11 @@ struct GemmArgs {
     int routed;
     int64_t rows_per_dest;
     float* dest[kMaxRouted];
+    // Row tiles the walk is rotated by (0 <= rotate_m < tiles along M): tile
+    // row mb is computed where mb - rotate_m (mod the tile rows) would be.
+    // Ranks of a routed K-split each start at a different owner's block, so
+    // at any moment every owner receives from one writer, not from all.
+    int rotate_m;
 };
 
 template <int FMT, int BN, int kStages, int kEpi>
@@ -213,6 +219,11 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
         const int r = t % per_group;
         mb = first + r % gsize;
         nb = r / gsize;
+        // a routed launch starts its walk at another row block (see GemmArgs)
+        if (args.rotate_m) {
+            mb += args.rotate_m;
+            if (mb >= num_m) mb -= num_m;
+        }
     };
 
     if (warp == 0) {
@@ -695,6 +706,7 @@ int launch_gemm(const uint8_t* a, int64_t lda, const uint8_t* sfa, const uint8_t
     args.routed = route != nullptr;
     args.rows_per_dest = route ? route->rows_per_dest : 0;
     for (int q = 0; q < kMaxRouted; ++q) args.dest[q] = route && q < route->count ? route->dest[q] : nullptr;
+    args.rotate_m = route ? (int)((int64_t(route->first) * route->rows_per_dest / kBM) % ((M + kBM - 1) / kBM)) : 0;
     auto kernel = mx_gemm_kernel<FMT, BN, kStages, kEpi>;
     SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes),
                 "set gemm smem");
@@ -835,8 +847,8 @@ extern "C" int sw_mx_gemm_batched(int fmt_a, int fmt_b, const uint8_t* a, int64_
 
 extern "C" int sw_mx_gemm_routed(int fmt, const uint8_t* a, int64_t lda, const uint8_t* scales_a, const uint8_t* b,
                                  int64_t ldb, const uint8_t* scales_b, float* const* dest, int ndest,
-                                 int64_t rows_per_dest, int64_t ldc, int64_t M, int64_t N, int64_t K, int max_ctas,
-                                 void* stream) {
+                                 int64_t rows_per_dest, int64_t ldc, int first, int64_t M, int64_t N, int64_t K,
+                                 int max_ctas, void* stream) {
     using namespace sw;
     if (ndest < 1 || ndest > kMaxRouted)
         return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: 1 to %d destinations (got %d)", kMaxRouted, ndest);
@@ -847,9 +859,13 @@ extern "C" int sw_mx_gemm_routed(int fmt, const uint8_t* a, int64_t lda, const u
                     ndest, (long long)M);
     if (ldc < N || ldc % 4 != 0 || N % 4 != 0)
         return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: N must be a multiple of 4 and ldc cover N, a multiple of 4");
+    if (first < 0 || first >= ndest)
+        return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: the first destination must be one of the %d (got %d)", ndest,
+                    first);
     Route route;
     route.count = ndest;
     route.rows_per_dest = rows_per_dest;
+    route.first = first;
     for (int q = 0; q < ndest; ++q) {
         if (!dest[q] || (reinterpret_cast<uintptr_t>(dest[q]) & 15))
             return fail(SW_ERR_INVALID, "sw_mx_gemm_routed: destination %d is null or not 16-byte aligned", q);

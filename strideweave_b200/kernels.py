@@ -159,15 +159,15 @@ def mx_gemm(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, 
 
 
 def mx_gemm_routed(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int,
-                   dests: Sequence[int], rows_per_dest: int, ldc: int, M: int, N_: int, K: int, *, max_ctas: int = 0,
-                   stream: int = 0) -> None:
+                   dests: Sequence[int], rows_per_dest: int, ldc: int, M: int, N_: int, K: int, *, first: int = 0,
+                   max_ctas: int = 0, stream: int = 0) -> None:
     """Float32 C[m, n] = sum_k A[m, k] B[n, k] with row block q written at
-    dests[q] (row-major, pitch ldc), any of them a peer's memory (see
-    sw_mx_gemm_routed)."""
+    dests[q] (row-major, pitch ldc), any of them a peer's memory; the tile
+    walk starts with row block `first` (see sw_mx_gemm_routed)."""
     arr = (c_void_p * len(dests))(*[int(d) for d in dests])
     N.check(N.lib.sw_mx_gemm_routed(fmt, c_void_p(a_ptr), lda, c_void_p(sfa_ptr), c_void_p(b_ptr), ldb,
-                                    c_void_p(sfb_ptr), arr, len(dests), rows_per_dest, ldc, M, N_, K, int(max_ctas),
-                                    c_void_p(stream)))
+                                    c_void_p(sfb_ptr), arr, len(dests), rows_per_dest, ldc, int(first), M, N_, K,
+                                    int(max_ctas), c_void_p(stream)))
 
 
 def mx_gemm_batched(fmt: int, a_ptr: int, lda: int, sfa_ptr: int, b_ptr: int, ldb: int, sfb_ptr: int, c_ptr: int,

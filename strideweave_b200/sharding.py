@@ -322,9 +322,11 @@ class MXShardedContraction:
         self.step += 1
         e = self.step & 0xFFFFFFFF
         L.wait(L.consumed_flags, e - 1, s)
+        # rank r writes owner r + 1's block first and its own last: at any
+        # moment each GPU receives from one writer
         self.kernels.mx_gemm_routed(self.fmt, self.a_pay, self.row_bytes, self.a_sc, self.b_pay, self.row_bytes,
                                     self.b_sc, L.dests(), plan.rows_local, plan.N, plan.M, plan.N, plan.k_local,
-                                    stream=s)
+                                    first=(plan.rank + 1) % plan.world, stream=s)
         L.signal(L.written_flag_of, e, s)
         L.wait(L.written_flags, e, s)
         L.sum_into(self.out.data_ptr, s)

@@ -112,6 +112,8 @@ def test_invalid_arguments_are_rejected_before_any_device_work(native):
         kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16, 32], 100, 256, 200, 256, 1024)
     with pytest.raises(ValueError, match="N must be a multiple of 4"):
         kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16], 128, 260, 128, 258, 1024)
+    with pytest.raises(ValueError, match="first destination must be one of the 2"):
+        kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16, 32], 128, 256, 256, 256, 1024, first=2)
     with pytest.raises(ValueError, match="destination 1 is null or not 16-byte aligned"):
         kernels.mx_gemm_routed(1, 16, 1024, 16, 16, 1024, 16, [16, 20], 128, 256, 256, 256, 1024)
     with pytest.raises(ValueError, match="bad flag count"):

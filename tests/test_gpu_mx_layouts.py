@@ -287,8 +287,9 @@ def test_routed_contraction_lands_each_row_block_at_its_destination(ndest, rows_
     want = to_host(c, (M, N_), np.float32)
     ldc, guard = N_ + pad, 64
     blocks = [empty(4 * (rows_per_dest * ldc + guard), fill=0xFF) for _ in range(ndest)]
+    # the walk starts at the last block (the rotation a K-split rank uses)
     kernels.mx_gemm_routed(fmt, pa.ptr, ra, sa.ptr, pb.ptr, rb, sb.ptr, [d.ptr for d in blocks], rows_per_dest,
-                           ldc, M, N_, K)
+                           ldc, M, N_, K, first=ndest - 1)
     N.raise_device_status()
     for q, d in enumerate(blocks):
         flat = to_host(d, rows_per_dest * ldc + guard, np.float32)
