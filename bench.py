@@ -46,7 +46,8 @@ sys.path.insert(0, str(ROOT))
 M5, N5, K5 = 65536, 16384, 16384
 FLOP5 = 2.0 * M5 * N5 * K5
 K_CHUNKS = 8
-PARITY_TOL = 2e-3  # relative Frobenius error of the contraction path
+PARITY_TOL = 2e-3
+E2E_CHUNK_ROWS = 2048  # rows per block of the host-streamed step  # relative Frobenius error of the contraction path
 # DRAM bytes (read + write) per launch of the M-split contraction at one GPU,
 # from ncu on the per-rank shape of eight GPUs (8192 x 16384 x 16384, the
 # committed capture) scaled by the 8x rows: A reads and C writes grow with the
@@ -428,23 +429,24 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
         for r0 in range(0, host.shape[0], 8192):
             host[r0:r0 + 8192].copy_(torch.randn((min(8192, host.shape[0] - r0), k), generator=gen, device="cuda"))
     torch.cuda.synchronize()
-    fa, fb = N.DeviceBuffer(4 * rows * k), N.DeviceBuffer(4 * N5 * k)
-    rb = kernels.mx_row_bytes(fmt, k)
 
     def e2e_step():
-        N.check(N.lib.sw_memcpy_h2d(N.c_void_p(fa.ptr), N.c_void_p(pin_a.data_ptr()), fa.nbytes, None))
-        N.check(N.lib.sw_memcpy_h2d(N.c_void_p(fb.ptr), N.c_void_p(pin_b.data_ptr()), fb.nbytes, None))
-        kernels.mx_quantize(fmt, fa.ptr, rows, k, k, 1, a[0].ptr, rb, a[1].ptr)
-        kernels.mx_quantize(fmt, fb.ptr, N5, k, k, 1, b[0].ptr, rb, b[1].ptr)
-        op.run()
-        N.check(N.lib.sw_memcpy_d2h(N.c_void_p(pin_c.data_ptr()), N.c_void_p(op.out.data_ptr), pin_c.numel() * 4,
-                                    None))
+        # copies, quantisation, contraction and the return of C, pipelined
+        # over blocks of rows on three streams (MXShardedContraction.run_from_host)
+        op.run_from_host(pin_a.data_ptr(), pin_b.data_ptr(), pin_c.data_ptr(), chunk_rows=E2E_CHUNK_ROWS)
 
     e2e_ms = time_steps(N, e2e_step, max(2, min(args.steps, 3)), 1, torch, dist, world)
     res["e2e"] = {"value": FLOP5 / (e2e_ms / 1e3) / 1e12, "ms": e2e_ms,
-                  "h2d": world * (fa.nbytes + fb.nbytes), "d2h": world * pin_c.numel() * 4}
+                  "h2d": world * 4 * (rows + N5) * k, "d2h": world * pin_c.numel() * 4,
+                  "chunk_rows": E2E_CHUNK_ROWS}
     N.raise_device_status()
-    del pin_a, pin_b, pin_c, fa, fb, op, a, b
+    # the streamed step's result equals the device step's on the same planes
+    got = np.empty((2, N5), np.float32)
+    N.check(N.lib.sw_memcpy_d2h(N.c_void_p(got.ctypes.data), N.c_void_p(op.out.data_ptr), got.nbytes, None))
+    N.synchronize()
+    res["e2e"]["host_rows_match_device"] = bool(np.array_equal(got, pin_c[:2].numpy()))
+    op.close()
+    del pin_a, pin_b, pin_c, op, a, b
     N.synchronize()
     torch.cuda.empty_cache()
 
@@ -674,7 +676,12 @@ def main() -> None:
                          "traffic": traffic, "frac_of_burst": round(kernel_tflops / (2.0 * peaks["bf16_tflops"]), 4),
                          "frac_of_spec_4500": round(kernel_tflops / 4500.0, 4)},
             "e2e": {"value": round(sharded["e2e"]["value"], 2), "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": sharded["e2e"]["h2d"], "d2h_bytes_per_step": sharded["e2e"]["d2h"]},
+                    "h2d_bytes_per_step": sharded["e2e"]["h2d"], "d2h_bytes_per_step": sharded["e2e"]["d2h"],
+                    "ms_per_step": round(sharded["e2e"]["ms"], 3),
+                    "path": f"MXShardedContraction.run_from_host: pinned Float32 A and B copied in blocks of "
+                            f"{sharded['e2e']['chunk_rows']} rows, quantised and contracted per block while "
+                            f"finished C blocks return (three streams)",
+                    "host_rows_match_device": sharded["e2e"]["host_rows_match_device"]},
             "gpu_launches": world * args.steps,
             "clocks": m["clocks"],
             "parity": {"m_split": m["parity"], "k_split": k["parity"]},

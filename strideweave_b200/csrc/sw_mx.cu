@@ -782,6 +782,9 @@ __global__ void __launch_bounds__(256) quantize_view_runs(const float* __restric
 // lane stores its four codes (E2M1: two bytes) and the block's first lane its
 // scale byte.
 constexpr int kViewVecSegment = 32;
+#ifndef SW_VIEW_TILES
+#define SW_VIEW_TILES 1  // the tile-ordered walk for tiled sources
+#endif
 
 template <int FMT>
 __global__ void __launch_bounds__(256) quantize_view_vec(const float* __restrict__ x, const ViewPlan p, int64_t rows,
@@ -838,6 +841,75 @@ __global__ void __launch_bounds__(256) quantize_view_vec(const float* __restrict
                 *reinterpret_cast<uint32_t*>(dst + kb * 32 + 4 * sub) = e4m3x4(a, b, c, d);
             } else {
                 const float e[8] = {a, b, c, d, 0.0f, 0.0f, 0.0f, 0.0f};
+                *reinterpret_cast<uint16_t*>(dst + kb * 16 + 2 * sub) = uint16_t(e2m1x8(e) & 0xFFFF);
+            }
+        }
+    }
+}
+
+// The vectorised walk for tiled sources, whose next row lies closer in memory
+// than the next run of the quantised mode (a 128 x 32 tile stores its rows'
+// 32-blocks back to back).  The unit is one block of 32 consecutive rows of
+// the first row leaf: each of the warp's eight 16-byte loads covers one block
+// of four adjacent rows (eight lanes a row), so a warp reads 32 x 128 bytes
+// that the tile holds contiguously.  Units run row group first, then block,
+// then the outer rows, which is the tile order of memory: consecutive warps
+// read consecutive tiles.  Conditions as for quantize_view_vec, plus a first
+// row leaf of whole 32-row groups.
+template <int FMT>
+__global__ void __launch_bounds__(256) quantize_view_tiles(const float* __restrict__ x, const ViewPlan p, int64_t rows,
+                                                           int64_t cols, uint8_t* __restrict__ payload, int64_t ldp,
+                                                           uint8_t* __restrict__ scales, int layout, int64_t lds) {
+    pdl_enter();
+    const int64_t kblocks = cols / 32;
+    const int64_t groups0 = p.rows.shape[0] / 32;  // 32-row groups along the first row leaf
+    const int64_t units = (rows / 32) * kblocks;
+    const int64_t stride0 = p.rows.stride[0];
+    const int lane = threadIdx.x & 31;
+    const int sub = lane & 7;   // the lane's four elements: 4 sub .. 4 sub + 3 of its block
+    const int rsub = lane >> 3; // the lane's row within each group of four
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t u = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
+        const int64_t a = u % groups0;
+        const int64_t rest = u / groups0;
+        const int64_t kb = rest % kblocks;
+        const int64_t hi = rest / kblocks;
+        const int64_t r0 = hi * p.rows.shape[0] + a * 32;
+        // rows r0 + 4 s + rsub: first-leaf coordinate a * 32 + 4 s + rsub, the outer leaves fixed by hi
+        const int64_t base = p.offset + leaf_offset(p.rows, hi * p.rows.shape[0]) + (a * 32 + rsub) * stride0 +
+                             leaf_offset(p.cols, kb * 32) + 4 * sub;
+        float4 q[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const int64_t f = view_swizzle(p, base + int64_t(4 * s) * stride0);
+            if (f >= 0 && f + 3 < p.x_size) {
+                q[s] = __ldcs(reinterpret_cast<const float4*>(x + f));
+            } else {
+                report_device_error(SW_ERR_INVALID);
+                const float nan = __int_as_float(0x7FC00000);
+                q[s] = make_float4(nan, nan, nan, nan);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const int64_t r = r0 + 4 * s + rsub;
+            uint32_t amax = max(max(__float_as_uint(q[s].x) & 0x7FFFFFFFu, __float_as_uint(q[s].y) & 0x7FFFFFFFu),
+                                max(__float_as_uint(q[s].z) & 0x7FFFFFFFu, __float_as_uint(q[s].w) & 0x7FFFFFFFu));
+            amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+            amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+            amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+            uint8_t sc;
+            float inv;
+            bool special;
+            block_scale<FMT>(amax, sc, inv, special);
+            if (sub == 0) scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+            const float e0 = special ? 0.0f : __fmul_rn(q[s].x, inv), e1 = special ? 0.0f : __fmul_rn(q[s].y, inv);
+            const float e2 = special ? 0.0f : __fmul_rn(q[s].z, inv), e3 = special ? 0.0f : __fmul_rn(q[s].w, inv);
+            uint8_t* dst = payload + r * ldp;
+            if (FMT == SW_MX_E4M3) {
+                *reinterpret_cast<uint32_t*>(dst + kb * 32 + 4 * sub) = e4m3x4(e0, e1, e2, e3);
+            } else {
+                const float e[8] = {e0, e1, e2, e3, 0.0f, 0.0f, 0.0f, 0.0f};
                 *reinterpret_cast<uint16_t*>(dst + kb * 16 + 2 * sub) = uint16_t(e2m1x8(e) & 0xFFFF);
             }
         }
@@ -994,11 +1066,16 @@ extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const fl
     for (int k = 0; k < p.rows.rank; ++k) vec = vec && p.rows.stride[k] % 4 == 0;
     for (int k = 1; k < p.cols.rank; ++k) vec = vec && p.cols.stride[k] % 4 == 0;
     for (int i = 0; i < p.swz_rank; ++i) vec = vec && p.swz_base[i] >= 2;
-    const int64_t units = vec    ? rows * ((kblocks + kViewVecSegment - 1) / kViewVecSegment)
+    // tiled sources (the next row nearer than the next run): 32-row units in tile order
+    const bool tiles = SW_VIEW_TILES && vec && p.rows.rank >= 1 && p.rows.shape[0] % 32 == 0 && p.cols.rank >= 2 &&
+                       std::llabs(p.rows.stride[0]) < std::llabs(p.cols.stride[1]);
+    const int64_t units = tiles  ? (rows / 32) * kblocks
+                          : vec  ? rows * ((kblocks + kViewVecSegment - 1) / kViewVecSegment)
                           : runs ? rows * ((kblocks + kViewSegment - 1) / kViewSegment)
                                  : rows * kblocks;
     const int grid = grid_for(units * 32, 256);
-    auto kernel = vec    ? (fmt == SW_MX_E4M3 ? quantize_view_vec<SW_MX_E4M3> : quantize_view_vec<SW_MX_E2M1>)
+    auto kernel = tiles  ? (fmt == SW_MX_E4M3 ? quantize_view_tiles<SW_MX_E4M3> : quantize_view_tiles<SW_MX_E2M1>)
+                  : vec  ? (fmt == SW_MX_E4M3 ? quantize_view_vec<SW_MX_E4M3> : quantize_view_vec<SW_MX_E2M1>)
                   : runs ? (fmt == SW_MX_E4M3 ? quantize_view_runs<SW_MX_E4M3> : quantize_view_runs<SW_MX_E2M1>)
                          : (fmt == SW_MX_E4M3 ? quantize_view<SW_MX_E4M3> : quantize_view<SW_MX_E2M1>);
     SW_CUDA_TRY(launch_pdl(kernel, grid, 256, 0, s, x, p, rows, cols, payload, ld_payload, scales, scale_layout,

@@ -30,7 +30,10 @@
 //               leaf: CTAs own 128 kept ordinals and a slice of the fibre;
 //               slices meet in a small scratch buffer (at most SMs x 3 x 128
 //               partials), folded by the last CTA of each column block.
-//   gather    - anything else: one warp per kept ordinal, scalar loads.
+//   cols_narrow - the same walk when there are kept ordinals enough for a
+//               CTA of 32 per SM: each CTA reads 128-byte row pieces of the
+//               whole fibre and folds in shared memory; no scratch memory.
+//   gather   - anything else: one warp per kept ordinal, scalar loads.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -784,6 +787,102 @@ __global__ void __launch_bounds__(kColsAffThreads, kColsAffPerSm) reduce_cols_af
     if (threadIdx.x == 0) counters[blockIdx.x] = 0;
 }
 
+// Narrow column walk: the kept mode is unit-stride and the reduced mode is one
+// leaf, as for cols_affine, but a CTA owns only kNarrowCols kept ordinals and
+// the whole fibre.  Lane l reads 16 bytes at column (l % (kNarrowCols / 4)) * 4
+// of row l / (kNarrowCols / 4) of its warp's row group, so one warp
+// instruction covers 128 / kNarrowCols rows of kNarrowCols * 4 bytes (whole
+// 128-byte lines at 32 columns), and the 8 warps interleave the row groups.
+// With enough kept ordinals to give every SM a CTA nothing crosses CTAs: no
+// slice partials, no ticket, no fold after the last load.  The CTA folds its
+// row streams in shared memory; the fold is the exact merge, so max and argmax
+// stay bit-exact whatever the stream order.
+// 16-byte loads in flight per lane, per operation; 0 keeps the operation on
+// the split walk.  Measured on the 8192 x 4096 transposed walk (GB/s, one
+// B200): argmax 5220 / 5697 / 5749 at 8 / 12 / 16 loads against 5078 split;
+// max 5374 at 8 against 5319 split, slower with more; sum 5367 at 8 against
+// 5741 split (the split walk's cluster fold), slower with more.
+#ifndef SW_NARROW_U_SUM
+#define SW_NARROW_U_SUM 0
+#endif
+#ifndef SW_NARROW_U_MAX
+#define SW_NARROW_U_MAX 8
+#endif
+#ifndef SW_NARROW_U_ARGMAX
+#define SW_NARROW_U_ARGMAX 16
+#endif
+template <class Op>
+struct NarrowLoads;
+template <>
+struct NarrowLoads<SumOp> { static constexpr int value = SW_NARROW_U_SUM; };
+template <>
+struct NarrowLoads<MaxOp> { static constexpr int value = SW_NARROW_U_MAX; };
+template <>
+struct NarrowLoads<ArgmaxOp> { static constexpr int value = SW_NARROW_U_ARGMAX; };
+#ifndef SW_COLS_NARROW_MIN_PER_SM
+#define SW_COLS_NARROW_MIN_PER_SM 1  // narrow walk once it has this many CTAs per SM
+#endif
+constexpr int kNarrowCols = 32;
+constexpr int kNarrowThreads = 256;
+
+template <class Op, bool kSwz, class Ord>
+__global__ void __launch_bounds__(kNarrowThreads, 2) reduce_cols_narrow(const float* __restrict__ x, DevPlan p,
+                                                                         int64_t stride, int64_t weight, void* out) {
+    using P = Packed<Op, Ord>;
+    constexpr int kLanesPerRow = kNarrowCols / 4;
+    constexpr int kRowsPerWarp = 32 / kLanesPerRow;
+    constexpr int kStreams = (kNarrowThreads / 32) * kRowsPerWarp;  // row streams of a CTA
+    constexpr int kGroups = kNarrowThreads / kNarrowCols;          // fold groups, 4 streams each
+    static_assert(kStreams == 4 * kGroups, "each fold group takes four row streams");
+    __shared__ typename P::T part[kStreams][kNarrowCols];
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int cv = lane % kLanesPerRow;
+    const int stream_id = warp * kRowsPerWarp + lane / kLanesPerRow;  // rows stream_id + t * kStreams
+    const int64_t kv = int64_t(blockIdx.x) * kLanesPerRow + cv;
+    const bool live = kv < (p.n_kept >> 2);
+    typename Op::S acc[4] = {Op::identity(), Op::identity(), Op::identity(), Op::identity()};
+    if (live && stream_id < p.n_red) {
+        const int64_t col = p.offset + kept_offset(p.kept, kv * 4);
+        LaneWalk<Ord> w;
+        w.off0 = int64_t(stream_id) * stride;
+        w.doff = int64_t(kStreams) * stride;
+        w.ord0 = Ord(int64_t(stream_id) * weight);
+        w.dord = Ord(int64_t(kStreams) * weight);
+        w.w0 = 0;  // the four components are four columns at the same ordinal
+        w.iters = int((p.n_red - stream_id + kStreams - 1) / kStreams);
+        FastFold<Op, Ord> f;
+        const float* ptr = x + phys<kSwz>(p.swz, col + w.off0);
+        constexpr int kU = NarrowLoads<Op>::value > 0 ? NarrowLoads<Op>::value : 8;
+        if (fast_walk<Op, Ord, kU>(ptr, w.doff, w.iters, f)) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] = f.component(e, w.ord0, w.dord, Ord(0));
+        } else {
+            exact_walk<Op, kSwz, Ord>(x, p.swz, col, w, acc, true);
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) part[stream_id][cv * 4 + e] = P::pack(acc[e]);
+    __syncthreads();
+    // thread (g, c) folds streams 4g .. 4g + 3 of column c, then thread c folds the groups
+    const int c = threadIdx.x % kNarrowCols;
+    const int g = threadIdx.x / kNarrowCols;
+    typename Op::S v = P::unpack(part[4 * g][c]);
+#pragma unroll
+    for (int s = 1; s < 4; ++s) Op::merge(v, P::unpack(part[4 * g + s][c]));
+    __syncthreads();
+    part[g][c] = P::pack(v);
+    __syncthreads();
+    const int64_t kept_i = int64_t(blockIdx.x) * kNarrowCols + threadIdx.x;
+    if (threadIdx.x < kNarrowCols && kept_i < p.n_kept) {
+        typename Op::S r = P::unpack(part[0][threadIdx.x]);
+#pragma unroll
+        for (int q = 1; q < kGroups; ++q) Op::merge(r, P::unpack(part[q][threadIdx.x]));
+        store_result<Op>(out, kept_i, r);
+    }
+}
+
 // ---- gather ------------------------------------------------------------------
 template <class Op>
 __global__ void __launch_bounds__(256) reduce_gather(const float* __restrict__ x, DevPlan p, void* out) {
@@ -976,7 +1075,7 @@ int reduce_scratch(size_t need, cudaStream_t stream, void** out) {
 }
 
 struct Launch {
-    int kernel = 2;  // 0 rows_vec, 1 cols_vec, 2 gather, 3 rows_affine, 4 cols_affine
+    int kernel = 2;  // 0 rows_vec, 1 cols_vec, 2 gather, 3 rows_affine, 4 cols_affine, 5 cols_narrow
     int splits = 1;
     int wpr = 1;     // warps per row of rows_affine
     RowWalk rw{};
@@ -1005,6 +1104,13 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         const cudaError_t err = launch_pdl(reduce_rows_affine<Op, kSwz, Ord>, dim3((unsigned)blocks),
                                            dim3(kRowsAffThreads), 0, stream, x, p, L.rw, rpw, out);
         if (err != cudaSuccess) return cuda_fail(err, "reduce_rows_affine launch");
+        return SW_OK;
+    }
+    if (L.kernel == 5 && NarrowLoads<Op>::value > 0) {
+        const int64_t blocks = (p.n_kept + kNarrowCols - 1) / kNarrowCols;
+        const cudaError_t err = launch_pdl(reduce_cols_narrow<Op, kSwz, Ord>, dim3((unsigned)blocks),
+                                           dim3(kNarrowThreads), 0, stream, x, p, L.cstride, L.cweight, out);
+        if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_narrow launch");
         return SW_OK;
     }
     const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
@@ -1074,7 +1180,7 @@ int launch_affine_swz(const float* x, const DevPlan& p, const Launch& L, void* o
 template <class Op>
 int launch_for(const float* x, const DevPlan& p, const Launch& L, void* out, cudaStream_t stream,
                const ScratchSource& src) {
-    if (L.kernel == 3 || L.kernel == 4) {
+    if (L.kernel >= 3) {
         // 32-bit ordinals whenever every ordinal of the fibre fits
         int rc = p.n_red < (int64_t(1) << 30) ? launch_affine_swz<Op, int32_t>(x, p, L, out, stream, src)
                                               : launch_affine_swz<Op, int64_t>(x, p, L, out, stream, src);
@@ -1145,6 +1251,18 @@ Launch choose(DevPlan& p, int kind, bool aligned) {
         const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
         // every CTA resident at once (kColsAffPerSm per SM): no second, partial wave
         const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * kColsAffPerSm / col_blocks);
+        const int64_t narrow_streams = (kNarrowThreads / 32) * (32 / (kNarrowCols / 4));
+        const bool narrow_op = (kind == SW_REDUCE_SUM && SW_NARROW_U_SUM > 0) ||
+                               (kind == SW_REDUCE_MAX && SW_NARROW_U_MAX > 0) ||
+                               (kind == SW_REDUCE_ARGMAX && SW_NARROW_U_ARGMAX > 0);
+        if (narrow_op && p.red.rank == 1 && p.n_kept >= int64_t(sm_count()) * SW_COLS_NARROW_MIN_PER_SM * kNarrowCols &&
+            swizzle_commutes(p.swz, narrow_streams * p.red.stride[0])) {
+            // a CTA of kNarrowCols kept ordinals for every SM: whole fibres per CTA
+            L.kernel = 5;
+            L.cstride = p.red.stride[0];
+            L.cweight = p.red.weight[0];
+            return L;
+        }
         if (p.red.rank == 1 && swizzle_commutes(p.swz, int64_t(kColsAffWarps) * p.red.stride[0])) {
             // slices meet in scratch memory: no cap from the cluster size.  About
             // 2.6 CTAs per SM streams fastest for every operation (measured on

@@ -312,6 +312,90 @@ class MXShardedContraction:
         run_ksplit(plan, contract, reduce_scatter, self.partials, outs, before_comm=before_comm, after_all=after_all)
         return self.result
 
+    def run_from_host(self, a_host: int, b_host: int, c_host: int, *, chunk_rows: int = 2048) -> Any:
+        """One M-split step whose operands and result live in host memory.
+
+        `a_host` holds this rank's Float32 A rows [M/g, K] and `b_host` the
+        Float32 B [N, K], both row-major; the rank's Float32 C rows [M/g, N]
+        land row-major at `c_host`.  Pinned (page-locked) host memory lets the
+        copies run asynchronously; pageable memory works but serialises them.
+
+        The step is a three-stream pipeline over blocks of `chunk_rows` rows:
+        a copy stream brings B and then block after block of A to the device,
+        the step's stream quantises B once and then, block by block, quantises
+        A into this contraction's A planes and contracts the block into the
+        result carrier, and a second copy stream returns each finished block of
+        C while later blocks are still arriving.  Host-to-device and
+        device-to-host copies use the two directions of the link at once, so
+        the step costs about the host-to-device time of A and B plus one
+        block's contraction and return.  Every block's result equals the one
+        `run()` gives from the same planes, bit for bit (each output tile runs
+        the same K loop).  Returns the result Tensor, as `run()` does; the
+        call only enqueues, so synchronise `stream` before reading `c_host`.
+        """
+        plan, N, kernels = self.plan, self.N, self.kernels
+        if plan.mode != "m":
+            raise ValueError("run_from_host streams an M-split; a K-split's operands are per-rank K slices")
+        rows, k, n = plan.rows_local, plan.k_local, plan.N
+        if chunk_rows <= 0 or chunk_rows % ROW_TILE != 0 or rows % chunk_rows != 0:
+            raise ValueError(f"chunk_rows={chunk_rows} must be a whole number of {ROW_TILE}-row tiles dividing the "
+                             f"rank's {rows} rows")
+        if not (a_host and b_host and c_host):
+            raise ValueError("run_from_host needs host addresses for A, B and C")
+        st = self._staging(chunk_rows)
+        s, h2d, d2h = self.stream, st["h2d"].handle, st["d2h"].handle
+        cvp = N.c_void_p
+        # the copy streams start after everything already enqueued on the step's stream
+        st["start"].record(s)
+        st["start"].wait(h2d)
+        st["start"].wait(d2h)
+        N.check(N.lib.sw_memcpy_h2d(cvp(st["b32"].ptr), cvp(b_host), st["b32"].nbytes, cvp(h2d)))
+        st["b_ready"].record(h2d)
+        block_a = 4 * chunk_rows * k
+        for i in range(rows // chunk_rows):
+            N.check(N.lib.sw_memcpy_h2d(cvp(st["a32"].ptr + i * block_a), cvp(a_host + i * block_a), block_a,
+                                        cvp(h2d)))
+            st["a_ready"][i].record(h2d)
+        st["b_ready"].wait(s)
+        kernels.mx_quantize(self.fmt, st["b32"].ptr, n, k, k, 1, self.b_pay, self.row_bytes, self.b_sc, stream=s)
+        block_c = 4 * chunk_rows * n
+        for i in range(rows // chunk_rows):
+            r0 = i * chunk_rows
+            a_pay = self.a_pay + r0 * self.row_bytes
+            a_sc = self.a_sc + (r0 // ROW_TILE) * self.katoms * 512
+            st["a_ready"][i].wait(s)
+            kernels.mx_quantize(self.fmt, st["a32"].ptr + i * block_a, chunk_rows, k, k, 1, a_pay, self.row_bytes,
+                                a_sc, stream=s)
+            kernels.mx_gemm(self.fmt, a_pay, self.row_bytes, a_sc, self.b_pay, self.row_bytes, self.b_sc,
+                            self.out.data_ptr + i * block_c, chunk_rows, n, k, ldc_m=n, ldc_n=1, stream=s)
+            st["c_ready"][i].record(s)
+            st["c_ready"][i].wait(d2h)
+            N.check(N.lib.sw_memcpy_d2h(cvp(c_host + i * block_c), cvp(self.out.data_ptr + i * block_c), block_c,
+                                        cvp(d2h)))
+        st["done"].record(d2h)
+        st["done"].wait(s)
+        return self.result
+
+    def _staging(self, chunk_rows: int) -> dict:
+        """Device staging of run_from_host (Float32 A and B), its copy streams
+        and events; made on first use for a block size and kept."""
+        st = getattr(self, "_host_staging", None)
+        if st is not None and st["chunk_rows"] == chunk_rows:
+            return st
+        N, plan = self.N, self.plan
+        blocks = plan.rows_local // chunk_rows
+        if st is None:
+            st = {"a32": N.DeviceBuffer(4 * plan.rows_local * plan.k_local),
+                  "b32": N.DeviceBuffer(4 * plan.N * plan.k_local),
+                  "h2d": N.Stream(), "d2h": N.Stream(), "start": N.Event(), "b_ready": N.Event(),
+                  "done": N.Event()}
+            N.synchronize()  # the buffers come from the legacy default stream's pool order
+        st["chunk_rows"] = chunk_rows
+        st["a_ready"] = [N.Event() for _ in range(blocks)]
+        st["c_ready"] = [N.Event() for _ in range(blocks)]
+        self._host_staging = st
+        return st
+
     def _run_peer(self) -> None:
         """One K-split step over NVLink peer memory (see PeerLanding): wait
         until every owner has summed this rank's previous contribution,
@@ -336,6 +420,16 @@ class MXShardedContraction:
         """Release the streams, events and peer mappings now (the carriers
         free themselves).  Every rank of a peer K-split calls it: it meets the
         others first, so no rank frees memory another still writes."""
+        st = getattr(self, "_host_staging", None)
+        if st is not None:
+            self.N.synchronize(self.stream)
+            for e in (st["start"], st["b_ready"], st["done"], *st["a_ready"], *st["c_ready"]):
+                e.close()
+            st["h2d"].close()
+            st["d2h"].close()
+            st["a32"].free()
+            st["b32"].free()
+            self._host_staging = None
         if self.plan.mode != "k":
             return
         if self.transport == "peer":

@@ -105,6 +105,42 @@ def test_one_rank_splits_equal_one_contraction(fmt_name):
     peer.close()
 
 
+@pytest.mark.parametrize("fmt_name", ["E4M3", "E2M1"])
+def test_host_streamed_msplit_equals_one_contraction(fmt_name):
+    """run_from_host: Float32 A and B in pinned host memory, copied, quantised
+    and contracted block by block, C copied back while later blocks arrive;
+    the host C equals the single contraction of the same operands bit for
+    bit, on two steps in a row (new data in the second), and the block size
+    is checked before anything is enqueued."""
+    import torch
+
+    from strideweave_b200 import _native as N
+    from strideweave_b200 import kernels
+    from strideweave_b200.sharding import MXShardedContraction, ShardPlan
+
+    fmt = N.SW_MX_E4M3 if fmt_name == "E4M3" else N.SW_MX_E2M1
+    rows, k = 1024, K
+    rb = kernels.mx_row_bytes(fmt, k)
+    pa = (N.DeviceBuffer(rows * rb), N.DeviceBuffer(kernels.scale_bytes_tc128(rows, k // 32)))
+    pb = (N.DeviceBuffer(NN * rb), N.DeviceBuffer(kernels.scale_bytes_tc128(NN, k // 32)))
+    op = MXShardedContraction(ShardPlan("m", 1, 0, rows, NN, k), fmt, pa, pb)
+    for chunk in (100, 384, 0):
+        with pytest.raises(ValueError):
+            op.run_from_host(1, 1, 1, chunk_rows=chunk)
+    host_c = torch.empty((rows, NN), dtype=torch.float32).pin_memory()
+    for seed in (11, 12):
+        a, b = operand(seed, rows, k), operand(seed + 100, NN, k, 0.02)
+        host_a = torch.from_numpy(a).pin_memory()
+        host_b = torch.from_numpy(b).pin_memory()
+        op.run_from_host(host_a.data_ptr(), host_b.data_ptr(), host_c.data_ptr(), chunk_rows=256)
+        N.synchronize()
+        N.raise_device_status()
+        np.testing.assert_array_equal(host_c.numpy(), full_contraction(fmt, a, b))
+        # the device result carrier holds the same rows
+        np.testing.assert_array_equal(op.result.carrier.to_numpy().reshape(rows, NN), host_c.numpy())
+    op.close()
+
+
 def test_multi_rank_ksplit_needs_a_communicator():
     from strideweave_b200 import _native as N
     from strideweave_b200.sharding import MXShardedContraction, ShardPlan
