@@ -46,8 +46,8 @@ sys.path.insert(0, str(ROOT))
 M5, N5, K5 = 65536, 16384, 16384
 FLOP5 = 2.0 * M5 * N5 * K5
 K_CHUNKS = 8
-PARITY_TOL = 2e-3
-E2E_CHUNK_ROWS = 2048  # rows per block of the host-streamed step  # relative Frobenius error of the contraction path
+PARITY_TOL = 2e-3  # relative Frobenius error of the contraction path
+E2E_CHUNK_ROWS = 2048  # rows per block of the host-streamed step
 # DRAM bytes (read + write) per launch of the M-split contraction at one GPU,
 # from ncu on the per-rank shape of eight GPUs (8192 x 16384 x 16384, the
 # committed capture) scaled by the 8x rows: A reads and C writes grow with the
@@ -440,6 +440,30 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
                   "h2d": world * 4 * (rows + N5) * k, "d2h": world * pin_c.numel() * 4,
                   "chunk_rows": E2E_CHUNK_ROWS}
     N.raise_device_status()
+    # the link bound: this rank's pinned host <-> device copy rates, each
+    # direction alone (1 GiB, best of three)
+    probe = N.DeviceBuffer(pin_b.numel() * 4)
+
+    def copy_rate(h2d: bool) -> float:
+        best = None
+        for _ in range(3):
+            e0, e1 = N.Event(timing=True), N.Event(timing=True)
+            e0.record(0)
+            if h2d:
+                N.check(N.lib.sw_memcpy_h2d(N.c_void_p(probe.ptr), N.c_void_p(pin_b.data_ptr()), probe.nbytes, None))
+            else:
+                N.check(N.lib.sw_memcpy_d2h(N.c_void_p(pin_b.data_ptr()), N.c_void_p(probe.ptr), probe.nbytes, None))
+            e1.record(0)
+            N.synchronize()
+            ms = e0.elapsed_ms(e1)
+            best = ms if best is None else min(best, ms)
+        return probe.nbytes / (best / 1e3) / 1e9
+
+    h2d_gbs, d2h_gbs = copy_rate(True), copy_rate(False)
+    probe.free()
+    link_ms = max(4 * (rows + N5) * k / h2d_gbs, pin_c.numel() * 4 / d2h_gbs) / 1e6
+    res["e2e"]["link"] = {"h2d_gbs": round(h2d_gbs, 1), "d2h_gbs": round(d2h_gbs, 1), "bound_ms": round(link_ms, 2),
+                          "frac_of_link_bound": round(link_ms / e2e_ms, 3)}
     # the streamed step's result equals the device step's on the same planes
     got = np.empty((2, N5), np.float32)
     N.check(N.lib.sw_memcpy_d2h(N.c_void_p(got.ctypes.data), N.c_void_p(op.out.data_ptr), got.nbytes, None))
@@ -681,7 +705,8 @@ def main() -> None:
                     "path": f"MXShardedContraction.run_from_host: pinned Float32 A and B copied in blocks of "
                             f"{sharded['e2e']['chunk_rows']} rows, quantised and contracted per block while "
                             f"finished C blocks return (three streams)",
-                    "host_rows_match_device": sharded["e2e"]["host_rows_match_device"]},
+                    "host_rows_match_device": sharded["e2e"]["host_rows_match_device"],
+                    "link": sharded["e2e"]["link"]},
             "gpu_launches": world * args.steps,
             "clocks": m["clocks"],
             "parity": {"m_split": m["parity"], "k_split": k["parity"]},

@@ -19,6 +19,7 @@
 
 #include "sw_common.cuh"
 #include "sw_gelu.cuh"
+#include "sw_ptx.cuh"
 
 namespace sw {
 namespace {
@@ -785,6 +786,12 @@ constexpr int kViewVecSegment = 32;
 #ifndef SW_VIEW_TILES
 #define SW_VIEW_TILES 1  // the tile-ordered walk for tiled sources
 #endif
+#ifndef SW_VIEW_STAGED
+#define SW_VIEW_STAGED 1  // the shared-memory staged walk for contiguous tiles
+#endif
+#ifndef SW_VIEW_TILES_MINB
+#define SW_VIEW_TILES_MINB 3  // resident CTAs per SM the tile walk is compiled for
+#endif
 
 template <int FMT>
 __global__ void __launch_bounds__(256) quantize_view_vec(const float* __restrict__ x, const ViewPlan p, int64_t rows,
@@ -857,27 +864,47 @@ __global__ void __launch_bounds__(256) quantize_view_vec(const float* __restrict
 // read consecutive tiles.  Conditions as for quantize_view_vec, plus a first
 // row leaf of whole 32-row groups.
 template <int FMT>
-__global__ void __launch_bounds__(256) quantize_view_tiles(const float* __restrict__ x, const ViewPlan p, int64_t rows,
+__global__ void __launch_bounds__(256, SW_VIEW_TILES_MINB) quantize_view_tiles(const float* __restrict__ x, const ViewPlan p, int64_t rows,
                                                            int64_t cols, uint8_t* __restrict__ payload, int64_t ldp,
                                                            uint8_t* __restrict__ scales, int layout, int64_t lds) {
     pdl_enter();
     const int64_t kblocks = cols / 32;
-    const int64_t groups0 = p.rows.shape[0] / 32;  // 32-row groups along the first row leaf
+    const int64_t shape0 = p.rows.shape[0];
+    const int64_t groups0 = shape0 / 32;  // 32-row groups along the first row leaf
     const int64_t units = (rows / 32) * kblocks;
     const int64_t stride0 = p.rows.stride[0];
     const int lane = threadIdx.x & 31;
     const int sub = lane & 7;   // the lane's four elements: 4 sub .. 4 sub + 3 of its block
     const int rsub = lane >> 3; // the lane's row within each group of four
+    // each warp walks a contiguous run of units; its position is decomposed
+    // once and then advanced as an odometer (row group, block, outer rows)
     const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t u = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < units; u += nwarps) {
-        const int64_t a = u % groups0;
-        const int64_t rest = u / groups0;
-        const int64_t kb = rest % kblocks;
-        const int64_t hi = rest / kblocks;
-        const int64_t r0 = hi * p.rows.shape[0] + a * 32;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t per = (units + nwarps - 1) / nwarps;
+    int64_t u = warp * per;
+    const int64_t u_end = min(units, u + per);
+    if (u >= u_end) return;
+    int64_t a = u % groups0;
+    const int64_t rest = u / groups0;
+    int64_t kb = rest % kblocks;
+    int64_t hi = rest / kblocks;
+    int64_t rowoff = p.offset + leaf_offset(p.rows, hi * shape0);
+    int64_t key[SW_MAX_LEAVES];
+    int64_t coloff = 0;
+    {
+        int64_t o = kb * 32;
+#pragma unroll
+        for (int k = 0; k < SW_MAX_LEAVES; ++k) {
+            if (k >= p.cols.rank) break;
+            key[k] = o % p.cols.shape[k];
+            o /= p.cols.shape[k];
+            coloff += key[k] * p.cols.stride[k];
+        }
+    }
+    for (; u < u_end; ++u) {
+        const int64_t r0 = hi * shape0 + a * 32;
         // rows r0 + 4 s + rsub: first-leaf coordinate a * 32 + 4 s + rsub, the outer leaves fixed by hi
-        const int64_t base = p.offset + leaf_offset(p.rows, hi * p.rows.shape[0]) + (a * 32 + rsub) * stride0 +
-                             leaf_offset(p.cols, kb * 32) + 4 * sub;
+        const int64_t base = rowoff + (a * 32 + rsub) * stride0 + coloff + 4 * sub;
         float4 q[8];
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
@@ -913,7 +940,183 @@ __global__ void __launch_bounds__(256) quantize_view_tiles(const float* __restri
                 *reinterpret_cast<uint16_t*>(dst + kb * 16 + 2 * sub) = uint16_t(e2m1x8(e) & 0xFFFF);
             }
         }
+        // next unit: row group, then block (an odometer over the quantised
+        // mode's leaves, 32 elements a step; leaf 0 holds whole blocks), then
+        // the outer rows
+        if (++a < groups0) continue;
+        a = 0;
+        if (++kb < kblocks) {
+            key[0] += 32;
+            coloff += 32 * p.cols.stride[0];
+            if (key[0] == p.cols.shape[0]) {
+                key[0] = 0;
+                coloff -= p.cols.shape[0] * p.cols.stride[0];
+#pragma unroll
+                for (int k = 1; k < SW_MAX_LEAVES; ++k) {
+                    if (k >= p.cols.rank) break;
+                    key[k] += 1;
+                    coloff += p.cols.stride[k];
+                    if (key[k] < p.cols.shape[k]) break;
+                    coloff -= p.cols.shape[k] * p.cols.stride[k];
+                    key[k] = 0;
+                }
+            }
+            continue;
+        }
+        kb = 0;
+        coloff = 0;
+#pragma unroll
+        for (int k = 0; k < SW_MAX_LEAVES; ++k) key[k] = 0;
+        ++hi;
+        if (u + 1 < u_end) rowoff = p.offset + leaf_offset(p.rows, hi * shape0);
     }
+}
+
+// The staged walk for tiled sources whose tiles are contiguous: the first row
+// leaf abuts the quantised mode's first leaf (row stride = run length), so a
+// tile of E_r rows x E_c columns (E_c whole blocks) fills one contiguous
+// E_r * E_c-float range, which one bulk copy brings into shared memory.  The
+// carrier swizzle, when there is one, permutes only inside a tile (the host
+// checks that every bit it reads or writes lies below the tile's alignment),
+// so the tile is copied as it lies and the swizzle is applied to shared-memory
+// offsets.  A thread then quantises one whole 32-block from shared memory
+// (eight 16-byte reads, the amax, the scale, 32 products and their packed
+// codes): a few instructions per element instead of the cross-lane amax and
+// the per-lane address arithmetic of the register walks.  A ring of
+// kStagedBufs buffers per CTA: the next kStagedBufs - 1 tiles are in flight
+// while one is quantised.
+constexpr int kStagedThreads = 128;
+#ifndef SW_VIEW_STAGED_BUFS
+#define SW_VIEW_STAGED_BUFS 2  // tiles in flight or in use per CTA
+#endif
+constexpr int kStagedBufs = SW_VIEW_STAGED_BUFS;
+#ifndef SW_VIEW_STAGED_MINB
+#define SW_VIEW_STAGED_MINB 6  // resident CTAs per SM (85 registers; measured best of 1, 4, 6, 7)
+#endif
+constexpr int64_t kStagedMaxTileFloats = 8192;  // 32 KiB per buffer
+
+__device__ __forceinline__ int swizzle_local(const ViewPlan& p, int f) {
+#pragma unroll
+    for (int i = 0; i < SW_MAX_SWIZZLE; ++i) {
+        if (i < p.swz_rank) {
+            const int mask = (1 << p.swz_bits[i]) - 1;
+            if (p.swz_shift[i] > 0) f ^= ((f >> (p.swz_base[i] + p.swz_shift[i])) & mask) << p.swz_base[i];
+            else f ^= ((f >> p.swz_base[i]) & mask) << (p.swz_base[i] - p.swz_shift[i]);
+        }
+    }
+    return f;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kStagedThreads, SW_VIEW_STAGED_MINB) quantize_view_staged(const float* __restrict__ x, const ViewPlan p,
+                                                                       int64_t rows, int64_t cols,
+                                                                       uint8_t* __restrict__ payload, int64_t ldp,
+                                                                       uint8_t* __restrict__ scales, int layout,
+                                                                       int64_t lds) {
+    extern __shared__ __align__(128) float staged[];
+    const int er = int(p.rows.shape[0]);
+    const int ec = int(p.cols.shape[0]);
+    const int tile = er * ec;       // floats per tile
+    const int bpr = ec / 32;        // blocks per tile row
+    const int64_t ncol = cols / ec;
+    const int64_t ntiles = (rows / er) * ncol;
+    const int64_t kblocks = cols / 32;
+    const uint32_t sbase = ptx::smem_addr(staged);
+    const uint32_t bar0 = sbase + uint32_t(kStagedBufs * tile) * 4u;  // one mbarrier per buffer, after the buffers
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kStagedBufs; ++b) ptx::mbar_init(bar0 + 8u * uint32_t(b), 1);
+        ptx::fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_enter();
+    // tile t: outer rows t / ncol, outer column group t % ncol, columns fastest
+    // (consecutive tiles are consecutive in memory for a row-of-tiles layout)
+    auto issue = [&](int64_t t, int buf) {
+        const int64_t co = t % ncol, ro = t / ncol;
+        const float* src = x + p.offset + leaf_offset(p.rows, ro * er) + leaf_offset(p.cols, co * ec);
+        const uint32_t bar = bar0 + 8u * uint32_t(buf);
+        ptx::mbar_arrive_expect_tx(bar, uint32_t(tile) * 4u);
+        ptx::bulk_load(sbase + uint32_t(buf * tile) * 4u, src, uint32_t(tile) * 4u, bar);
+    };
+    const int64_t g = gridDim.x;
+    uint32_t phases = 0u;   // bit b: parity of buffer b's next completion
+    uint32_t pending = 0u;  // bit b: a copy into buffer b not yet waited for
+    // the first kStagedBufs - 1 tiles of this CTA go out at once
+    for (int b = 0; b + 1 < kStagedBufs; ++b) {
+        const int64_t t = blockIdx.x + b * g;
+        if (t < ntiles) {
+            if (threadIdx.x == 0) issue(t, b);
+            pending |= 1u << b;
+        }
+    }
+    int k = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += g, ++k) {
+        const int buf = k % kStagedBufs;
+        // the buffer the copy kStagedBufs - 1 tiles ahead lands in was freed
+        // by the barrier that ended the previous tile; order its readers'
+        // accesses before the copy's writes
+        const int nb = (k + kStagedBufs - 1) % kStagedBufs;
+        const int64_t tn = t + int64_t(kStagedBufs - 1) * g;
+        if (tn < ntiles) {
+            if (threadIdx.x == 0) {
+                ptx::fence_proxy_async_smem();
+                issue(tn, nb);
+            }
+            pending |= 1u << nb;
+        }
+        const bool ok = ptx::mbar_wait(bar0 + 8u * uint32_t(buf), (phases >> buf) & 1u);
+        phases ^= 1u << buf;
+        pending &= ~(1u << buf);
+        if (!__syncthreads_and(ok)) break;  // a copy that never landed: leave together
+        const float* tb = staged + buf * tile;
+        const int64_t co = t % ncol, ro = t / ncol;
+        for (int item = threadIdx.x; item < er * bpr; item += kStagedThreads) {
+            const int i = item / bpr, j = item - (item / bpr) * bpr;
+            const int64_t r = ro * er + i, kb = co * bpr + j;
+            const int f0 = i * ec + j * 32;
+            float4 v[8];
+            uint32_t amax = 0;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const int f = p.swz_rank > 0 ? swizzle_local(p, f0 + 4 * c) : f0 + 4 * c;
+                v[c] = *reinterpret_cast<const float4*>(tb + f);
+                amax = max(amax, max(max(__float_as_uint(v[c].x) & 0x7FFFFFFFu, __float_as_uint(v[c].y) & 0x7FFFFFFFu),
+                                     max(__float_as_uint(v[c].z) & 0x7FFFFFFFu, __float_as_uint(v[c].w) & 0x7FFFFFFFu)));
+            }
+            uint8_t sc;
+            float inv;
+            bool special;
+            block_scale<FMT>(amax, sc, inv, special);
+            scales[scale_offset(layout, r, kb, kblocks, lds)] = sc;
+            float q[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                q[4 * c] = special ? 0.0f : __fmul_rn(v[c].x, inv);
+                q[4 * c + 1] = special ? 0.0f : __fmul_rn(v[c].y, inv);
+                q[4 * c + 2] = special ? 0.0f : __fmul_rn(v[c].z, inv);
+                q[4 * c + 3] = special ? 0.0f : __fmul_rn(v[c].w, inv);
+            }
+            uint8_t* dst = payload + r * ldp;
+            if (FMT == SW_MX_E4M3) {
+                uint32_t w[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) w[c] = e4m3x4(q[4 * c], q[4 * c + 1], q[4 * c + 2], q[4 * c + 3]);
+                uint4* o = reinterpret_cast<uint4*>(dst + kb * 32);
+                o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+                uint32_t w[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) w[c] = e2m1x8(q + 8 * c);
+                *reinterpret_cast<uint4*>(dst + kb * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        __syncthreads();  // buffer `buf` may be refilled from the next tile on
+    }
+    // a CTA that left early still owns copies in flight: let them land (bounded)
+    if (threadIdx.x == 0)
+        for (int b = 0; b < kStagedBufs; ++b)
+            if (pending & (1u << b)) ptx::mbar_wait(bar0 + 8u * uint32_t(b), (phases >> b) & 1u);
 }
 
 // Row-major E8M0 scales -> the SW_SCALES_TC128 atom placement (padding left at
@@ -1066,6 +1269,41 @@ extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const fl
     for (int k = 0; k < p.rows.rank; ++k) vec = vec && p.rows.stride[k] % 4 == 0;
     for (int k = 1; k < p.cols.rank; ++k) vec = vec && p.cols.stride[k] % 4 == 0;
     for (int i = 0; i < p.swz_rank; ++i) vec = vec && p.swz_base[i] >= 2;
+    // tiles that lie contiguously (the first row leaf abuts the first run) and
+    // hold whole swizzle windows: staged through shared memory a tile at a time
+    bool staged = SW_VIEW_STAGED && vec && p.rows.rank >= 1 && p.rows.stride[0] == p.cols.shape[0] &&
+                  p.rows.shape[0] * p.cols.shape[0] <= kStagedMaxTileFloats &&
+                  size_t(kStagedBufs) * size_t(p.rows.shape[0] * p.cols.shape[0]) * 4 + 8 * kStagedBufs <= 232448 &&
+                  (reinterpret_cast<uintptr_t>(payload) & 15) == 0 && ld_payload % 16 == 0;
+    if (staged) {
+        int topbit = 1;  // 16-byte alignment of every tile
+        for (int i = 0; i < p.swz_rank; ++i)
+            topbit = std::max(topbit, p.swz_base[i] + std::abs(p.swz_shift[i]) + p.swz_bits[i] - 1);
+        const int64_t align = int64_t(1) << (topbit + 1);
+        staged = (p.rows.shape[0] * p.cols.shape[0]) % align == 0 && p.offset % align == 0;
+        for (int k = 1; k < p.rows.rank; ++k) staged = staged && p.rows.stride[k] % align == 0;
+        for (int k = 1; k < p.cols.rank; ++k) staged = staged && p.cols.stride[k] % align == 0;
+    }
+    if (staged) {
+        const int64_t tile = p.rows.shape[0] * p.cols.shape[0];
+        const int64_t ntiles = rows / p.rows.shape[0] * (cols / p.cols.shape[0]);
+        const size_t smem = size_t(kStagedBufs * tile) * 4 + 8 * kStagedBufs;
+        auto kernel = fmt == SW_MX_E4M3 ? quantize_view_staged<SW_MX_E4M3> : quantize_view_staged<SW_MX_E2M1>;
+        SW_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                    "quantize_view_staged smem");
+        int per_sm = 0;  // every CTA resident: a persistent walk over the tiles
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kStagedThreads, smem) != cudaSuccess ||
+            per_sm < 1) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ntiles, int64_t(sm_count_mx()) * per_sm));
+        SW_CUDA_TRY(launch_pdl(kernel, grid, kStagedThreads, smem, s, x, p, rows, cols, payload, ld_payload, scales,
+                               scale_layout, ld_scales),
+                    "quantize_view_staged launch");
+        SW_LAUNCH_CHECK("sw_mx_quantize_view launch");
+        return ok();
+    }
     // tiled sources (the next row nearer than the next run): 32-row units in tile order
     const bool tiles = SW_VIEW_TILES && vec && p.rows.rank >= 1 && p.rows.shape[0] % 32 == 0 && p.cols.rank >= 2 &&
                        std::llabs(p.rows.stride[0]) < std::llabs(p.cols.stride[1]);
@@ -1073,7 +1311,9 @@ extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const fl
                           : vec  ? rows * ((kblocks + kViewVecSegment - 1) / kViewVecSegment)
                           : runs ? rows * ((kblocks + kViewSegment - 1) / kViewSegment)
                                  : rows * kblocks;
-    const int grid = grid_for(units * 32, 256);
+    // the tile walk gives each warp a run of about four units (one
+    // decomposition per run); the others a unit per warp and grid step
+    const int grid = tiles ? grid_for(units * 8, 256) : grid_for(units * 32, 256);
     auto kernel = tiles  ? (fmt == SW_MX_E4M3 ? quantize_view_tiles<SW_MX_E4M3> : quantize_view_tiles<SW_MX_E2M1>)
                   : vec  ? (fmt == SW_MX_E4M3 ? quantize_view_vec<SW_MX_E4M3> : quantize_view_vec<SW_MX_E2M1>)
                   : runs ? (fmt == SW_MX_E4M3 ? quantize_view_runs<SW_MX_E4M3> : quantize_view_runs<SW_MX_E2M1>)

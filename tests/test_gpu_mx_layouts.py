@@ -123,6 +123,9 @@ VIEWS = {
     # runs of 16 columns: every block spans two runs (the per-element walk)
     "short_runs": (Layout(Shape([128, [16, 8]]), Stride([16, [1, 2048]])), None),
     "short_runs_swizzled": (Layout(Shape([128, [16, 8]]), Stride([16, [1, 2048]])), (2, 4, 3)),
+    # the swizzled tiles again with an all-zero block, NaN and infinities
+    "tiled_swizzled_special": (Layout(Shape([[128, 2], [32, 4]]), Stride([[32, 128 * 32 * 4], [1, 128 * 32]])),
+                               (3, 2, 3)),
 }
 
 
@@ -135,6 +138,10 @@ def test_view_quantiser_equals_the_oracle_on_logical_values(fmt, code, view):
     size = layout.cosize
     flat = np.random.default_rng(len(view)).standard_normal(size).astype(np.float32)
     flat[::97] *= 300.0  # blocks with large spreads (saturation, tiny elements)
+    if view.endswith("special"):
+        flat[0:32] = 0.0  # logical row 0, block 0
+        flat[32:64] = -0.0
+        flat[100], flat[5000], flat[9000] = np.nan, np.inf, -np.inf
     swz = Swizzle(Shape(size), SwizzleStage(bits=stage[0], base=stage[1], shift=stage[2])) if stage else None
     t = Tensor(CUDA.from_numpy(flat, swizzle=swz), 0, layout)
     q = mx.quantize(t, fmt)
