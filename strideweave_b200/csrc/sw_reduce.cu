@@ -576,8 +576,25 @@ constexpr int kRowsAffWarps = kRowsAffThreads / 32;
 // One warp reduces whole rows: warp w owns the contiguous kept ordinals
 // [w * rpw, (w + 1) * rpw).  The host sizes the grid so that every warp is
 // resident at once and all carry the same number of rows: no tail wave.
+// Loads in flight per lane (and the resident CTAs per SM the kernel is
+// compiled for) of the row walk, per operation.  Argmax, whose fold issues
+// more instructions per element, holds eight 16-byte loads per lane at four
+// CTAs per SM (measured, tiled + swizzled / row-major: 5.47 / 5.74 TB/s,
+// against 5.27 / 5.65 with four loads; 4.92 / 5.42 with eight loads at three
+// CTAs per SM; 5.16 / 5.42 with six).
+#ifndef SW_ROWS_U_ARGMAX
+#define SW_ROWS_U_ARGMAX 8
+#endif
+#ifndef SW_ROWS_MINB_ARGMAX
+#define SW_ROWS_MINB_ARGMAX 4
+#endif
+template <class Op>
+struct RowsWalkCfg { static constexpr int kU = 4, kMinBlocks = 4; };
+template <>
+struct RowsWalkCfg<ArgmaxOp> { static constexpr int kU = SW_ROWS_U_ARGMAX, kMinBlocks = SW_ROWS_MINB_ARGMAX; };
+
 template <class Op, bool kSwz, class Ord>
-__global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const float* __restrict__ x, DevPlan p,
+__global__ void __launch_bounds__(kRowsAffThreads, RowsWalkCfg<Op>::kMinBlocks) reduce_rows_affine(const float* __restrict__ x, DevPlan p,
                                                                          RowWalk rw, int64_t rpw, void* out) {
     pdl_enter();
     const int lane = threadIdx.x & 31;
@@ -606,7 +623,7 @@ __global__ void __launch_bounds__(kRowsAffThreads, 4) reduce_rows_affine(const f
         typename Op::S r = Op::identity();
         FastFold<Op, Ord> f;
         const float* ptr = x + phys<kSwz>(p.swz, row + w.off0);
-        if (fast_walk<Op, Ord, 4>(ptr, w.doff, w.iters, f)) {
+        if (fast_walk<Op, Ord, RowsWalkCfg<Op>::kU>(ptr, w.doff, w.iters, f)) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) Op::merge(r, f.component(e, w.ord0, w.dord, w.w0));
         } else {
