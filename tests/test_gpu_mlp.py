@@ -172,6 +172,37 @@ def test_gelu_and_mse_operations_through_autograd():
     np.testing.assert_allclose(xt.grad.carrier.to_numpy(), want, rtol=1e-5, atol=1e-7)
 
 
+def test_gelu_and_its_derivative_over_the_whole_range():
+    """The device GELU and GELU' (the elementwise kernels; the two-way
+    quantiser applies the same device functions) against the float64 erf
+    formula of the reference's CPU operation over [-12, 12] and at +-0,
+    +-inf and NaN: 2e-6 relative, 2e-7 absolute for GELU and 5e-7 absolute
+    for GELU' (which crosses zero near x = -0.75)."""
+    from strideweave_b200 import _native as N
+    from tests.gpu_util import empty, to_device, to_host
+
+    x = np.concatenate([np.linspace(-12, 12, 240001, dtype=np.float32),
+                        np.array([0.0, -0.0, 1e-30, -1e-30, 30.0, -30.0], np.float32)])
+    n = x.size
+    dx, ones = to_device(x), to_device(np.ones(n, np.float32))
+    out = empty(4 * n)
+    N.check(N.lib.sw_elementwise_f32(N.SW_EW_GELU, n, N.c_void_p(dx.ptr), None, N.c_void_p(out.ptr), 0.0, None))
+    got = to_host(out, n, np.float32).astype(np.float64)
+    want = gelu(x.astype(np.float64))
+    np.testing.assert_allclose(got, want, rtol=2e-6, atol=2e-7)
+    assert np.signbit(got[x.size - 5]) and got[x.size - 5] == 0.0  # gelu(-0) = -0
+    N.check(N.lib.sw_elementwise_f32(N.SW_EW_GELU_GRAD, n, N.c_void_p(dx.ptr), N.c_void_p(ones.ptr),
+                                     N.c_void_p(out.ptr), 0.0, None))
+    np.testing.assert_allclose(to_host(out, n, np.float32).astype(np.float64), gelu_grad(x.astype(np.float64)),
+                               rtol=2e-6, atol=5e-7)
+    special = np.array([np.inf, -np.inf, np.nan], np.float32)
+    ds, so = to_device(special), empty(12)
+    N.check(N.lib.sw_elementwise_f32(N.SW_EW_GELU, 3, N.c_void_p(ds.ptr), None, N.c_void_p(so.ptr), 0.0, None))
+    g = to_host(so, 3, np.float32)
+    assert g[0] == np.inf and np.isnan(g[1]) and np.isnan(g[2])  # inf * 1, -inf * 0, NaN
+    N.raise_device_status()
+
+
 def test_fused_train_step_equals_the_autograd_step():
     from strideweave_b200 import CUDA, nn
 
