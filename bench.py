@@ -399,11 +399,18 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
 
     fmt = N.SW_MX_E4M3
     res: dict = {}
+    # the C-ABI NCCL communicator: the end-to-end pass all-gathers the
+    # quantised B slices with it, the K-split reduce-scatters with it
+    comm = None
+    if world > 1:
+        ids = [NcclCommunicator.new_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        comm = NcclCommunicator(world, rank, ids[0])
     # ---- M-split ----
     mp = ShardPlan("m", world, rank, M5, N5, K5)
     a = quantize_generated(torch, N, kernels, fmt, mp.rows_local, K5, seed=7000 + rank)
     b = quantize_generated(torch, N, kernels, fmt, N5, K5, seed=9000)
-    op = MXShardedContraction(mp, fmt, a, b)
+    op = MXShardedContraction(mp, fmt, a, b, comm=comm)
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))).__enter__()
     t_soak = time.perf_counter()
     while time.perf_counter() - t_soak < args.soak_seconds:  # clocks settle under load
@@ -436,8 +443,9 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
         op.run_from_host(pin_a.data_ptr(), pin_b.data_ptr(), pin_c.data_ptr(), chunk_rows=E2E_CHUNK_ROWS)
 
     e2e_ms = time_steps(N, e2e_step, max(2, min(args.steps, 3)), 1, torch, dist, world)
+    b_rows = N5 // world if world > 1 else N5  # each rank's share of B from host memory
     res["e2e"] = {"value": FLOP5 / (e2e_ms / 1e3) / 1e12, "ms": e2e_ms,
-                  "h2d": world * 4 * (rows + N5) * k, "d2h": world * pin_c.numel() * 4,
+                  "h2d": world * 4 * (rows + b_rows) * k, "d2h": world * pin_c.numel() * 4,
                   "chunk_rows": E2E_CHUNK_ROWS}
     N.raise_device_status()
     # the link bound: this rank's pinned host <-> device copy rates, each
@@ -461,7 +469,7 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
 
     h2d_gbs, d2h_gbs = copy_rate(True), copy_rate(False)
     probe.free()
-    link_ms = max(4 * (rows + N5) * k / h2d_gbs, pin_c.numel() * 4 / d2h_gbs) / 1e6
+    link_ms = max(4 * (rows + b_rows) * k / h2d_gbs, pin_c.numel() * 4 / d2h_gbs) / 1e6
     res["e2e"]["link"] = {"h2d_gbs": round(h2d_gbs, 1), "d2h_gbs": round(d2h_gbs, 1), "bound_ms": round(link_ms, 2),
                           "frac_of_link_bound": round(link_ms / e2e_ms, 3)}
     # the streamed step's result equals the device step's on the same planes
@@ -476,11 +484,6 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
 
     # ---- K-split ----
     kp = ShardPlan("k", world, rank, M5, N5, K5, chunks=K_CHUNKS)
-    comm = None
-    if world > 1:
-        ids = [NcclCommunicator.new_id() if rank == 0 else None]
-        dist.broadcast_object_list(ids, src=0)
-        comm = NcclCommunicator(world, rank, ids[0])
     a = quantize_generated(torch, N, kernels, fmt, M5, kp.k_local, seed=8000 + rank)
     b = quantize_generated(torch, N, kernels, fmt, N5, kp.k_local, seed=9500 + rank)
     ksteps = max(3, args.steps // 4)
@@ -704,7 +707,9 @@ def main() -> None:
                     "ms_per_step": round(sharded["e2e"]["ms"], 3),
                     "path": f"MXShardedContraction.run_from_host: pinned Float32 A and B copied in blocks of "
                             f"{sharded['e2e']['chunk_rows']} rows, quantised and contracted per block while "
-                            f"finished C blocks return (three streams)",
+                            f"finished C blocks return (three streams)" +
+                            (f"; each rank copies N/{world} rows of B and NCCL all-gathers the quantised B planes"
+                             if world > 1 else ""),
                     "host_rows_match_device": sharded["e2e"]["host_rows_match_device"],
                     "link": sharded["e2e"]["link"]},
             "gpu_launches": world * args.steps,

@@ -332,6 +332,12 @@ class MXShardedContraction:
         `run()` gives from the same planes, bit for bit (each output tile runs
         the same K loop).  Returns the result Tensor, as `run()` does; the
         call only enqueues, so synchronise `stream` before reading `c_host`.
+
+        With several ranks and a communicator, B crosses each rank's host link
+        once in all: rank r copies and quantises only B rows
+        [r N/g, (r + 1) N/g) and an NCCL all-gather over NVLink assembles the
+        quantised B planes on every rank (in place, on the step's stream),
+        instead of every rank copying all of B from host memory.
         """
         plan, N, kernels = self.plan, self.N, self.kernels
         if plan.mode != "m":
@@ -345,11 +351,13 @@ class MXShardedContraction:
         st = self._staging(chunk_rows)
         s, h2d, d2h = self.stream, st["h2d"].handle, st["d2h"].handle
         cvp = N.c_void_p
+        # B rows this rank brings from host memory: all of them, or its slice
+        b_rows, b_row0 = st["b_rows"], st["b_row0"]
         # the copy streams start after everything already enqueued on the step's stream
         st["start"].record(s)
         st["start"].wait(h2d)
         st["start"].wait(d2h)
-        N.check(N.lib.sw_memcpy_h2d(cvp(st["b32"].ptr), cvp(b_host), st["b32"].nbytes, cvp(h2d)))
+        N.check(N.lib.sw_memcpy_h2d(cvp(st["b32"].ptr), cvp(b_host + 4 * b_row0 * k), st["b32"].nbytes, cvp(h2d)))
         st["b_ready"].record(h2d)
         block_a = 4 * chunk_rows * k
         for i in range(rows // chunk_rows):
@@ -357,7 +365,14 @@ class MXShardedContraction:
                                         cvp(h2d)))
             st["a_ready"][i].record(h2d)
         st["b_ready"].wait(s)
-        kernels.mx_quantize(self.fmt, st["b32"].ptr, n, k, k, 1, self.b_pay, self.row_bytes, self.b_sc, stream=s)
+        sc_group = self.katoms * 512  # scale bytes of one 128-row group
+        kernels.mx_quantize(self.fmt, st["b32"].ptr, b_rows, k, k, 1, self.b_pay + b_row0 * self.row_bytes,
+                            self.row_bytes, self.b_sc + (b_row0 // ROW_TILE) * sc_group, stream=s)
+        if b_rows != n:
+            # in-place all-gathers of the quantised slices (counts in 4-byte words)
+            pay_bytes, sc_bytes = b_rows * self.row_bytes, (b_rows // ROW_TILE) * sc_group
+            self.comm.all_gather_f32(self.b_pay, self.b_pay + plan.rank * pay_bytes, pay_bytes // 4, s)
+            self.comm.all_gather_f32(self.b_sc, self.b_sc + plan.rank * sc_bytes, sc_bytes // 4, s)
         block_c = 4 * chunk_rows * n
         for i in range(rows // chunk_rows):
             r0 = i * chunk_rows
@@ -385,8 +400,13 @@ class MXShardedContraction:
         N, plan = self.N, self.plan
         blocks = plan.rows_local // chunk_rows
         if st is None:
+            # with a communicator each rank brings N/g rows of B (whole 128-row
+            # scale groups) and the ranks all-gather the quantised rest
+            sliced = self.comm is not None and plan.world > 1 and plan.N % (plan.world * ROW_TILE) == 0
+            b_rows = plan.N // plan.world if sliced else plan.N
             st = {"a32": N.DeviceBuffer(4 * plan.rows_local * plan.k_local),
-                  "b32": N.DeviceBuffer(4 * plan.N * plan.k_local),
+                  "b32": N.DeviceBuffer(4 * b_rows * plan.k_local), "b_rows": b_rows,
+                  "b_row0": plan.rank * b_rows if sliced else 0,
                   "h2d": N.Stream(), "d2h": N.Stream(), "start": N.Event(), "b_ready": N.Event(),
                   "done": N.Event()}
             N.synchronize()  # the buffers come from the legacy default stream's pool order

@@ -8,7 +8,9 @@ one contraction of the whole problem.
 * Two ranks, where the box has two GPUs: the M-split rows match bit for bit;
   the K-split sums two K halves in another order, so it is held to the
   path's 2e-3 relative Frobenius bound.  The reduce-scatter runs through the
-  C-ABI NCCL communicator; nothing on the data path uses torch.
+  C-ABI NCCL communicator; nothing on the data path uses torch.  The
+  host-streamed M-split, each rank copying half of B's rows and the
+  quantised halves all-gathered, gives the same rows bit for bit.
 """
 
 from __future__ import annotations
@@ -150,6 +152,10 @@ def test_multi_rank_ksplit_needs_a_communicator():
 
 
 def _rank(rank: int, world: int, ids, results) -> None:
+    # torch (the pinned host buffers of the streamed step) loads its own NCCL;
+    # it is imported before the C-ABI communicator opens NCCL, as in bench.py
+    import torch
+
     from strideweave_b200 import _native as N
     from strideweave_b200.sharding import MXShardedContraction, NcclCommunicator, ShardPlan
 
@@ -183,10 +189,29 @@ def _rank(rank: int, world: int, ids, results) -> None:
         peers = [peer.run().carrier.to_numpy().reshape(pp.rows_local, NN) for _ in range(3)]
         N.raise_device_status()
         peer.close()
+        # the host-streamed M-split: this rank copies its A rows and its half
+        # of B's rows from host memory; the quantised B halves are all-gathered
+        from strideweave_b200 import kernels
+
+        rb = kernels.mx_row_bytes(fmt, K)
+        hp_a = (N.DeviceBuffer(mp.rows_local * rb), N.DeviceBuffer(kernels.scale_bytes_tc128(mp.rows_local, K // 32)))
+        hp_b = (N.DeviceBuffer(NN * rb), N.DeviceBuffer(kernels.scale_bytes_tc128(NN, K // 32)))
+        hop = MXShardedContraction(mp, fmt, hp_a, hp_b, comm=comm)
+        host_a = torch.from_numpy(np.ascontiguousarray(a[rows])).pin_memory()
+        host_b = torch.from_numpy(b).pin_memory()
+        host_c = torch.empty((mp.rows_local, NN), dtype=torch.float32).pin_memory()
+        streamed = []
+        for _ in range(2):
+            hop.run_from_host(host_a.data_ptr(), host_b.data_ptr(), host_c.data_ptr(), chunk_rows=128)
+            N.synchronize()
+            streamed.append(host_c.numpy().copy())
+        N.raise_device_status()
+        hop.close()
         comm.close()
-        results.put((rank, mp.row0, got_m.carrier.to_numpy().reshape(mp.rows_local, NN), got_k, again, peers))
+        results.put((rank, mp.row0, got_m.carrier.to_numpy().reshape(mp.rows_local, NN), got_k, again, peers,
+                     streamed))
     except Exception as exc:  # reported to the parent, which fails the test
-        results.put((rank, repr(exc), None, None, None, None))
+        results.put((rank, repr(exc), None, None, None, None, None))
 
 
 def test_two_rank_splits_match_one_contraction():
@@ -214,10 +239,12 @@ def test_two_rank_splits_match_one_contraction():
     a, b = operand(1, M, K), operand(2, NN, K, 0.02)
     want = full_contraction(N.SW_MX_E4M3, a, b)
     for rank in range(world):
-        row0, m_rows, k_rows, again, peers = got[rank]
+        row0, m_rows, k_rows, again, peers, streamed = got[rank]
         assert m_rows is not None, row0  # the rank's exception
         block = want[row0:row0 + M // world]
         np.testing.assert_array_equal(m_rows, block)
+        for c in streamed:  # B sliced over the ranks and all-gathered: the same rows, bit for bit
+            np.testing.assert_array_equal(c, block)
         err = np.linalg.norm(k_rows - block) / np.linalg.norm(block)
         assert err <= TOL, err
         np.testing.assert_array_equal(again, k_rows)  # the same step again, bit for bit
