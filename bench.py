@@ -1077,6 +1077,18 @@ def profile_misc(N, kernels, reps: int) -> None:
         kernels.mx_scales_to_tc128(rm_sc.ptr, C // 32, R, C // 32, vq_sc.ptr)
         N.check(N.lib.sw_binary_f32(N.SW_BIN_MUL, 2, shape, N.c_void_p(xa.ptr), 0, dense, R * C, N.c_void_p(go.ptr),
                                     0, bcast, R, N.c_void_p(grad.ptr), 0, dense, R * C, None))
+        # the other view-quantiser walks: a transposed source (runs of whole
+        # blocks at a stride), tiles whose rows do not abut (row pitch 64),
+        # and a strided source through sw_mx_quantize
+        kernels.mx_quantize_view(fmt, xa.ptr, R * C, 0, [(R, 1)], [(C, R)], vq_pay.ptr, C, vq_sc.ptr)
+        kernels.mx_quantize_view(fmt, xa.ptr, 2 * R * C, 0, [(128, 64), (32, 64 * 128 * 128)],
+                                 [(32, 1), (128, 64 * 128)], vq_pay.ptr, C, vq_sc.ptr)
+        kernels.mx_quantize(fmt, xa.ptr, R, C // 2, 2 * C, 2, vq_pay.ptr, C // 2, vq_sc.ptr)
+        # dequantisation of the row-quantised plane, and the peer K-split's
+        # ordered sum of two 32 Mi-float slots
+        kernels.mx_dequantize(fmt, vq_pay.ptr, C, rm_sc.ptr, R, C, grad.ptr, C, scale_layout=N.SW_SCALES_ROWMAJOR,
+                              ld_scales=C // 32)
+        N.check(N.lib.sw_sum_slots_f32(N.c_void_p(xa.ptr), n // 2, 2, N.c_void_p(grad.ptr), None))
         N.synchronize()
 
 

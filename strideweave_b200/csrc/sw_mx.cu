@@ -1257,6 +1257,14 @@ extern "C" int sw_mx_quantize_view(int fmt, const sw_reduce_plan* view, const fl
                     (long long)min_ldp);
     if (scale_layout == SW_SCALES_ROWMAJOR && ld_scales < kblocks)
         return fail(SW_ERR_INVALID, "sw_mx_quantize_view: scale pitch smaller than blocks per row");
+    // a plain strided matrix (one leaf per mode, positive strides, no
+    // swizzle) whose rows or columns are contiguous takes the dense kernels:
+    // the row walk, or the shared-memory tiles of a column-contiguous source
+    if (p.swz_rank == 0 && p.rows.rank == 1 && p.cols.rank == 1 && p.rows.stride[0] > 0 && p.cols.stride[0] > 0 &&
+        (p.cols.stride[0] == 1 || (p.rows.stride[0] == 1 && rows % 4 == 0 && p.cols.stride[0] % 4 == 0 &&
+                                   ((reinterpret_cast<uintptr_t>(x + p.offset) & 15) == 0))))
+        return sw_mx_quantize(fmt, x + p.offset, rows, cols, p.rows.stride[0], p.cols.stride[0], payload, ld_payload,
+                              scales, scale_layout, ld_scales, stream);
     cudaStream_t s = (cudaStream_t)stream;
     if (scale_layout == SW_SCALES_TC128 && (rows % 128 != 0 || kblocks % 4 != 0))
         SW_CUDA_TRY(cudaMemsetAsync(scales, 127, (size_t)sw_mx_scale_bytes_tc128(rows, kblocks), s),

@@ -184,6 +184,32 @@ def test_view_quantiser_on_the_config2_layout_at_full_size(fmt, code):
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
 
 
+@pytest.mark.parametrize("fmt,code", FORMATS)
+@pytest.mark.parametrize("order", ["rows", "cols"])
+def test_view_quantiser_on_plain_strided_matrices(fmt, code, order):
+    # one leaf per mode, no swizzle: the view entry hands the matrix to the
+    # dense kernels (the row walk, or the column tiles for a column-major
+    # source at an offset); planes equal the oracle's on the logical values
+    from strideweave_b200 import kernels
+
+    R, C, off = 256, 512, 64
+    store = np.random.default_rng(17).standard_normal(off + R * C).astype(np.float32)
+    if order == "rows":
+        rows, cols = [(R, C)], [(C, 1)]
+        vals = store[off:].reshape(R, C)
+    else:
+        rows, cols = [(R, 1)], [(C, R)]
+        vals = store[off:].reshape(C, R).T
+    rb = C if code == O.E4M3 else C // 2
+    d = to_device(store)
+    pay, sc = empty(R * rb), empty(O.scale_bytes_tc128(R, C // 32))
+    kernels.mx_quantize_view(code, d.ptr, store.size, off, rows, cols, pay.ptr, rb, sc.ptr)
+    N.raise_device_status()
+    pw, sw_ = O.mx_quantize(code, np.ascontiguousarray(vals), scale_layout=1)
+    np.testing.assert_array_equal(to_host(pay, R * rb, np.uint8), pw.ravel())
+    np.testing.assert_array_equal(to_host(sc, O.scale_bytes_tc128(R, C // 32), np.uint8), sw_.ravel())
+
+
 def test_view_quantiser_refuses_views_outside_the_carrier():
     from strideweave_b200 import kernels
 
