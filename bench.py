@@ -468,9 +468,37 @@ def bench_sharded(torch, dist, N, kernels, args, world, rank) -> dict:
         return probe.nbytes / (best / 1e3) / 1e9
 
     h2d_gbs, d2h_gbs = copy_rate(True), copy_rate(False)
+    # both directions at once (1 GiB each way on two streams): the rate the
+    # streamed step actually shares between its inbound and outbound copies
+    probe2 = N.DeviceBuffer(probe.nbytes)
+    s_in, s_out = N.Stream(), N.Stream()
+    both = None
+    for _ in range(3):
+        e0, e1, d_in, d_out = N.Event(timing=True), N.Event(timing=True), N.Event(), N.Event()
+        e0.record(0)
+        e0.wait(s_in.handle)
+        e0.wait(s_out.handle)
+        N.check(N.lib.sw_memcpy_h2d(N.c_void_p(probe.ptr), N.c_void_p(pin_b.data_ptr()), probe.nbytes,
+                                    N.c_void_p(s_in.handle)))
+        N.check(N.lib.sw_memcpy_d2h(N.c_void_p(pin_a.data_ptr()), N.c_void_p(probe2.ptr), probe.nbytes,
+                                    N.c_void_p(s_out.handle)))
+        d_in.record(s_in.handle)
+        d_out.record(s_out.handle)
+        d_in.wait(0)
+        d_out.wait(0)
+        e1.record(0)
+        N.synchronize()
+        ms = e0.elapsed_ms(e1)
+        both = ms if both is None else min(both, ms)
+    both_gbs = 2 * probe.nbytes / (both / 1e3) / 1e9
+    s_in.close()
+    s_out.close()
     probe.free()
-    link_ms = max(4 * (rows + b_rows) * k / h2d_gbs, pin_c.numel() * 4 / d2h_gbs) / 1e6
-    res["e2e"]["link"] = {"h2d_gbs": round(h2d_gbs, 1), "d2h_gbs": round(d2h_gbs, 1), "bound_ms": round(link_ms, 2),
+    probe2.free()
+    h2d_bytes, d2h_bytes = 4 * (rows + b_rows) * k, pin_c.numel() * 4
+    link_ms = max(h2d_bytes / h2d_gbs, d2h_bytes / d2h_gbs, (h2d_bytes + d2h_bytes) / both_gbs) / 1e6
+    res["e2e"]["link"] = {"h2d_gbs": round(h2d_gbs, 1), "d2h_gbs": round(d2h_gbs, 1),
+                          "both_directions_gbs": round(both_gbs, 1), "bound_ms": round(link_ms, 2),
                           "frac_of_link_bound": round(link_ms / e2e_ms, 3)}
     # the streamed step's result equals the device step's on the same planes
     got = np.empty((2, N5), np.float32)
