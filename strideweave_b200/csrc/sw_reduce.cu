@@ -805,47 +805,41 @@ __global__ void __launch_bounds__(kColsAffThreads, kColsAffPerSm) reduce_cols_af
 }
 
 // Narrow column walk: the kept mode is unit-stride and the reduced mode is one
-// leaf, as for cols_affine, but a CTA owns only kNarrowCols kept ordinals and
-// the whole fibre.  Lane l reads 16 bytes at column (l % (kNarrowCols / 4)) * 4
-// of row l / (kNarrowCols / 4) of its warp's row group, so one warp
-// instruction covers 128 / kNarrowCols rows of kNarrowCols * 4 bytes (whole
-// 128-byte lines at 32 columns), and the 8 warps interleave the row groups.
-// With enough kept ordinals to give every SM a CTA nothing crosses CTAs: no
-// slice partials, no ticket, no fold after the last load.  The CTA folds its
-// row streams in shared memory; the fold is the exact merge, so max and argmax
-// stay bit-exact whatever the stream order.
-// 16-byte loads in flight per lane, per operation; 0 keeps the operation on
-// the split walk.  Measured on the 8192 x 4096 transposed walk (GB/s, one
-// B200): argmax 5220 / 5697 / 5749 at 8 / 12 / 16 loads against 5078 split;
-// max 5374 at 8 against 5319 split, slower with more; sum 5367 at 8 against
-// 5741 split (the split walk's cluster fold), slower with more.
-#ifndef SW_NARROW_U_SUM
-#define SW_NARROW_U_SUM 0
-#endif
-#ifndef SW_NARROW_U_MAX
-#define SW_NARROW_U_MAX 8
-#endif
-#ifndef SW_NARROW_U_ARGMAX
-#define SW_NARROW_U_ARGMAX 16
-#endif
+// leaf, as for cols_affine, but a CTA owns only kCols kept ordinals and the
+// whole fibre.  Lane l reads 16 bytes at column (l % (kCols / 4)) * 4 of row
+// l / (kCols / 4) of its warp's row group, so one warp instruction covers
+// 128 / kCols rows of kCols * 4 bytes, and the 8 warps interleave the row
+// groups.  With enough kept ordinals to give every SM a CTA nothing crosses
+// CTAs: no slice partials, no ticket, no fold after the last load.  The CTA
+// folds its row streams in shared memory; the fold is the exact merge, so max
+// and argmax stay bit-exact whatever the stream order.
+//
+// Per operation: kept columns per CTA, the resident CTAs per SM the kernel is
+// compiled for, and 16-byte loads in flight per lane (0: the operation keeps
+// the split walk).  Measured on the 8192 x 4096 transposed walk (GB/s, one
+// B200): argmax 5220 / 5697 / 5749 at 8 / 12 / 16 loads (32 columns, two CTAs
+// per SM) against 5078 split; max 5440 at 32 columns and eight loads, 5621 at
+// 16 columns with four CTAs per SM (one wave of 512 CTAs), 4470 with three
+// (two waves), against 5319 split; sum 5367 at eight loads against 5741 split
+// (the split walk's cluster fold), slower with more.
 template <class Op>
-struct NarrowLoads;
+struct NarrowCfg;
 template <>
-struct NarrowLoads<SumOp> { static constexpr int value = SW_NARROW_U_SUM; };
+struct NarrowCfg<SumOp> { static constexpr int kCols = 32, kMinBlocks = 2, kU = 0; };
 template <>
-struct NarrowLoads<MaxOp> { static constexpr int value = SW_NARROW_U_MAX; };
+struct NarrowCfg<MaxOp> { static constexpr int kCols = 16, kMinBlocks = 4, kU = 8; };
 template <>
-struct NarrowLoads<ArgmaxOp> { static constexpr int value = SW_NARROW_U_ARGMAX; };
+struct NarrowCfg<ArgmaxOp> { static constexpr int kCols = 32, kMinBlocks = 2, kU = 16; };
 #ifndef SW_COLS_NARROW_MIN_PER_SM
 #define SW_COLS_NARROW_MIN_PER_SM 1  // narrow walk once it has this many CTAs per SM
 #endif
-constexpr int kNarrowCols = 32;
 constexpr int kNarrowThreads = 256;
 
 template <class Op, bool kSwz, class Ord>
-__global__ void __launch_bounds__(kNarrowThreads, 2) reduce_cols_narrow(const float* __restrict__ x, DevPlan p,
+__global__ void __launch_bounds__(kNarrowThreads, NarrowCfg<Op>::kMinBlocks) reduce_cols_narrow(const float* __restrict__ x, DevPlan p,
                                                                          int64_t stride, int64_t weight, void* out) {
     using P = Packed<Op, Ord>;
+    constexpr int kNarrowCols = NarrowCfg<Op>::kCols;
     constexpr int kLanesPerRow = kNarrowCols / 4;
     constexpr int kRowsPerWarp = 32 / kLanesPerRow;
     constexpr int kStreams = (kNarrowThreads / 32) * kRowsPerWarp;  // row streams of a CTA
@@ -871,7 +865,7 @@ __global__ void __launch_bounds__(kNarrowThreads, 2) reduce_cols_narrow(const fl
         w.iters = int((p.n_red - stream_id + kStreams - 1) / kStreams);
         FastFold<Op, Ord> f;
         const float* ptr = x + phys<kSwz>(p.swz, col + w.off0);
-        constexpr int kU = NarrowLoads<Op>::value > 0 ? NarrowLoads<Op>::value : 8;
+        constexpr int kU = NarrowCfg<Op>::kU > 0 ? NarrowCfg<Op>::kU : 8;
         if (fast_walk<Op, Ord, kU>(ptr, w.doff, w.iters, f)) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[e] = f.component(e, w.ord0, w.dord, Ord(0));
@@ -1123,8 +1117,8 @@ int launch_affine(const float* x, const DevPlan& p, const Launch& L, void* out, 
         if (err != cudaSuccess) return cuda_fail(err, "reduce_rows_affine launch");
         return SW_OK;
     }
-    if (L.kernel == 5 && NarrowLoads<Op>::value > 0) {
-        const int64_t blocks = (p.n_kept + kNarrowCols - 1) / kNarrowCols;
+    if (L.kernel == 5 && NarrowCfg<Op>::kU > 0) {
+        const int64_t blocks = (p.n_kept + NarrowCfg<Op>::kCols - 1) / NarrowCfg<Op>::kCols;
         const cudaError_t err = launch_pdl(reduce_cols_narrow<Op, kSwz, Ord>, dim3((unsigned)blocks),
                                            dim3(kNarrowThreads), 0, stream, x, p, L.cstride, L.cweight, out);
         if (err != cudaSuccess) return cuda_fail(err, "reduce_cols_narrow launch");
@@ -1268,13 +1262,14 @@ Launch choose(DevPlan& p, int kind, bool aligned) {
         const int64_t col_blocks = (p.n_kept / 4 + 31) / 32;
         // every CTA resident at once (kColsAffPerSm per SM): no second, partial wave
         const int64_t want = std::max<int64_t>(1, int64_t(sm_count()) * kColsAffPerSm / col_blocks);
-        const int64_t narrow_streams = (kNarrowThreads / 32) * (32 / (kNarrowCols / 4));
-        const bool narrow_op = (kind == SW_REDUCE_SUM && SW_NARROW_U_SUM > 0) ||
-                               (kind == SW_REDUCE_MAX && SW_NARROW_U_MAX > 0) ||
-                               (kind == SW_REDUCE_ARGMAX && SW_NARROW_U_ARGMAX > 0);
-        if (narrow_op && p.red.rank == 1 && p.n_kept >= int64_t(sm_count()) * SW_COLS_NARROW_MIN_PER_SM * kNarrowCols &&
+        int ncols = 0, nu = 0;  // the operation's narrow-walk width and load depth
+        if (kind == SW_REDUCE_SUM) { ncols = NarrowCfg<SumOp>::kCols; nu = NarrowCfg<SumOp>::kU; }
+        if (kind == SW_REDUCE_MAX) { ncols = NarrowCfg<MaxOp>::kCols; nu = NarrowCfg<MaxOp>::kU; }
+        if (kind == SW_REDUCE_ARGMAX) { ncols = NarrowCfg<ArgmaxOp>::kCols; nu = NarrowCfg<ArgmaxOp>::kU; }
+        const int64_t narrow_streams = nu > 0 ? (kNarrowThreads / 32) * (32 / (ncols / 4)) : 0;
+        if (nu > 0 && p.red.rank == 1 && p.n_kept >= int64_t(sm_count()) * SW_COLS_NARROW_MIN_PER_SM * ncols &&
             swizzle_commutes(p.swz, narrow_streams * p.red.stride[0])) {
-            // a CTA of kNarrowCols kept ordinals for every SM: whole fibres per CTA
+            // a CTA of ncols kept ordinals for every SM: whole fibres per CTA
             L.kernel = 5;
             L.cstride = p.red.stride[0];
             L.cweight = p.red.weight[0];

@@ -148,6 +148,35 @@ def test_extrema_specials_in_every_lane_position(kind):
         check(kind, gpu_reduce(kind, storage, 0, kept, reduced), O.reduce(kind, storage, 0, kept, reduced))
 
 
+@pytest.mark.parametrize("kind", ["sum", "max", "argmax"])
+@pytest.mark.parametrize("n_kept,n_red", [(2372, 517), (4740, 33), (8196, 130)])
+def test_narrow_column_walk_with_ragged_blocks_and_specials(kind, n_kept, n_red):
+    # transposed fibres with kept extents that take the narrow walk (a CTA of
+    # 16 or 32 kept columns over the whole fibre) and end in a partial CTA;
+    # NaN payloads, signed zeros, ties and infinities in several row streams
+    rng = np.random.default_rng(n_kept + n_red)
+    x = rng.uniform(-1, 1, size=(n_kept, n_red)).astype(np.float32)
+    nan1 = np.array([0x7FC0BEEF], dtype=np.uint32).view(np.float32)[0]
+    nan2 = np.array([0xFF800001], dtype=np.uint32).view(np.float32)[0]
+    for i in range(0, n_kept, 7):
+        j = (i * 31) % n_red
+        k = i % 5
+        if k == 0:
+            x[i, j], x[i, (j + n_red // 2) % n_red] = nan1, nan2
+        elif k == 1:
+            x[i, :] = -1.0
+            x[i, j], x[i, (j + 3) % n_red] = -0.0, 0.0
+        elif k == 2:
+            x[i, j] = x[i, (j * 7 + 1) % n_red] = 4.0
+        elif k == 3:
+            x[i, :] = -np.inf
+        else:
+            x[i, j] = np.inf
+    storage = x.T.ravel().copy()
+    kept, reduced = [(n_kept, 1)], [(n_red, n_kept)]
+    check(kind, gpu_reduce(kind, storage, 0, kept, reduced), O.reduce(kind, storage, 0, kept, reduced))
+
+
 def test_hierarchical_modes_with_permuted_leaves():
     # reduced mode ((8, 16):(64, 1)) - its unit-stride leaf is not the first
     rng = np.random.default_rng(5)
