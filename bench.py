@@ -52,7 +52,7 @@ E2E_CHUNK_ROWS = 2048  # rows per block of the host-streamed step
 # from ncu on the per-rank shape of eight GPUs (8192 x 16384 x 16384, the
 # committed capture) scaled by the 8x rows: A reads and C writes grow with the
 # rows, and so do B's re-reads (one pass of B per raster group of row tiles).
-NCU_TRAFFIC_GEMM_8192_ROWS = 2874.225e6 + 574.960e6
+NCU_TRAFFIC_GEMM_8192_ROWS = 2330.479e6 + 558.476e6
 
 # ---- the layout-aware reductions (config 2) ---------------------------------------
 R, C = 8192, 4096

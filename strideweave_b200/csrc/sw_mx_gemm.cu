@@ -45,6 +45,12 @@
 namespace sw {
 namespace {
 
+#ifndef SW_GEMM_RASTER_GROUP_E4M3
+#define SW_GEMM_RASTER_GROUP_E4M3 16  // M blocks per raster group (measured, below)
+#endif
+#ifndef SW_GEMM_RASTER_GROUP_E2M1
+#define SW_GEMM_RASTER_GROUP_E2M1 8
+#endif
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // payload bytes of K per stage (one 128B swizzle row)
 constexpr int kTmemCols = 512;
@@ -203,7 +209,13 @@ __global__ void __launch_bounds__(kEpi == kEpiDirect ? 192 : 320, 1)
     const int num_n = (args.N + BN - 1) / BN;
     const int per_batch = num_m * num_n;
     const int num_tiles = args.batch * per_batch;
-    constexpr int kGroup = 8;  // M blocks per raster group (L2 reuse of B)
+    // M blocks per raster group: the tiles of a group share B's panels in L2,
+    // so B crosses HBM once per group.  MXFP8 at 65536 x 16384 x 16384 back to
+    // back under the power cap, groups of 4 / 8 / 16 / 32: 1.80 / 1.90 / 1.95 /
+    // 1.93 PF/s (SM clock 1354 / 1372-1414 / 1436-1440 / 1425 MHz; fewer HBM
+    // bytes leave more of the power budget to the tensor cores); at 8192^3,
+    // 16 against 8: MXFP8 2.30 against 2.24 PF/s, MXFP4 4.27 against 4.39.
+    constexpr int kGroup = FMT == SW_MX_E4M3 ? SW_GEMM_RASTER_GROUP_E4M3 : SW_GEMM_RASTER_GROUP_E2M1;
 
     // Tile t of a batched launch is tile t % per_batch of problem
     // t / per_batch.  (mb, nb) are the problem's own blocks; problem p's A
