@@ -1039,6 +1039,9 @@ __global__ void __launch_bounds__(kStagedThreads, SW_VIEW_STAGED_MINB) quantize_
         ptx::bulk_load(sbase + uint32_t(buf * tile) * 4u, src, uint32_t(tile) * 4u, bar);
     };
     const int64_t g = gridDim.x;
+    int dsw[8];  // swizzled offsets of a block's eight 16-byte chunks from its start
+#pragma unroll
+    for (int c = 0; c < 8; ++c) dsw[c] = p.swz_rank > 0 ? swizzle_local(p, 4 * c) : 4 * c;
     uint32_t phases = 0u;   // bit b: parity of buffer b's next completion
     uint32_t pending = 0u;  // bit b: a copy into buffer b not yet waited for
     // the first kStagedBufs - 1 tiles of this CTA go out at once
@@ -1074,11 +1077,15 @@ __global__ void __launch_bounds__(kStagedThreads, SW_VIEW_STAGED_MINB) quantize_
             const int i = item / bpr, j = item - (item / bpr) * bpr;
             const int64_t r = ro * er + i, kb = co * bpr + j;
             const int f0 = i * ec + j * 32;
+            // the swizzle is linear over the bits (each stage XORs shifted,
+            // masked bits in) and f0 + 4 c = f0 ^ 4 c, so the block's eight
+            // chunk offsets are swizzle(f0) ^ swizzle(4 c): one evaluation a block
+            const int s0 = p.swz_rank > 0 ? swizzle_local(p, f0) : f0;
             float4 v[8];
             uint32_t amax = 0;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const int f = p.swz_rank > 0 ? swizzle_local(p, f0 + 4 * c) : f0 + 4 * c;
+                const int f = s0 ^ dsw[c];
                 v[c] = *reinterpret_cast<const float4*>(tb + f);
                 amax = max(amax, max(max(__float_as_uint(v[c].x) & 0x7FFFFFFFu, __float_as_uint(v[c].y) & 0x7FFFFFFFu),
                                      max(__float_as_uint(v[c].z) & 0x7FFFFFFFu, __float_as_uint(v[c].w) & 0x7FFFFFFFu)));
