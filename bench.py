@@ -600,17 +600,23 @@ def bench_reductions(torch, N, kernels, args) -> dict:
     for lay in LAYOUTS:
         N.check(N.lib.sw_memcpy_d2d(N.c_void_p(spare[lay].ptr), N.c_void_p(dev[lay].ptr), X_BYTES, None))
     per_kernel = {}
-    runs = max(6, args.steps // 3)
+    # (20 launches a run, so the host's enqueue keeps ahead of the device;
+    # the best of three runs)
+    runs = 20
     for op in OPS:
         for lay in LAYOUTS:
             bufs = (dev[lay].ptr, spare[lay].ptr)
             launch_on(op, lay, bufs[0])
-            k0, k1 = N.Event(timing=True), N.Event(timing=True)
-            k0.record(0)
-            for r in range(runs):
-                launch_on(op, lay, bufs[(r + 1) % 2])
-            k1.record(0)
-            per_kernel[(op, lay)] = k0.elapsed_ms(k1) / runs
+            best = None
+            for _ in range(3):
+                k0, k1 = N.Event(timing=True), N.Event(timing=True)
+                k0.record(0)
+                for r in range(runs):
+                    launch_on(op, lay, bufs[(r + 1) % 2])
+                k1.record(0)
+                ms = k0.elapsed_ms(k1) / runs
+                best = ms if best is None else min(best, ms)
+            per_kernel[(op, lay)] = best
     # the timed reduce_max agrees with the sequential rule
     check = np.empty(R, dtype=np.float32)
     outs[("reduce_max", "rowmajor")].download(check)
