@@ -63,6 +63,13 @@ int sw_free(void* ptr);
 /* Copies.  Host pointers may be pageable or pinned; pinned ones overlap. */
 int sw_memcpy_h2d(void* dst, const void* src, int64_t bytes, void* stream);
 int sw_memcpy_d2h(void* dst, const void* src, int64_t bytes, void* stream);
+/* Device-to-host copy that returns once the copy is enqueued: with a pinned
+ * destination it overlaps work on other streams; the caller synchronises the
+ * stream (or an event recorded after it) before reading the destination.
+ * sw_memcpy_d2h above waits for its copy.  Replaces, with sw_memcpy_h2d, the
+ * host-side reads of a carrier (CPU carrier element access,
+ * src/strideweave/carriers/cpu/native/_cpu_carrier.hpp:38-67). */
+int sw_memcpy_d2h_async(void* dst, const void* src, int64_t bytes, void* stream);
 int sw_memcpy_d2d(void* dst, const void* src, int64_t bytes, void* stream);
 int sw_memset(void* dst, int value, int64_t bytes, void* stream);
 

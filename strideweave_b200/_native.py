@@ -91,6 +91,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sw_free": (c_int, [c_void_p]),
     "sw_memcpy_h2d": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "sw_memcpy_d2h": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "sw_memcpy_d2h_async": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "sw_memcpy_d2d": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "sw_memset": (c_int, [c_void_p, c_int, c_int64, c_void_p]),
     "sw_host_alloc": (c_int, [POINTER(c_void_p), c_int64]),

@@ -136,6 +136,12 @@ int sw_memcpy_d2h(void* dst, const void* src, int64_t bytes, void* stream) {
     return ok();
 }
 
+int sw_memcpy_d2h_async(void* dst, const void* src, int64_t bytes, void* stream) {
+    // no host synchronisation: the caller waits on the stream (or an event
+    // recorded after the copy) before it reads the destination
+    return copy(dst, src, bytes, cudaMemcpyDeviceToHost, stream, "sw_memcpy_d2h_async");
+}
+
 int sw_memcpy_d2d(void* dst, const void* src, int64_t bytes, void* stream) {
     return copy(dst, src, bytes, cudaMemcpyDeviceToDevice, stream, "sw_memcpy_d2d");
 }

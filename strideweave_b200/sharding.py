@@ -385,8 +385,10 @@ class MXShardedContraction:
                             self.out.data_ptr + i * block_c, chunk_rows, n, k, ldc_m=n, ldc_n=1, stream=s)
             st["c_ready"][i].record(s)
             st["c_ready"][i].wait(d2h)
-            N.check(N.lib.sw_memcpy_d2h(cvp(c_host + i * block_c), cvp(self.out.data_ptr + i * block_c), block_c,
-                                        cvp(d2h)))
+            # enqueued without a host wait, so the next blocks' work is
+            # enqueued while this block's copy runs
+            N.check(N.lib.sw_memcpy_d2h_async(cvp(c_host + i * block_c), cvp(self.out.data_ptr + i * block_c),
+                                              block_c, cvp(d2h)))
         st["done"].record(d2h)
         st["done"].wait(s)
         return self.result
